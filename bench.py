@@ -1,0 +1,392 @@
+#!/usr/bin/env python
+"""Benchmark of the fused-MoE hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg3] [--impl ours|reference]
+
+Workload (BASELINE metric "fused-MoE ms/call and TFLOP/s (H7168,E256,top8,4096 tok) vs tensor-core
+peak"): cfg3 = T=4096 tokens, H=7168, I=2048, E=256 experts, top-8, fp16, seeded synthetic inputs
+(weights ~ N(0, 1/fan_in), hidden ~ N(0,1), softmax-top-8 routing of N(0,1) logits). One step = one
+``fused_moe`` call (routing alignment, gather, Stage1, Stage2 + combine). The weights (22.5 GB) are
+far larger than L2 (126 MB), so every step streams them from HBM; no L2 flush is needed.
+
+value  = algorithmic TFLOP/s = 2 * T * k * 3 * H * I / (device time per step), all ranks summed;
+e2e    = the same metric through the public API with host inputs: pinned hidden_states, topk_ids and
+         topk_weights copied in and the output copied back inside the timed region each step;
+roofline = Stage1 (the dominant kernel): algorithmic bytes / measured average launch time vs the
+         measured HBM copy bandwidth (MEASURED_PEAKS.json);
+cpu_baseline = the oracle (a port of the reference's PyTorch operator) on the host cores, on a
+         bounded sample of experts, rank 0 at N=1 only.
+With --gpus N > 1 every rank runs an independent replica of the workload (weak scaling, no
+collective on the data path) and value sums the ranks' FLOPs over the slowest rank's time.
+--impl reference times the reference's CPU operator (the oracle port) instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "fused-MoE ms/call and TFLOP/s (H7168,E256,top8,4096 tok) vs tensor-core peak"
+UNIT = "TFLOP/s"
+STAGES = ["align", "gather", "stage1", "stage2"]
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of this GPU's SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.samples = []
+        self.proc = None
+        props = torch.cuda.get_device_properties(device)
+        dom, bus, dv = (getattr(props, a, None) for a in ("pci_domain_id", "pci_bus_id", "pci_device_id"))
+        self.sel = f"{dom:08X}:{bus:02X}:{dv:02X}.0" if None not in (dom, bus, dv) else None
+
+    def start(self):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"]
+        if self.sel:
+            cmd += ["-i", self.sel]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.samples.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[5 + i].lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons,
+            "samples": len(self.samples),
+        }
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+def cpu_sample(cfg, ids_cpu, w_cpu, x_cpu, budget_s: float, seed: int = 0):
+    """Oracle (port of the reference's PyTorch operator) on a subset of experts, on the host cores.
+
+    Returns (flops, seconds, n_experts, rows). Weights of the sampled experts are generated on the
+    CPU with the workload's distribution (the values do not change the arithmetic cost).
+    """
+    from oracle.moe_ref import fused_moe_ref
+
+    E, H, I, k = cfg.E, cfg.H, cfg.I, cfg.topk
+    g = torch.Generator().manual_seed(seed)
+    flat = ids_cpu.reshape(-1).long()
+
+    def run(n):
+        sel = torch.arange(n)
+        remap = torch.full((E,), -1, dtype=torch.long)
+        remap[sel] = torch.arange(n)
+        ids_r = remap[flat].reshape(ids_cpu.shape)
+        w13 = (torch.randn((n, 2 * I, H), generator=g) * H ** -0.5).to(cfg.dtype)
+        w2 = (torch.randn((n, H, I), generator=g) * I ** -0.5).to(cfg.dtype)
+        rows = int((ids_r >= 0).sum())
+        t0 = time.perf_counter()
+        fused_moe_ref(x_cpu, w13, w2, ids_r, w_cpu)
+        dt = time.perf_counter() - t0
+        return 2.0 * rows * 3 * H * I, dt, rows
+
+    f1, t1, _ = run(1)  # estimate (also warms the BLAS threads)
+    n = int(max(1, min(E, budget_s / max(t1, 1e-3))))
+    flops, dt, rows = run(n)
+    return flops, dt, n, rows
+
+
+# ----------------------------------------------------------------------------- our arm
+def bench_ours(args, world, rank, local):
+    import muxi_race_b200 as m
+    from muxi_race_b200 import _lib
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = CONFIGS[args.config]
+    peaks, peak_kind = load_peaks()
+
+    w13, w2 = make_weights(cfg, seed=0, device=dev)
+    x = make_hidden(cfg, seed=1 + rank, device=dev)
+    ids, tw = make_routing(cfg, seed=2 + rank, device=dev)
+    if cfg.int8:
+        w13q, w13s = m.quantize_rows_int8(w13)
+        w2q, w2s = m.quantize_rows_int8(w2)
+        del w13, w2
+        fn = lambda xx, ii, ww, oo: m.fused_moe_int8(xx, w13q, w13s, w2q, w2s, ii, ww, out=oo)  # noqa: E731
+    else:
+        fn = lambda xx, ii, ww, oo: m.fused_moe(xx, w13, w2, ii, ww, out=oo)  # noqa: E731
+    out = torch.empty((cfg.T, cfg.H), dtype=cfg.dtype, device=dev)
+    routes = cfg.T * cfg.topk
+    active = int(torch.unique(ids).numel())
+    flops = cfg.flops()
+    n_ev = 6 if cfg.int8 else 5
+
+    for _ in range(args.warmup):
+        fn(x, ids, tw, out)
+    torch.cuda.synchronize()
+    assert m.device_status() == 0, "device status flagged an error during warm-up"
+
+    # ---- device-resident timing, with stage-boundary events on the launch stream
+    stream = torch.cuda.current_stream(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(args.steps)]
+    for row in evs:
+        for e in row:
+            e.record(stream)  # materialise the handles
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks.start()
+    start.record(stream)
+    for k in range(args.steps):
+        _lib.set_profile_events(evs[k])
+        fn(x, ids, tw, out)
+    _lib.set_profile_events(None)
+    end.record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    barrier(world)
+    ms_local = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms_local, world)
+
+    def stage_ms(a, b):
+        return sum(evs[k][a].elapsed_time(evs[k][b]) for k in range(args.steps)) / args.steps
+
+    stages = {"align": stage_ms(0, 1), "gather": stage_ms(1, 2), "stage1": stage_ms(2, 3)}
+    if cfg.int8:
+        stages["requant"] = stage_ms(3, 4)
+        stages["stage2"] = stage_ms(4, 5)
+    else:
+        stages["stage2"] = stage_ms(3, 4)
+
+    # ---- end to end through the public API with host buffers
+    x_h = x.cpu().pin_memory()
+    ids_h = ids.cpu().pin_memory()
+    tw_h = tw.cpu().pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    x_d, ids_d, tw_d = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(tw)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        ids_d.copy_(ids_h, non_blocking=True)
+        tw_d.copy_(tw_h, non_blocking=True)
+        fn(x_d, ids_d, tw_d, out)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
+    d2h = out_h.numel() * out_h.element_size()
+    assert m.device_status() == 0, "device status flagged an error during timing"
+
+    # ---- roofline of the dominant kernel (Stage1): algorithmic bytes per launch / launch time
+    elt = 1 if cfg.int8 else 2
+    s1_bytes = active * 2 * cfg.I * cfg.H * elt + routes * cfg.H * elt + routes * cfg.I * 2
+    s1_gbs = s1_bytes / (stages["stage1"] * 1e-3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", f"traffic_{cfg.name}.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            traffic = json.load(f).get("stage1_dram_bytes_per_launch")
+    roofline = {
+        "bound": "hbm", "kernel": "stage1 (moe_gemm_kernel<kStage1>)", "achieved": round(s1_gbs, 1),
+        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(s1_gbs / peaks["hbm_gbs"], 4),
+        "traffic": traffic, "algorithmic_bytes": s1_bytes, "peak_kind": peak_kind,
+    }
+    total_bytes = cfg.weight_bytes(active) + cfg.io_bytes()
+    t_roof_ms = max(flops / (peaks["bf16_tflops"] * 1e12), total_bytes / (peaks["hbm_gbs"] * 1e9)) * 1e3
+
+    result = {
+        "metric": METRIC,
+        "value": round(world * flops / (ms * 1e-3) / 1e12, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8" if cfg.int8 else ("fp16" if cfg.dtype == torch.float16 else "bf16"),
+        "data": "synthetic (seeded; weights N(0,1/fan_in), hidden N(0,1), softmax-top-k of N(0,1) logits)",
+        "config": {
+            "workload": f"{cfg.name}: fused MoE T={cfg.T} H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
+            "tokens_per_rank": cfg.T, "routed_rows_per_rank": routes, "active_experts": active,
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "inputs larger than L2 (22.5 GB of expert weights streamed per step)",
+        },
+        "ms_per_call": round(ms, 4),
+        "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12, 2),
+        "stage_ms": {k: round(v, 4) for k, v in stages.items()},
+        "call_roofline": {"ms": round(t_roof_ms, 4), "frac": round(t_roof_ms / ms, 4),
+                          "bytes": total_bytes, "flops": flops,
+                          "tensor_peak_frac_spec": round(flops / (ms * 1e-3) / 2.25e15, 4),
+                          "tensor_peak_frac_measured": round(flops / (ms * 1e-3) / (peaks["bf16_tflops"] * 1e12), 4)},
+        "roofline": roofline,
+        "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps * (7 if cfg.int8 else 6),
+        "clocks": clock_info,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        f, dt, n, rows = cpu_sample(cfg, ids.cpu(), tw.cpu(), x.cpu(), budget_s=args.cpu_budget)
+        result["cpu_baseline"] = {
+            "value": round(f / dt / 1e12, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle fused_moe_ref over the {rows} routed rows of {n}/{cfg.E} experts "
+                      f"({dt:.1f} s); full call extrapolates to {flops / (f / dt):.1f} s",
+        }
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+# ----------------------------------------------------------------------------- reference arm
+def bench_reference(args, world, rank):
+    """The reference's CPU operator (oracle port of its PyTorch implementation) on the host cores."""
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing
+
+    if rank != 0:
+        return
+    cfg = CONFIGS[args.config]
+    x = make_hidden(cfg, device="cpu")
+    ids, tw = make_routing(cfg, device="cpu")
+    budget = max(2.0, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_sample(cfg, ids, tw, x, budget_s=budget)
+    tot_f = tot_t = 0.0
+    last = None
+    for k in range(args.steps):
+        f, dt, n, rows = cpu_sample(cfg, ids, tw, x, budget_s=budget, seed=k)
+        tot_f += f
+        tot_t += dt
+        last = (n, rows, dt)
+    value = tot_f / tot_t / 1e12
+    flops = cfg.flops()
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(flops / (value * 1e12) * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (fp16 inputs)",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"{cfg.name}: fused MoE T={cfg.T} H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"per step: oracle over the routed rows of a subset of experts "
+                                   f"(last step {last[0]} experts, {last[1]} rows, {last[2]:.1f} s); "
+                                   f"ms_per_step extrapolates one full call"},
+        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="cfg3")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        bench_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        bench_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

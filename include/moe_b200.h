@@ -1,0 +1,175 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) fused Mixture-of-Experts operator.
+ *
+ * Conventions (the judge's CUDA C ABI for this operator, xpuoj_data/evaluation_guide.md:79-97):
+ *   - every tensor is a device pointer (`void*`) to contiguous, row-major memory on the current
+ *     CUDA device; integers are int64_t; `stream` is a cudaStream_t (NULL = legacy default);
+ *   - calls are stream-ordered and asynchronous: no entry point synchronises the device or the
+ *     stream, except moe_device_status();
+ *   - the caller owns every buffer, including the scratch `workspace` (size from the matching
+ *     *_workspace_bytes query); outputs are the only memory written besides the workspace;
+ *   - every entry point returns 0 on success or a negative moe_status_t, and never aborts; the
+ *     message of the last failure on the calling thread is returned by moe_last_error();
+ *   - the library holds no mutable state other than per-device launch-attribute flags, a
+ *     per-device SM-count cache and the per-device status word below.
+ *
+ * Element types (`dtype` arguments): MOE_F16 / MOE_BF16 for activations, weights and outputs,
+ * MOE_F32 / MOE_F16 / MOE_BF16 for routing weights, MOE_I32 / MOE_I64 for expert ids.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  MOE_F16 = 0,
+  MOE_BF16 = 1,
+  MOE_F32 = 2,
+  MOE_I32 = 3,
+  MOE_I64 = 4,
+  MOE_I8 = 5
+} moe_dtype_t;
+
+typedef enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID_ARG = -1,  /* bad shape, count or dtype */
+  MOE_ERR_UNSUPPORTED = -2,  /* valid request this build does not implement */
+  MOE_ERR_ALIGNMENT = -3,    /* pointer or row pitch not 16-byte aligned */
+  MOE_ERR_CUDA = -4,         /* a CUDA runtime/driver call failed */
+  MOE_ERR_WORKSPACE = -5     /* workspace missing or smaller than the query returned */
+} moe_status_t;
+
+/* Library version string. */
+MOE_API const char* moe_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+MOE_API const char* moe_last_error(void);
+
+/* Reads (and with `clear` != 0 resets) the device status word of the current device after
+ * synchronising `stream`: bit 0 = a bounded pipeline wait gave up, bit 1 = an expert index
+ * outside [0, E) was met, bit 2 = a route index outside [0, R). 0 means every kernel since the
+ * last clear completed normally. No reference counterpart (the reference has no device-side
+ * error reporting). */
+MOE_API int moe_device_status(void* stream, int clear, uint32_t* status_out);
+
+/* Profiling hook, no reference counterpart. While set on the calling thread, moe_fused and
+ * moe_fused_int8 record the given cudaEvent_t handles on their stream at stage boundaries:
+ *   [0] before alignment, [1] after alignment, [2] after the gather, [3] after Stage1,
+ *   [4] after Stage2 (int8: [4] after the intermediate requantisation, [5] after Stage2).
+ * Events beyond n are not recorded. events = NULL or n = 0 turns the hook off. */
+MOE_API int moe_set_profile_events(void* const* events, int n);
+
+/* ------------------------------------------------------------------------------------------
+ * Reference drop-in: the contest operator.
+ * Replaces run_kernel(stacked_expert_tokens, gate_w, up_w, down_w, routed_expert_weights,
+ * group_sizes, group_offsets, group_padded_offsets, group_idx_for_bx, out)
+ * (初审材料/源代码/submission.py:2098-2184; problem statement xpuoj_data/problem1_contest5.json,
+ * interface section), with the shape scalars the Python entry point reads from tensor shapes
+ * (:2110-2115) passed explicitly, as the judge's C ABI does for `int` arguments.
+ *
+ *   stacked_expert_tokens [P, H]  dtype   (expert-grouped, padded to 128 rows per expert)
+ *   gate_w, up_w          [E, I, H] dtype
+ *   down_w                [E, H, I] dtype
+ *   routed_expert_weights [R]     routed_dtype (MOE_F32 or MOE_F16), real-token order
+ *   group_sizes [E], group_offsets [E+1], group_padded_offsets [E+1], group_idx_for_bx [P/128]  int32
+ *   out                   [P, H]  dtype   (written in full: pad rows = 0)
+ * Empty inputs follow the reference (:2117-2153): P == 0 writes nothing, R == 0 zero-fills out.
+ * Route indices are clamped to [0, R-1] as in :935-947.
+ * Requirements: H % 8 == 0, I % 8 == 0, P == 128 * num_blocks_m, 16-byte aligned pointers.
+ * workspace >= moe_run_kernel_workspace_bytes(P, I, dtype) (the reference's cached up_logits
+ * [P, I] buffer, :2081-2095).
+ * ---------------------------------------------------------------------------------------- */
+MOE_API size_t moe_run_kernel_workspace_bytes(int64_t total_padded_tokens, int64_t intermediate, int dtype);
+
+MOE_API int moe_run_kernel(const void* stacked_expert_tokens, const void* gate_w, const void* up_w, const void* down_w,
+                   const void* routed_expert_weights, int routed_dtype, const int32_t* group_sizes,
+                   const int32_t* group_offsets, const int32_t* group_padded_offsets,
+                   const int32_t* group_idx_for_bx, void* out, int64_t total_padded_tokens, int64_t hidden,
+                   int64_t intermediate, int64_t num_experts, int64_t total_valid_tokens, int64_t num_blocks_m,
+                   int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Routing alignment on the device.
+ * Replaces the metadata construction the reference's callers run in torch before run_kernel
+ * (初审材料/源代码/benchmark/remote_bench.py:82-101, race_stress2.py:65-69): histogram of the
+ * flat top-k ids, cumsum, ceil to block_m, repeat_interleave — plus the row permutation
+ * (sorted_route_ids, a stable argsort of the ids; route_slot, its inverse).
+ *
+ *   topk_ids [R] (ids_dtype MOE_I32 / MOE_I64); ids outside [0, E) are skipped
+ *   group_sizes [E], group_offsets [E+1], group_padded_offsets [E+1]       int32
+ *   group_idx_for_bx [moe_max_padded_rows(R,E,block_m) / block_m] int32 (may be NULL)
+ *   sorted_route_ids [moe_max_padded_rows(R,E,block_m)] int32, pad rows hold R
+ *   route_slot [R] int32 (-1 for skipped ids)
+ *   meta [4] int32: {P, P / block_m, valid routes, 0}
+ * Requirements: 1 <= E <= 1024, block_m >= 1.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API int64_t moe_max_padded_rows(int64_t num_routes, int64_t num_experts, int64_t block_m);
+MOE_API size_t moe_align_workspace_bytes(int64_t num_routes, int64_t num_experts);
+
+MOE_API int moe_align(const void* topk_ids, int ids_dtype, int64_t num_routes, int64_t num_experts, int64_t block_m,
+              int32_t* group_sizes, int32_t* group_offsets, int32_t* group_padded_offsets,
+              int32_t* group_idx_for_bx, int32_t* sorted_route_ids, int32_t* route_slot, int32_t* meta,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Fused MoE on token-major tensors (the routed expert MLP with routing, grouping and the top-k
+ * combine included). Mathematically the reference operator (problem1_contest5.json, PyTorch
+ * reference section) applied to the stacked layout that moe_align builds, followed by the
+ * weighted sum over each token's top-k routes that the reference leaves to its caller:
+ *   out[t] = sum_j topk_weights[t, j] * Down_e(silu(Gate_e x_t) * Up_e x_t),  e = topk_ids[t, j]
+ *
+ *   hidden_states [T, H] dtype;  w_gate_up [E, 2I, H] dtype (rows 0..I-1 gate, I..2I-1 up);
+ *   w_down [E, H, I] dtype;  topk_ids [T, topk] ids_dtype;  topk_weights [T, topk] weights_dtype;
+ *   out [T, H] dtype.
+ * No device synchronisation: block counts stay on the device.
+ * Requirements: H % 8 == 0, I % 8 == 0, 1 <= E <= 1024.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API size_t moe_fused_workspace_bytes(int64_t num_tokens, int64_t topk, int64_t num_experts, int64_t hidden,
+                                 int64_t intermediate, int dtype);
+
+MOE_API int moe_fused(const void* hidden_states, const void* w_gate_up, const void* w_down, const void* topk_ids,
+              int ids_dtype, const void* topk_weights, int weights_dtype, void* out, int64_t num_tokens,
+              int64_t hidden, int64_t intermediate, int64_t num_experts, int64_t topk, int dtype,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * W8A8 int8 route. Semantics of the reference's int8 experiment
+ * (xpuoj_data/submission_v322_int8_v2.py:164-205 weight quantisation, :207-232 activation
+ * quantisation, :234-454 int8 GEMMs with int32 accumulation and dequantisation), with one scale
+ * per weight output row and per token instead of per expert / fixed.
+ *
+ * moe_quantize_rows_int8: q[r, :] = round_half_away(w[r, :] * 127 / amax_r), scale[r] = amax_r/127,
+ *   w [rows, K] dtype -> q [rows, K] int8, scale [rows] fp32. Used offline on the weights.
+ * moe_fused_int8: as moe_fused, with w13_q [E, 2I, H] int8 + w13_scale [E*2I] fp32 and
+ *   w2_q [E, H, I] int8 + w2_scale [E*H] fp32; activations quantised per token on the device;
+ *   the Stage1 intermediate is re-quantised per row; int32 accumulation; `dtype` output.
+ * Requirements: H % 16 == 0, I % 16 == 0, 1 <= E <= 1024.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale,
+                           void* stream);
+
+MOE_API size_t moe_fused_int8_workspace_bytes(int64_t num_tokens, int64_t topk, int64_t num_experts, int64_t hidden,
+                                      int64_t intermediate, int dtype);
+
+MOE_API int moe_fused_int8(const void* hidden_states, const void* w13_q, const float* w13_scale, const void* w2_q,
+                   const float* w2_scale, const void* topk_ids, int ids_dtype, const void* topk_weights,
+                   int weights_dtype, void* out, int64_t num_tokens, int64_t hidden, int64_t intermediate,
+                   int64_t num_experts, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

@@ -1,0 +1,20 @@
+"""muxi_race_b200 — a B200-native (sm_100a) fused Mixture-of-Experts operator.
+
+Entry points:
+  run_kernel(...)      drop-in for the contest operator's ``run_kernel`` (10 tensors, padded layout)
+  fused_moe(...)       token-major fused MoE (routing alignment + both GEMM stages + top-k combine)
+  fused_moe_int8(...)  W8A8 variant; weights from quantize_rows_int8()
+  moe_align(...)       device-side routing metadata
+  ep.ExpertParallelMoE expert-parallel fused MoE over torch.distributed (NCCL all-to-all)
+
+All compute runs in hand-written CUDA kernels of ``libmoe_b200.so`` (C ABI in
+``include/moe_b200.h``); there is no CPU or library fallback.
+"""
+from .fused import (Alignment, clear_workspace_cache, device_status, fused_moe, fused_moe_int8, max_padded_rows,
+                    moe_align, quantize_rows_int8)
+from .submission import run_kernel
+
+__all__ = [
+    "Alignment", "clear_workspace_cache", "device_status", "fused_moe", "fused_moe_int8", "max_padded_rows",
+    "moe_align", "quantize_rows_int8", "run_kernel",
+]

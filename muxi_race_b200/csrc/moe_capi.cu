@@ -1,0 +1,602 @@
+// moe_capi.cu — host side of the C ABI declared in include/moe_b200.h: argument checks, TMA
+// descriptor encoding, workspace carving and the launch sequences of the three operator paths.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/moe_b200.h"
+#include "gather_quant.cuh"
+#include "moe_gemm.cuh"
+#include "route_align.cuh"
+
+namespace moe {
+
+__device__ uint32_t g_status;  // device status word (kStatus* bits)
+
+namespace {
+
+thread_local std::string t_last_error;
+thread_local void* const* t_prof_events = nullptr;
+thread_local int t_prof_n = 0;
+
+void prof_record(int i, cudaStream_t s) {
+  if (t_prof_events && i < t_prof_n && t_prof_events[i]) cudaEventRecord(static_cast<cudaEvent_t>(t_prof_events[i]), s);
+}
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+#define MOE_CUDA(call)                                                                        \
+  do {                                                                                        \
+    cudaError_t err_ = (call);                                                                \
+    if (err_ != cudaSuccess)                                                                  \
+      return fail(MOE_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(err_), __FILE__, __LINE__); \
+  } while (0)
+
+#define MOE_TRY(expr)          \
+  do {                         \
+    int rc_ = (expr);          \
+    if (rc_ != MOE_OK) return rc_; \
+  } while (0)
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  std::atomic<int> sms{0};
+  std::atomic<uint32_t*> status{nullptr};
+  std::atomic<uint32_t> attr_done{0};  // bit per kernel whose smem attribute has been raised
+};
+DeviceInfo g_dev[kMaxDevices];
+
+int current_device(int* dev) {
+  MOE_CUDA(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(MOE_ERR_UNSUPPORTED, "device ordinal %d out of range", *dev);
+  return MOE_OK;
+}
+
+int device_sms(int dev, int* sms) {
+  int v = g_dev[dev].sms.load(std::memory_order_relaxed);
+  if (v == 0) {
+    MOE_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    g_dev[dev].sms.store(v, std::memory_order_relaxed);
+  }
+  *sms = v;
+  return MOE_OK;
+}
+
+int device_status_ptr(int dev, uint32_t** p) {
+  uint32_t* v = g_dev[dev].status.load(std::memory_order_acquire);
+  if (v == nullptr) {
+    MOE_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&v), g_status));
+    g_dev[dev].status.store(v, std::memory_order_release);
+  }
+  *p = v;
+  return MOE_OK;
+}
+
+template <typename K>
+int raise_smem(int dev, int bit, K kernel, int bytes) {
+  const uint32_t mask = 1u << bit;
+  if (g_dev[dev].attr_done.load(std::memory_order_acquire) & mask) return MOE_OK;
+  MOE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  g_dev[dev].attr_done.fetch_or(mask, std::memory_order_acq_rel);
+  return MOE_OK;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Row-major [rows, cols] matrix, box = box_rows x (128 bytes), 128-byte swizzle.
+int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, int64_t cols, int box_rows,
+              const char* what) {
+  auto enc = get_encode();
+  if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MOE_ERR_ALIGNMENT, "%s is not 16-byte aligned", what);
+  if ((cols * elt_bytes) % 16 != 0) return fail(MOE_ERR_ALIGNMENT, "%s row pitch is not a multiple of 16 bytes", what);
+  if (rows <= 0 || rows > (int64_t(1) << 31) - 1 || cols <= 0 || cols > (int64_t(1) << 31) - 1)
+    return fail(MOE_ERR_INVALID_ARG, "%s has unsupported extent %lld x %lld", what, (long long)rows, (long long)cols);
+  const CUtensorMapDataType dt = elt_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * elt_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBytes / elt_bytes), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, (int)r);
+  return MOE_OK;
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ------------------------------------------------------------------ GEMM launch
+enum KernelBit {
+  kBitS1F16 = 0, kBitS1BF16, kBitS2PadF16, kBitS2PadBF16, kBitS2CombF16, kBitS2CombBF16,
+  kBitS1I8F16, kBitS1I8BF16, kBitS2CombI8F16, kBitS2CombI8BF16
+};
+
+template <int MODE, typename OutT, bool I8>
+int launch_gemm(int dev, int bit, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_kernel<MODE, OutT, I8>;
+  MOE_TRY(raise_smem(dev, bit, kern, kSmemBytes));
+  int sms = 0;
+  MOE_TRY(device_sms(dev, &sms));
+  const int grid = max_tiles < sms ? max_tiles : sms;
+  if (grid <= 0) return MOE_OK;
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(a, b0, b1, args);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+// ------------------------------------------------------------------ align
+int align_chunk(int64_t R) {
+  int64_t c = (R + 255) / 256;
+  c = (c + 31) / 32 * 32;
+  if (c < 256) c = 256;
+  if (c > 4096) c = 4096;
+  return static_cast<int>(c);
+}
+int64_t align_chunks(int64_t R) { return R <= 0 ? 0 : (R + align_chunk(R) - 1) / align_chunk(R); }
+
+int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, int32_t* gs, int32_t* go,
+                 int32_t* gpo, int32_t* gidx, int32_t* sorted, int32_t* route_slot, int32_t* meta, int* counts,
+                 cudaStream_t stream) {
+  const int chunk = align_chunk(R);
+  const int n_chunks = static_cast<int>(align_chunks(R));
+  const int grid = (n_chunks + kAlignWarps - 1) / kAlignWarps;
+  const size_t smem = sizeof(int) * kAlignWarps * E;
+  if (n_chunks > 0) {
+    if (ids_dtype == MOE_I32)
+      align_count_kernel<int32_t><<<grid, kAlignWarps * 32, smem, stream>>>(
+          static_cast<const int32_t*>(ids), (int)R, (int)E, chunk, n_chunks, counts);
+    else
+      align_count_kernel<int64_t><<<grid, kAlignWarps * 32, smem, stream>>>(
+          static_cast<const int64_t*>(ids), (int)R, (int)E, chunk, n_chunks, counts);
+    MOE_CUDA(cudaGetLastError());
+  }
+  align_scan_kernel<<<1, 1024, 0, stream>>>(counts, n_chunks, (int)E, (int)bm, (int)R, gs, go, gpo, gidx, sorted, meta);
+  MOE_CUDA(cudaGetLastError());
+  if (n_chunks > 0) {
+    if (ids_dtype == MOE_I32)
+      align_scatter_kernel<int32_t><<<grid, kAlignWarps * 32, smem, stream>>>(
+          static_cast<const int32_t*>(ids), (int)R, (int)E, chunk, n_chunks, counts, gpo, sorted, route_slot);
+    else
+      align_scatter_kernel<int64_t><<<grid, kAlignWarps * 32, smem, stream>>>(
+          static_cast<const int64_t*>(ids), (int)R, (int)E, chunk, n_chunks, counts, gpo, sorted, route_slot);
+    MOE_CUDA(cudaGetLastError());
+  }
+  return MOE_OK;
+}
+
+// Workspace carving for the token-major paths.
+struct FusedLayout {
+  size_t counts, gs, go, gpo, meta, gidx, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
+  int64_t P_max, nblk_max;
+};
+
+FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8) {
+  FusedLayout L{};
+  const int64_t R = T * topk;
+  L.P_max = moe_max_padded_rows(R, E, kBM);
+  L.nblk_max = L.P_max / kBM;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = round_up(off + bytes, 256);
+    return o;
+  };
+  L.counts = take(sizeof(int) * (size_t)align_chunks(R) * E);
+  L.gs = take(sizeof(int) * E);
+  L.go = take(sizeof(int) * (E + 1));
+  L.gpo = take(sizeof(int) * (E + 1));
+  L.meta = take(sizeof(int) * 4);
+  L.gidx = take(sizeof(int) * (size_t)L.nblk_max);
+  L.sorted = take(sizeof(int) * (size_t)L.P_max);
+  L.slot = take(sizeof(int) * (size_t)R);
+  L.xs = take((int8 ? 1 : 2) * (size_t)L.P_max * H);
+  L.xscale = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
+  L.u = take(2 * (size_t)L.P_max * I);
+  L.uq = take(int8 ? (size_t)L.P_max * I : 0);
+  L.uscale = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
+  L.amax = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
+  L.total = off;
+  return L;
+}
+
+int check_common(int64_t H, int64_t I, int64_t E, int dtype, int mult) {
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (H <= 0 || I <= 0 || E <= 0) return fail(MOE_ERR_INVALID_ARG, "hidden, intermediate and experts must be > 0");
+  if (H % mult != 0 || I % mult != 0)
+    return fail(MOE_ERR_INVALID_ARG, "hidden (%lld) and intermediate (%lld) must be multiples of %d", (long long)H,
+                (long long)I, mult);
+  if (H > (1 << 30) || I > (1 << 30)) return fail(MOE_ERR_INVALID_ARG, "hidden/intermediate too large");
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+const char* moe_version(void) { return "muxi_race_b200 0.1.0 (sm_100a)"; }
+
+const char* moe_last_error(void) { return t_last_error.c_str(); }
+
+int moe_set_profile_events(void* const* events, int n) {
+  t_prof_events = n > 0 ? events : nullptr;
+  t_prof_n = n > 0 ? n : 0;
+  return MOE_OK;
+}
+
+int moe_device_status(void* stream, int clear, uint32_t* status_out) {
+  int dev;
+  MOE_TRY(current_device(&dev));
+  uint32_t* p;
+  MOE_TRY(device_status_ptr(dev, &p));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  MOE_CUDA(cudaMemcpyAsync(&v, p, sizeof(v), cudaMemcpyDeviceToHost, s));
+  MOE_CUDA(cudaStreamSynchronize(s));
+  if (clear) {
+    MOE_CUDA(cudaMemsetAsync(p, 0, sizeof(uint32_t), s));
+    MOE_CUDA(cudaStreamSynchronize(s));
+  }
+  if (status_out) *status_out = v;
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------- run_kernel
+size_t moe_run_kernel_workspace_bytes(int64_t P, int64_t I, int dtype) {
+  (void)dtype;
+  if (P <= 0 || I <= 0) return 0;
+  return round_up(static_cast<size_t>(P) * I * 2, 256);
+}
+
+int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const void* down_w, const void* routed,
+                   int routed_dtype, const int32_t* gs, const int32_t* go, const int32_t* gpo, const int32_t* gidx,
+                   void* out, int64_t P, int64_t H, int64_t I, int64_t E, int64_t R, int64_t nblk, int dtype,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(check_common(H, I, E, dtype, 8));
+  if (P < 0 || R < 0 || nblk < 0) return fail(MOE_ERR_INVALID_ARG, "negative size");
+  if (P != nblk * kBM)
+    return fail(MOE_ERR_INVALID_ARG, "total_padded_tokens (%lld) != 128 * num_blocks_m (%lld)", (long long)P,
+                (long long)nblk);
+  if (routed_dtype != MOE_F32 && routed_dtype != MOE_F16)
+    return fail(MOE_ERR_INVALID_ARG, "routed_expert_weights must be fp32 or fp16");
+  if (P > (int64_t(1) << 31) - 1 || R > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "too many rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (P == 0) return MOE_OK;  // SUB/submission.py:2117-2120
+  if (!out || !aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "out must be a 16-byte aligned device pointer");
+  if (R == 0) {  // SUB/submission.py:2130-2153: no valid rows, Stage2 zero-fills the padded output
+    MOE_CUDA(cudaMemsetAsync(out, 0, static_cast<size_t>(P) * H * 2, s));
+    return MOE_OK;
+  }
+  if (!x || !gate_w || !up_w || !down_w || !routed || !gs || !go || !gpo || !gidx)
+    return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  if (!workspace || workspace_bytes < moe_run_kernel_workspace_bytes(P, I, dtype))
+    return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", moe_run_kernel_workspace_bytes(P, I, dtype));
+  if (!aligned16(workspace)) return fail(MOE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  if (E * I > (int64_t(1) << 31) - 1 || E * H > (int64_t(1) << 31) - 1)
+    return fail(MOE_ERR_INVALID_ARG, "experts x rows exceeds the TMA coordinate range");
+  int dev;
+  MOE_TRY(current_device(&dev));
+  uint32_t* status;
+  MOE_TRY(device_status_ptr(dev, &status));
+
+  CUtensorMap tA, tG, tU, tUA, tD;
+  MOE_TRY(make_tmap(&tA, x, 2, P, H, kBM, "stacked_expert_tokens"));
+  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, kBN / 2, "gate_w"));
+  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, kBN / 2, "up_w"));
+  MOE_TRY(make_tmap(&tUA, workspace, 2, P, I, kBM, "workspace"));
+  MOE_TRY(make_tmap(&tD, down_w, 2, E * H, I, kBN, "down_w"));
+
+  GemmArgs a1{};
+  a1.K = (int)H;
+  a1.N = (int)I;
+  a1.n_tiles = (int)((I + kBN / 2 - 1) / (kBN / 2));
+  a1.nblk = (int)nblk;
+  a1.E = (int)E;
+  a1.block_expert = gidx;
+  a1.b_rows_per_expert = (int)I;
+  a1.b1_row_offset = 0;
+  a1.U = workspace;
+  a1.ldu = (int)I;
+  a1.status = status;
+
+  GemmArgs a2{};
+  a2.K = (int)I;
+  a2.N = (int)H;
+  a2.n_tiles = (int)((H + kBN - 1) / kBN);
+  a2.nblk = (int)nblk;
+  a2.E = (int)E;
+  a2.block_expert = gidx;
+  a2.b_rows_per_expert = (int)H;
+  a2.out = out;
+  a2.ldo = (int)H;
+  a2.group_sizes = gs;
+  a2.group_offsets = go;
+  a2.group_padded_offsets = gpo;
+  a2.routed = routed;
+  a2.routed_dtype = routed_dtype == MOE_F32 ? 0 : 1;
+  a2.R = (int)R;
+  a2.status = status;
+
+  const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
+  if (dtype == MOE_F16) {
+    MOE_TRY((launch_gemm<kStage1, __half, false>(dev, kBitS1F16, tA, tG, tU, a1, tiles1, s)));
+    MOE_TRY((launch_gemm<kStage2Pad, __half, false>(dev, kBitS2PadF16, tUA, tD, tD, a2, tiles2, s)));
+  } else {
+    MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, false>(dev, kBitS1BF16, tA, tG, tU, a1, tiles1, s)));
+    MOE_TRY((launch_gemm<kStage2Pad, __nv_bfloat16, false>(dev, kBitS2PadBF16, tUA, tD, tD, a2, tiles2, s)));
+  }
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------- align
+int64_t moe_max_padded_rows(int64_t R, int64_t E, int64_t bm) {
+  if (R <= 0 || E <= 0 || bm <= 0) return 0;
+  const int64_t nonempty = R < E ? R : E;
+  return (R + nonempty * (bm - 1) + bm - 1) / bm * bm;
+}
+
+size_t moe_align_workspace_bytes(int64_t R, int64_t E) {
+  return round_up(sizeof(int) * static_cast<size_t>(align_chunks(R)) * static_cast<size_t>(E > 0 ? E : 0), 256);
+}
+
+int moe_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, int32_t* gs, int32_t* go,
+              int32_t* gpo, int32_t* gidx, int32_t* sorted, int32_t* route_slot, int32_t* meta, void* workspace,
+              size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (E < 1 || E > kAlignMaxExperts) return fail(MOE_ERR_INVALID_ARG, "num_experts must be in [1, %d]", kAlignMaxExperts);
+  if (bm < 1 || bm > (1 << 20)) return fail(MOE_ERR_INVALID_ARG, "block_m must be in [1, 2^20]");
+  if (R < 0 || moe_max_padded_rows(R, E, bm) > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "bad route count");
+  if (ids_dtype != MOE_I32 && ids_dtype != MOE_I64) return fail(MOE_ERR_INVALID_ARG, "topk_ids must be int32 or int64");
+  if (!gs || !go || !gpo || !sorted || !meta || (R > 0 && (!ids || !route_slot)))
+    return fail(MOE_ERR_INVALID_ARG, "null output");
+  if (R > 0 && (!workspace || workspace_bytes < moe_align_workspace_bytes(R, E)))
+    return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", moe_align_workspace_bytes(R, E));
+  MOE_TRY(launch_align(ids, ids_dtype, R, E, bm, gs, go, gpo, gidx, sorted, route_slot, meta,
+                       static_cast<int*>(workspace), static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------- fused
+size_t moe_fused_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
+  (void)dtype;
+  if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+  return fused_layout(T, topk, E, H, I, false).total;
+}
+
+static int fused_common(bool int8, const void* x, const void* w13, const float* w13_scale, const void* w2,
+                        const float* w2_scale, const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out,
+                        int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(check_common(H, I, E, dtype, int8 ? 16 : 8));
+  if (T < 0 || topk < 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be >= 0 and topk >= 1");
+  if (E > kAlignMaxExperts) return fail(MOE_ERR_INVALID_ARG, "num_experts must be <= %d", kAlignMaxExperts);
+  if (ids_dtype != MOE_I32 && ids_dtype != MOE_I64) return fail(MOE_ERR_INVALID_ARG, "topk_ids must be int32 or int64");
+  if (w_dtype != MOE_F32 && w_dtype != MOE_F16 && w_dtype != MOE_BF16)
+    return fail(MOE_ERR_INVALID_ARG, "topk_weights must be fp32, fp16 or bf16");
+  if (T == 0) return MOE_OK;
+  const int64_t R = T * topk;
+  if (moe_max_padded_rows(R, E, kBM) > (int64_t(1) << 31) - 1 || 2 * E * I > (int64_t(1) << 31) - 1 ||
+      E * H > (int64_t(1) << 31) - 1)
+    return fail(MOE_ERR_INVALID_ARG, "problem exceeds 32-bit row indexing");
+  if (!x || !w13 || !w2 || !ids || !tw || !out) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  if (int8 && (!w13_scale || !w2_scale)) return fail(MOE_ERR_INVALID_ARG, "null weight scales");
+  if (!aligned16(x) || !aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "hidden_states/out must be 16-byte aligned");
+  const FusedLayout L = fused_layout(T, topk, E, H, I, int8);
+  if (!workspace || workspace_bytes < L.total) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", L.total);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+
+  int dev;
+  MOE_TRY(current_device(&dev));
+  uint32_t* status;
+  MOE_TRY(device_status_ptr(dev, &status));
+  int sms;
+  MOE_TRY(device_sms(dev, &sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + L.counts);
+  int32_t* gs = reinterpret_cast<int32_t*>(ws + L.gs);
+  int32_t* go = reinterpret_cast<int32_t*>(ws + L.go);
+  int32_t* gpo = reinterpret_cast<int32_t*>(ws + L.gpo);
+  int32_t* meta = reinterpret_cast<int32_t*>(ws + L.meta);
+  int32_t* gidx = reinterpret_cast<int32_t*>(ws + L.gidx);
+  int32_t* sorted = reinterpret_cast<int32_t*>(ws + L.sorted);
+  int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
+  void* xs = ws + L.xs;
+  void* U = ws + L.u;
+
+  // 1. routing metadata
+  prof_record(0, s);
+  MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s));
+  prof_record(1, s);
+
+  // 2. gather token rows into the expert-grouped layout (+ per-token int8 quantisation),
+  //    zero the output the Stage2 epilogue accumulates into
+  const int gblocks = sms * 4;
+  float* amax = int8 ? reinterpret_cast<float*>(ws + L.amax) : nullptr;
+  float* xscale = int8 ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
+  if (dtype == MOE_F16) {
+    if (int8)
+      gather_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
+                                                            (int)H, static_cast<int8_t*>(xs), xscale,
+                                                            static_cast<__half*>(out), (int)T, amax, (int)L.P_max);
+    else
+      gather_rows_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
+                                                         (int)H, static_cast<__half*>(xs), static_cast<__half*>(out),
+                                                         (int)T, nullptr, 0);
+  } else {
+    if (int8)
+      gather_rows_q8_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<int8_t*>(xs), xscale,
+          static_cast<__nv_bfloat16*>(out), (int)T, amax, (int)L.P_max);
+    else
+      gather_rows_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<__nv_bfloat16*>(xs),
+          static_cast<__nv_bfloat16*>(out), (int)T, nullptr, 0);
+  }
+  MOE_CUDA(cudaGetLastError());
+  prof_record(2, s);
+
+  // 3. Stage1 (gate/up GEMM + SiLU*up) and 4. Stage2 (down GEMM * topk weight, combine)
+  const int elt = int8 ? 1 : 2;
+  CUtensorMap tA, tW13, tUA, tW2;
+  MOE_TRY(make_tmap(&tA, xs, elt, L.P_max, H, kBM, "gathered hidden_states"));
+  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, kBN / 2, "w_gate_up"));
+  MOE_TRY(make_tmap(&tUA, int8 ? (void*)(ws + L.uq) : U, elt, L.P_max, I, kBM, "intermediate"));
+  MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kBN, "w_down"));
+
+  GemmArgs a1{};
+  a1.K = (int)H;
+  a1.N = (int)I;
+  a1.n_tiles = (int)((I + kBN / 2 - 1) / (kBN / 2));
+  a1.nblk = -1;
+  a1.nblk_dev = meta + 1;
+  a1.E = (int)E;
+  a1.block_expert = gidx;
+  a1.b_rows_per_expert = (int)(2 * I);
+  a1.b1_row_offset = (int)I;
+  a1.U = U;
+  a1.ldu = (int)I;
+  a1.a_scale = xscale;
+  a1.b0_scale = w13_scale;
+  a1.b1_scale = w13_scale;
+  a1.row_amax = amax;
+  a1.status = status;
+
+  GemmArgs a2{};
+  a2.K = (int)I;
+  a2.N = (int)H;
+  a2.n_tiles = (int)((H + kBN - 1) / kBN);
+  a2.nblk = -1;
+  a2.nblk_dev = meta + 1;
+  a2.E = (int)E;
+  a2.block_expert = gidx;
+  a2.b_rows_per_expert = (int)H;
+  a2.out = out;
+  a2.ldo = (int)H;
+  a2.routed = tw;
+  a2.routed_dtype = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
+  a2.R = (int)R;
+  a2.sorted_route_ids = sorted;
+  a2.topk = (int)topk;
+  a2.a_scale = int8 ? reinterpret_cast<const float*>(ws + L.uscale) : nullptr;
+  a2.b0_scale = w2_scale;
+  a2.status = status;
+
+  const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
+  if (!int8) {
+    if (dtype == MOE_F16) {
+      MOE_TRY((launch_gemm<kStage1, __half, false>(dev, kBitS1F16, tA, tW13, tW13, a1, max_tiles1, s)));
+      prof_record(3, s);
+      MOE_TRY((launch_gemm<kStage2Comb, __half, false>(dev, kBitS2CombF16, tUA, tW2, tW2, a2, max_tiles2, s)));
+    } else {
+      MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, false>(dev, kBitS1BF16, tA, tW13, tW13, a1, max_tiles1, s)));
+      prof_record(3, s);
+      MOE_TRY((launch_gemm<kStage2Comb, __nv_bfloat16, false>(dev, kBitS2CombBF16, tUA, tW2, tW2, a2, max_tiles2, s)));
+    }
+    prof_record(4, s);
+  } else {
+    // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
+    if (dtype == MOE_F16)
+      MOE_TRY((launch_gemm<kStage1, __half, true>(dev, kBitS1I8F16, tA, tW13, tW13, a1, max_tiles1, s)));
+    else
+      MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, true>(dev, kBitS1I8BF16, tA, tW13, tW13, a1, max_tiles1, s)));
+    prof_record(3, s);
+    if (dtype == MOE_F16)
+      quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
+                                                              amax, reinterpret_cast<int8_t*>(ws + L.uq),
+                                                              reinterpret_cast<float*>(ws + L.uscale));
+    else
+      quantize_rows_q8_kernel<__nv_bfloat16><<<sms * 4, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
+          reinterpret_cast<float*>(ws + L.uscale));
+    MOE_CUDA(cudaGetLastError());
+    prof_record(4, s);
+    if (dtype == MOE_F16)
+      MOE_TRY((launch_gemm<kStage2Comb, __half, true>(dev, kBitS2CombI8F16, tUA, tW2, tW2, a2, max_tiles2, s)));
+    else
+      MOE_TRY((launch_gemm<kStage2Comb, __nv_bfloat16, true>(dev, kBitS2CombI8BF16, tUA, tW2, tW2, a2, max_tiles2, s)));
+    prof_record(5, s);
+  }
+  return MOE_OK;
+}
+
+int moe_fused(const void* x, const void* w13, const void* w2, const void* ids, int ids_dtype, const void* tw,
+              int w_dtype, void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype,
+              void* workspace, size_t workspace_bytes, void* stream) {
+  return fused_common(false, x, w13, nullptr, w2, nullptr, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk, dtype,
+                      workspace, workspace_bytes, stream);
+}
+
+int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale, void* stream) {
+  t_last_error.clear();
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (rows < 0 || cols <= 0 || cols % 16 != 0) return fail(MOE_ERR_INVALID_ARG, "cols must be a positive multiple of 16");
+  if (rows == 0) return MOE_OK;
+  if (!w || !q || !scale) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  if (!aligned16(w) || !aligned16(q)) return fail(MOE_ERR_ALIGNMENT, "w and q must be 16-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MOE_F16)
+    quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(w), rows, (int)cols, nullptr,
+                                                            nullptr, static_cast<int8_t*>(q), scale);
+  else
+    quantize_rows_q8_kernel<__nv_bfloat16><<<sms * 4, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(w), rows,
+                                                                   (int)cols, nullptr, nullptr,
+                                                                   static_cast<int8_t*>(q), scale);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+size_t moe_fused_int8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
+  (void)dtype;
+  if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+  return fused_layout(T, topk, E, H, I, true).total;
+}
+
+int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, const void* w2_q, const float* w2_scale,
+                   const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out, int64_t T, int64_t H,
+                   int64_t I, int64_t E, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+  return fused_common(true, x, w13_q, w13_scale, w2_q, w2_scale, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
+                      dtype, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,217 @@
+"""Token-major fused MoE: routing alignment, grouped gate/up + SiLU, grouped down + top-k combine.
+
+``fused_moe(hidden_states, w_gate_up, w_down, topk_ids, topk_weights)`` is the north-star call:
+it builds the expert-grouped, 128-row-padded layout that the reference's ``run_kernel`` receives
+pre-built (初审材料/源代码/benchmark/remote_bench.py:82-101), runs the same two GEMM stages
+(初审材料/源代码/submission.py:586-641 and 317-357) and folds the weighted sum over each token's
+top-k routes into the Stage2 epilogue. Every step is a CUDA kernel of ``libmoe_b200.so``; block
+counts stay on the device, so a call never synchronises the host.
+"""
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+BLOCK_M = 128
+_DTYPES = {torch.float16: _lib.MOE_F16, torch.bfloat16: _lib.MOE_BF16}
+_W_DTYPES = {torch.float32: _lib.MOE_F32, torch.float16: _lib.MOE_F16, torch.bfloat16: _lib.MOE_BF16}
+_ID_DTYPES = {torch.int32: _lib.MOE_I32, torch.int64: _lib.MOE_I64}
+
+_WS: dict = {}
+_WS_LOCK = threading.Lock()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _workspace(key, nbytes: int, device: torch.device) -> torch.Tensor:
+    with _WS_LOCK:
+        ws = _WS.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+            _WS[key] = ws
+    return ws
+
+
+def clear_workspace_cache() -> None:
+    with _WS_LOCK:
+        _WS.clear()
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+# ----------------------------------------------------------------------------- alignment
+@dataclass
+class Alignment:
+    """Routing metadata in the reference's layout (remote_bench.py:82-101) plus the permutation."""
+
+    group_sizes: torch.Tensor            # [E] int32
+    group_offsets: torch.Tensor          # [E+1] int32
+    group_padded_offsets: torch.Tensor   # [E+1] int32
+    group_idx_for_bx: torch.Tensor       # [max_blocks] int32 (first num_blocks valid)
+    sorted_route_ids: torch.Tensor       # [max_rows] int32 (first padded_rows valid; pad = R)
+    route_slot: torch.Tensor             # [R] int32
+    meta: torch.Tensor                   # [4] int32: padded rows, blocks, valid routes, 0
+
+    def padded_rows(self) -> int:
+        return int(self.meta[0].item())
+
+    def num_blocks(self) -> int:
+        return int(self.meta[1].item())
+
+
+def max_padded_rows(num_routes: int, num_experts: int, block_m: int = BLOCK_M) -> int:
+    return int(_lib.lib().moe_max_padded_rows(num_routes, num_experts, block_m))
+
+
+def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) -> Alignment:
+    """Device-side routing alignment of the flat ``topk_ids`` (ids outside [0, E) are skipped)."""
+    _check(topk_ids.is_cuda and topk_ids.is_contiguous(), "topk_ids must be a contiguous CUDA tensor")
+    _check(topk_ids.dtype in _ID_DTYPES, "topk_ids must be int32 or int64")
+    dev = topk_ids.device
+    R = topk_ids.numel()
+    p_max = max_padded_rows(R, num_experts, block_m)
+    i32 = dict(dtype=torch.int32, device=dev)
+    al = Alignment(
+        group_sizes=torch.empty(num_experts, **i32),
+        group_offsets=torch.empty(num_experts + 1, **i32),
+        group_padded_offsets=torch.empty(num_experts + 1, **i32),
+        group_idx_for_bx=torch.empty(max(p_max // block_m, 1), **i32),
+        sorted_route_ids=torch.empty(max(p_max, 1), **i32),
+        route_slot=torch.empty(max(R, 1), **i32),
+        meta=torch.empty(4, **i32),
+    )
+    nbytes = _lib.lib().moe_align_workspace_bytes(R, num_experts)
+    ws = _workspace(("align", dev, R, num_experts, _stream(dev)), nbytes, dev)
+    _lib.call(
+        "moe_align", topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], R, num_experts, block_m,
+        al.group_sizes.data_ptr(), al.group_offsets.data_ptr(), al.group_padded_offsets.data_ptr(),
+        al.group_idx_for_bx.data_ptr(), al.sorted_route_ids.data_ptr(), al.route_slot.data_ptr(),
+        al.meta.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev),
+    )
+    return al
+
+
+# ----------------------------------------------------------------------------- fused fp16/bf16
+def _check_fused(hidden_states, w13, w2, topk_ids, topk_weights, int8: bool):
+    _check(hidden_states.dim() == 2, "hidden_states must be [T, H]")
+    T, H = hidden_states.shape
+    _check(w13.dim() == 3 and w2.dim() == 3, "w_gate_up must be [E, 2I, H] and w_down [E, H, I]")
+    E, two_i, h2 = w13.shape
+    I = two_i // 2
+    _check(two_i == 2 * I and h2 == H, f"w_gate_up shape {tuple(w13.shape)} does not match H={H}")
+    _check(tuple(w2.shape) == (E, H, I), f"w_down shape {tuple(w2.shape)} != {(E, H, I)}")
+    _check(topk_ids.shape == topk_weights.shape and topk_ids.dim() == 2 and topk_ids.shape[0] == T,
+           "topk_ids and topk_weights must both be [T, topk]")
+    for t in (hidden_states, w13, w2, topk_ids, topk_weights):
+        _check(t.is_cuda and t.is_contiguous() and t.device == hidden_states.device,
+               "all tensors must be contiguous CUDA tensors on one device")
+    _check(hidden_states.dtype in _DTYPES, f"unsupported activation dtype {hidden_states.dtype}")
+    if int8:
+        _check(w13.dtype == torch.int8 and w2.dtype == torch.int8, "int8 weights expected")
+    else:
+        _check(w13.dtype == hidden_states.dtype and w2.dtype == hidden_states.dtype,
+               "weights must have the activation dtype")
+    _check(topk_ids.dtype in _ID_DTYPES, "topk_ids must be int32 or int64")
+    _check(topk_weights.dtype in _W_DTYPES, "topk_weights must be fp32, fp16 or bf16")
+    return int(T), int(H), int(I), int(E), int(topk_ids.shape[1])
+
+
+def fused_moe(
+    hidden_states: torch.Tensor,
+    w_gate_up: torch.Tensor,
+    w_down: torch.Tensor,
+    topk_ids: torch.Tensor,
+    topk_weights: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """out[t] = sum_j topk_weights[t,j] * W_down[e] (silu(W_gate[e] x_t) * W_up[e] x_t), e = topk_ids[t,j].
+
+    hidden_states [T, H] fp16/bf16; w_gate_up [E, 2I, H] (gate rows first, then up rows);
+    w_down [E, H, I]; topk_ids [T, k] int32/int64; topk_weights [T, k] fp32/fp16/bf16.
+    """
+    T, H, I, E, k = _check_fused(hidden_states, w_gate_up, w_down, topk_ids, topk_weights, False)
+    if out is None:
+        out = torch.empty((T, H), dtype=hidden_states.dtype, device=hidden_states.device)
+    _check(tuple(out.shape) == (T, H) and out.dtype == hidden_states.dtype and out.is_contiguous(), "bad out")
+    if T == 0:
+        return out
+    dev = hidden_states.device
+    dt = _DTYPES[hidden_states.dtype]
+    nbytes = _lib.lib().moe_fused_workspace_bytes(T, k, E, H, I, dt)
+    ws = _workspace(("fused", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    _lib.call(
+        "moe_fused", hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), topk_ids.data_ptr(),
+        _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(), _W_DTYPES[topk_weights.dtype], out.data_ptr(),
+        T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
+    )
+    return out
+
+
+# ----------------------------------------------------------------------------- W8A8 int8
+def quantize_rows_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8: q = round_half_away(w * 127 / amax_row), scale = amax_row / 127.
+
+    ``w`` [..., K] fp16/bf16 (e.g. stacked weights [E, N, K], one scale per output row).
+    Returns (q int8 of w's shape, scale fp32 of shape w.shape[:-1]).
+    """
+    _check(w.is_cuda and w.is_contiguous() and w.dtype in _DTYPES, "w must be a contiguous fp16/bf16 CUDA tensor")
+    K = w.shape[-1]
+    rows = w.numel() // K if K else 0
+    q = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+    scale = torch.empty(w.shape[:-1], dtype=torch.float32, device=w.device)
+    _lib.call("moe_quantize_rows_int8", w.data_ptr(), _DTYPES[w.dtype], rows, K, q.data_ptr(), scale.data_ptr(),
+              _stream(w.device))
+    return q, scale
+
+
+def fused_moe_int8(
+    hidden_states: torch.Tensor,
+    w13_q: torch.Tensor,
+    w13_scale: torch.Tensor,
+    w2_q: torch.Tensor,
+    w2_scale: torch.Tensor,
+    topk_ids: torch.Tensor,
+    topk_weights: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """W8A8 ``fused_moe``: int8 weights with per-output-row scales (from :func:`quantize_rows_int8`),
+    activations quantised per token on the device, int32 accumulation, output in the activation dtype."""
+    T, H, I, E, k = _check_fused(hidden_states, w13_q, w2_q, topk_ids, topk_weights, True)
+    _check(w13_scale.dtype == torch.float32 and w13_scale.numel() == E * 2 * I and w13_scale.is_contiguous(),
+           "w13_scale must be fp32 [E, 2I]")
+    _check(w2_scale.dtype == torch.float32 and w2_scale.numel() == E * H and w2_scale.is_contiguous(),
+           "w2_scale must be fp32 [E, H]")
+    if out is None:
+        out = torch.empty((T, H), dtype=hidden_states.dtype, device=hidden_states.device)
+    if T == 0:
+        return out
+    dev = hidden_states.device
+    dt = _DTYPES[hidden_states.dtype]
+    nbytes = _lib.lib().moe_fused_int8_workspace_bytes(T, k, E, H, I, dt)
+    ws = _workspace(("fused_i8", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    _lib.call(
+        "moe_fused_int8", hidden_states.data_ptr(), w13_q.data_ptr(), w13_scale.data_ptr(), w2_q.data_ptr(),
+        w2_scale.data_ptr(), topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(),
+        _W_DTYPES[topk_weights.dtype], out.data_ptr(), T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
+    )
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    """Device status word of the current device (0 = every kernel completed normally)."""
+    import ctypes
+
+    v = ctypes.c_uint32(0)
+    dev = torch.cuda.current_device()
+    _lib.call("moe_device_status", _stream(torch.device("cuda", dev)), int(clear), ctypes.byref(v))
+    return int(v.value)

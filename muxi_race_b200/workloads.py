@@ -1,0 +1,92 @@
+"""Seeded synthetic inputs with the shapes and distributions of the benchmark configurations.
+
+No dataset or checkpoint is involved: weights ~ N(0, (1/sqrt(fan_in))^2) (fan_in = H for gate/up,
+I for down), hidden_states ~ N(0, 1), router logits ~ N(0, 1) -> softmax -> top-k -> weights
+renormalised to sum to 1. The skewed expert-parallel configuration adds a Zipf(s) bias to the
+logits in log form: expert with popularity rank r (a seeded permutation of the experts) gets
+bias log(r^-s / H_{E,s}), which makes the top experts "hot" (they appear in most tokens' top-k).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass(frozen=True)
+class MoeConfig:
+    name: str
+    T: int
+    H: int
+    I: int
+    E: int
+    topk: int
+    dtype: torch.dtype
+    int8: bool = False
+    zipf_s: float = 0.0
+    note: str = field(default="", compare=False)
+
+    def flops(self, routes: int | None = None) -> float:
+        """Algorithmic FLOPs: 2 * routed rows * 3 * H * I (padding rows excluded)."""
+        r = self.T * self.topk if routes is None else routes
+        return 2.0 * r * 3 * self.H * self.I
+
+    def weight_bytes(self, active_experts: int | None = None) -> float:
+        e = self.E if active_experts is None else active_experts
+        return float(e) * 3 * self.H * self.I * (1 if self.int8 else 2)
+
+    def io_bytes(self) -> float:
+        return 2.0 * self.T * self.H * 2  # hidden_states in + out
+
+
+CONFIGS = {
+    "cfg1": MoeConfig("cfg1", 64, 1024, 512, 8, 2, torch.float16, note="small, CPU-runnable"),
+    "cfg2": MoeConfig("cfg2", 1024, 4096, 14336, 8, 2, torch.bfloat16, note="Mixtral-style"),
+    "cfg3": MoeConfig("cfg3", 4096, 7168, 2048, 256, 8, torch.float16, note="DeepSeek-V3-style, 1 GPU"),
+    "cfg3_t128": MoeConfig("cfg3_t128", 128, 7168, 2048, 256, 8, torch.float16, note="decode-like"),
+    "cfg4": MoeConfig("cfg4", 4096, 7168, 2048, 256, 8, torch.float16, int8=True, note="W8A8 of cfg3"),
+    "cfg5": MoeConfig("cfg5", 32768, 7168, 2048, 256, 8, torch.float16, zipf_s=1.1, note="EP, Zipf-skewed"),
+}
+
+
+def _gen(device, seed: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def make_weights(cfg: MoeConfig, seed: int = 0, device="cuda", experts: int | None = None):
+    """w_gate_up [E, 2I, H] (gate rows then up rows) and w_down [E, H, I] in cfg.dtype."""
+    E = cfg.E if experts is None else experts
+    g = _gen(device, seed)
+    w13 = torch.empty((E, 2 * cfg.I, cfg.H), dtype=cfg.dtype, device=device)
+    w2 = torch.empty((E, cfg.H, cfg.I), dtype=cfg.dtype, device=device)
+    # fill one expert at a time in fp32 to bound the temporary
+    for e in range(E):
+        w13[e].copy_(torch.randn((2 * cfg.I, cfg.H), generator=g, device=device) * (cfg.H ** -0.5))
+        w2[e].copy_(torch.randn((cfg.H, cfg.I), generator=g, device=device) * (cfg.I ** -0.5))
+    return w13, w2
+
+
+def make_hidden(cfg: MoeConfig, seed: int = 1, device="cuda", T: int | None = None) -> torch.Tensor:
+    T = cfg.T if T is None else T
+    return torch.randn((T, cfg.H), generator=_gen(device, seed), device=device).to(cfg.dtype)
+
+
+def zipf_bias(E: int, s: float, seed: int, device="cpu") -> torch.Tensor:
+    ranks = torch.randperm(E, generator=_gen("cpu", seed)).to(torch.float64) + 1.0
+    pmf = ranks.pow(-s)
+    pmf = pmf / pmf.sum()
+    return pmf.log().to(torch.float32).to(device)
+
+
+def make_routing(cfg: MoeConfig, seed: int = 2, device="cuda", T: int | None = None, id_dtype=torch.int32):
+    """topk_ids [T, k] (id_dtype) and topk_weights [T, k] fp32 from softmax-top-k of N(0,1) logits."""
+    T = cfg.T if T is None else T
+    logits = torch.randn((T, cfg.E), generator=_gen(device, seed), device=device)
+    if cfg.zipf_s > 0:
+        logits = logits + zipf_bias(cfg.E, cfg.zipf_s, seed + 1000, device)
+    probs = torch.softmax(logits, dim=-1)
+    vals, ids = torch.topk(probs, cfg.topk, dim=-1)
+    weights = vals / vals.sum(dim=-1, keepdim=True)
+    return ids.to(id_dtype).contiguous(), weights.to(torch.float32).contiguous()

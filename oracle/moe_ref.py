@@ -1,0 +1,209 @@
+"""Oracle for the fused-MoE hot path — TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may use this
+module, and only as the checker or the timed CPU baseline. The product (``muxi_race_b200``) never
+imports it.
+
+What it restates (the reference is William7743/muxi_race):
+
+* ``run_kernel_ref`` — the official PyTorch reference of the contest operator,
+  ``xpuoj_data/problem1_contest5.json``, section "PyTorch 参考实现" (reference implementation):
+  ``out.zero_()``; for each expert with ``valid_count > 0``: slice the padded rows, fp32
+  gate/up matmuls, ``sigmoid(g) * g * u``, fp32 down matmul, scale by
+  ``routed_expert_weights[raw_start : raw_start + valid_count]``, copy into the padded rows as
+  the output dtype. The same formula is ``reference()`` in
+  ``初审材料/源代码/benchmark/race_stress2.py:29-48``. One deliberate difference: weights are
+  converted to fp32 one expert at a time instead of whole-tensor up front (the whole-tensor
+  conversion needs about 67 GB at the 256-expert shape); the arithmetic is identical.
+* ``align_ref`` — the routing metadata the reference harness builds with torch
+  (``初审材料/源代码/benchmark/remote_bench.py:82-101``, ``race_stress2.py:65-69``): bincount,
+  cumsum, ceil to the block size, repeat_interleave; plus ``sorted_route_ids`` = stable argsort
+  of the flat ids laid into the padded rows (pad rows hold R).
+* ``fused_moe_ref`` — the token-major operator: align, stack, ``run_kernel_ref``, then the
+  weighted sum over each token's routes (the combine the reference leaves to its caller;
+  the problem statement excludes "router, top-k or scatter reduce").
+* ``fused_moe_int8_ref`` — the W8A8 route with the quantisation scheme of the reference's int8
+  experiment (``xpuoj_data/submission_v322_int8_v2.py:186-203``: amax/127 scale, round half away
+  from zero, clamp to +-127), per output row for weights and per row for activations.
+
+Parity is pinned by ``tests/golden/`` (outputs of the reference's own PyTorch code, extracted
+from the problem statement and run by ``tests/golden/make_golden.py``).
+
+All functions take torch tensors on any device; with CPU tensors this is the CPU baseline, with
+CUDA tensors it is the plain fp32 PyTorch reference used by the large-shape GPU tests.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+BLOCK_M = 128
+
+
+# --------------------------------------------------------------------------- run_kernel oracle
+def run_kernel_ref(
+    stacked_expert_tokens: torch.Tensor,
+    gate_w: torch.Tensor,
+    up_w: torch.Tensor,
+    down_w: torch.Tensor,
+    routed_expert_weights: torch.Tensor,
+    group_sizes: torch.Tensor,
+    group_offsets: torch.Tensor,
+    group_padded_offsets: torch.Tensor,
+    group_idx_for_bx: torch.Tensor,
+    out: torch.Tensor,
+    experts=None,
+) -> None:
+    """problem1_contest5.json "PyTorch 参考实现", per-expert fp32 conversion.
+
+    ``experts`` (optional iterable) restricts the loop to a subset of experts (bounded CPU
+    baseline samples); rows of other experts are left at zero.
+    """
+    out.zero_()
+    num_experts = int(group_sizes.numel())
+    sizes = group_sizes.tolist()
+    offs = group_offsets.tolist()
+    pads = group_padded_offsets.tolist()
+    x_f32 = stacked_expert_tokens.to(torch.float32)
+    for expert_idx in (range(num_experts) if experts is None else experts):
+        valid_count = int(sizes[expert_idx])
+        if valid_count == 0:
+            continue
+        raw_start = int(offs[expert_idx])
+        padded_start = int(pads[expert_idx])
+        x_e = x_f32[padded_start:padded_start + valid_count]
+        gate_f32 = gate_w[expert_idx].to(torch.float32)
+        up_f32 = up_w[expert_idx].to(torch.float32)
+        down_f32 = down_w[expert_idx].to(torch.float32)
+        gate_logits = torch.matmul(x_e, gate_f32.transpose(0, 1))
+        up_logits = torch.matmul(x_e, up_f32.transpose(0, 1))
+        hidden_act = torch.sigmoid(gate_logits) * gate_logits * up_logits
+        y_e = torch.matmul(hidden_act, down_f32.transpose(0, 1))
+        y_e *= routed_expert_weights[raw_start:raw_start + valid_count].to(torch.float32).unsqueeze(1)
+        out[padded_start:padded_start + valid_count].copy_(y_e.to(out.dtype))
+
+
+def run_kernel_ref_f32(x, gate_w, up_w, down_w, routed, gs, go, gpo, gidx) -> torch.Tensor:
+    """Same as ``run_kernel_ref`` but returns the fp32 result before the output cast
+    (race_stress2.py:29-48 compares against this fp32 tensor)."""
+    P, H = x.shape
+    out = torch.zeros((P, H), dtype=torch.float32, device=x.device)
+    run_kernel_ref(x, gate_w, up_w, down_w, routed, gs, go, gpo, gidx, out)
+    return out
+
+
+# --------------------------------------------------------------------------- routing oracle
+def align_ref(topk_ids, num_experts: int, block_m: int = BLOCK_M) -> dict:
+    """remote_bench.py:82-101 metadata from the flat top-k ids (numpy, int64 math, int32 out).
+
+    Ids outside [0, E) are skipped. Returns group_sizes, group_offsets, group_padded_offsets,
+    group_idx_for_bx, sorted_route_ids (pad rows = R), route_slot (-1 if skipped), padded_rows.
+    """
+    ids = np.asarray(topk_ids).reshape(-1).astype(np.int64)
+    R = ids.size
+    valid = (ids >= 0) & (ids < num_experts)
+    group_sizes = np.bincount(ids[valid], minlength=num_experts).astype(np.int64)
+    group_offsets = np.concatenate([[0], np.cumsum(group_sizes)])
+    padded = (group_sizes + block_m - 1) // block_m * block_m
+    group_padded_offsets = np.concatenate([[0], np.cumsum(padded)])
+    group_idx_for_bx = np.repeat(np.arange(num_experts), padded // block_m)
+    P = int(group_padded_offsets[-1])
+    sorted_route_ids = np.full(P, R, dtype=np.int64)
+    route_slot = np.full(R, -1, dtype=np.int64)
+    order = np.argsort(np.where(valid, ids, num_experts), kind="stable")[: int(valid.sum())]
+    rank_in_expert = np.arange(order.size) - group_offsets[ids[order]]
+    slots = group_padded_offsets[ids[order]] + rank_in_expert
+    sorted_route_ids[slots] = order
+    route_slot[order] = slots
+    i32 = lambda a: np.asarray(a, dtype=np.int32)
+    return dict(
+        group_sizes=i32(group_sizes),
+        group_offsets=i32(group_offsets),
+        group_padded_offsets=i32(group_padded_offsets),
+        group_idx_for_bx=i32(group_idx_for_bx),
+        sorted_route_ids=i32(sorted_route_ids),
+        route_slot=i32(route_slot),
+        padded_rows=P,
+    )
+
+
+# --------------------------------------------------------------------------- token-major oracle
+def fused_moe_ref(hidden_states, w_gate_up, w_down, topk_ids, topk_weights, experts=None) -> torch.Tensor:
+    """fp32 ``sum_j w[t,j] * Down_e(silu(Gate_e x_t) * Up_e x_t)``; returns fp32 [T, H].
+
+    Computed the reference's way: stack the routed rows per expert in the padded layout that
+    ``align_ref`` builds, run ``run_kernel_ref`` (fp32 result, routing weight folded in), then sum
+    each token's rows.
+    """
+    T, H = hidden_states.shape
+    E = w_gate_up.shape[0]
+    I = w_gate_up.shape[1] // 2
+    k = topk_ids.shape[1]
+    dev = hidden_states.device
+    al = align_ref(topk_ids.detach().cpu().numpy(), E)
+    P = al["padded_rows"]
+    R = T * k
+    sorted_ids = torch.from_numpy(al["sorted_route_ids"].astype(np.int64)).to(dev)
+    valid_rows = sorted_ids < R
+    stacked = torch.zeros((P, H), dtype=hidden_states.dtype, device=dev)
+    stacked[valid_rows] = hidden_states[sorted_ids[valid_rows] // k]
+    flat_w = topk_weights.reshape(-1).to(torch.float32)
+    # routed weights in "raw" (expert-grouped, unpadded) order, as group_offsets index them
+    raw_order = sorted_ids[valid_rows]
+    routed = flat_w[raw_order]
+    g = lambda a: torch.from_numpy(a).to(dev)
+    y = torch.zeros((P, H), dtype=torch.float32, device=dev)
+    run_kernel_ref(stacked, w_gate_up[:, :I], w_gate_up[:, I:], w_down, routed, g(al["group_sizes"]),
+                   g(al["group_offsets"]), g(al["group_padded_offsets"]), g(al["group_idx_for_bx"]), y,
+                   experts=experts)
+    out = torch.zeros((T, H), dtype=torch.float32, device=dev)
+    out.index_add_(0, raw_order // k, y[valid_rows])
+    return out
+
+
+# --------------------------------------------------------------------------- int8 oracle
+def quantize_rows_ref(w: torch.Tensor):
+    """amax/127 per row, round half away from zero, clamp +-127 (submission_v322_int8_v2.py:186-203)."""
+    wf = w.to(torch.float32)
+    amax = wf.abs().amax(dim=-1)
+    inv = torch.where(amax > 0, 127.0 / amax, torch.zeros_like(amax))
+    v = wf * inv.unsqueeze(-1)
+    # exact round-half-away-from-zero: v - trunc(v) is exact in fp32, so no double rounding
+    t = torch.trunc(v)
+    q = t + torch.where((v - t).abs() >= 0.5, torch.sign(v), torch.zeros_like(v))
+    q = q.clamp(-127, 127).to(torch.int8)
+    return q, amax / 127.0
+
+
+def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights,
+                       out_dtype=torch.float16) -> torch.Tensor:
+    """Exact model of the W8A8 route: per-token int8 x, per-row int8 weights, exact integer GEMMs
+    (float64 accumulation of int8 products is exact here), dequant, silu*up rounded to the output
+    dtype, per-row requantisation of the intermediate, int8 down GEMM, dequant, route weight,
+    per-token sum. Returns fp32 [T, H]."""
+    T, H = hidden_states.shape
+    E = w13_q.shape[0]
+    I = w13_q.shape[1] // 2
+    k = topk_ids.shape[1]
+    dev = hidden_states.device
+    xq, xs = quantize_rows_ref(hidden_states)
+    ids = topk_ids.reshape(-1).to(torch.int64)
+    w = topk_weights.reshape(-1).to(torch.float32)
+    out = torch.zeros((T, H), dtype=torch.float32, device=dev)
+    w13s = w13_scale.reshape(E, 2 * I).to(torch.float32)
+    w2s = w2_scale.reshape(E, H).to(torch.float32)
+    for e in range(E):
+        routes = torch.nonzero(ids == e).flatten()
+        if routes.numel() == 0:
+            continue
+        tok = routes // k
+        a = xq[tok].to(torch.float64)
+        acc = a @ w13_q[e].to(torch.float64).T  # exact int32-range sums
+        deq = acc.to(torch.float32) * xs[tok].unsqueeze(1) * w13s[e].unsqueeze(0)
+        g, u = deq[:, :I], deq[:, I:]
+        h = (g * torch.reciprocal(1.0 + torch.exp(-g)) * u).to(out_dtype)
+        hq, hs = quantize_rows_ref(h)
+        acc2 = hq.to(torch.float64) @ w2_q[e].to(torch.float64).T
+        y = acc2.to(torch.float32) * hs.unsqueeze(1) * w2s[e].unsqueeze(0)
+        out.index_add_(0, tok, y * w[routes].unsqueeze(1))
+    return out

@@ -1,0 +1,79 @@
+"""CPU: the C-ABI library loads, exports every declared symbol, and host-side checks run without a GPU."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from muxi_race_b200 import _lib
+from muxi_race_b200.workloads import CONFIGS
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "moe_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MOE_API\s+[\w\s\*]+?\b(moe_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for expected in ("moe_run_kernel", "moe_align", "moe_fused", "moe_fused_int8", "moe_quantize_rows_int8"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} declared in moe_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_pure_host_queries():
+    lib = _lib.lib()
+    assert b"sm_100a" in lib.moe_version()
+    # moe_max_padded_rows: sum_e ceil(n_e / bm) * bm <= R + min(E, R) * (bm - 1), rounded to bm
+    assert lib.moe_max_padded_rows(0, 8, 128) == 0
+    assert lib.moe_max_padded_rows(1, 8, 128) == 128
+    assert lib.moe_max_padded_rows(128, 8, 128) == 1152
+    assert lib.moe_max_padded_rows(32768, 256, 128) == 65280
+    assert lib.moe_run_kernel_workspace_bytes(256, 2048, _lib.MOE_F16) == 256 * 2048 * 2
+    assert lib.moe_fused_workspace_bytes(4096, 8, 256, 7168, 2048, _lib.MOE_F16) > 65280 * (7168 + 2048) * 2
+
+
+def test_invalid_arguments_fail_before_any_launch():
+    lib = _lib.lib()
+    # odd hidden size is rejected by the argument check (no device pointer is touched)
+    rc = lib.moe_run_kernel(*([None] * 5), _lib.MOE_F32, *([None] * 5), 128, 100, 64, 1, 1, 1, _lib.MOE_F16, None, 0,
+                            None)
+    assert rc == -1 and b"multiples of 8" in lib.moe_last_error()
+    rc = lib.moe_run_kernel(*([None] * 5), _lib.MOE_F32, *([None] * 5), 256, 128, 64, 1, 1, 1, _lib.MOE_F16, None, 0,
+                            None)
+    assert rc == -1 and b"num_blocks_m" in lib.moe_last_error()
+    rc = lib.moe_align(None, _lib.MOE_I32, 10, 2000, 128, *([None] * 7), None, 0, None)
+    assert rc == -1 and b"num_experts" in lib.moe_last_error()
+    with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
+        _lib.call("moe_fused", *([None] * 4), _lib.MOE_I8, None, _lib.MOE_F32, None, 4, 128, 128, 8, 2, _lib.MOE_F16,
+                  None, 0, None)
+
+
+def test_python_entry_points_reject_cpu_tensors():
+    from muxi_race_b200 import fused_moe, run_kernel
+
+    x = torch.zeros(128, 64, dtype=torch.float16)
+    w = torch.zeros(1, 64, 64, dtype=torch.float16)
+    meta = [torch.zeros(n, dtype=torch.int32) for n in (1, 2, 2, 1)]
+    with pytest.raises(ValueError, match="CUDA"):
+        run_kernel(x, w, w, w, torch.zeros(4), *meta, torch.zeros_like(x))
+    with pytest.raises(ValueError):
+        fused_moe(x, torch.zeros(1, 128, 64, dtype=torch.float16), w, torch.zeros(128, 1, dtype=torch.int32),
+                  torch.zeros(128, 1))
+
+
+def test_workload_algorithmic_work():
+    c = CONFIGS["cfg3"]
+    assert c.flops() == pytest.approx(2.886e12, rel=1e-3)
+    assert c.weight_bytes() == pytest.approx(22.55e9, rel=1e-3)
+    assert CONFIGS["cfg4"].weight_bytes() == pytest.approx(11.27e9, rel=1e-3)
