@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -59,7 +60,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   std::atomic<int> sms{0};
   std::atomic<uint32_t*> status{nullptr};
-  std::atomic<uint32_t> attr_done{0};  // bit per kernel whose smem attribute has been raised
+  std::atomic<uint64_t> attr_done[2] = {};  // bit per kernel whose smem attribute has been raised
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -91,10 +92,11 @@ int device_status_ptr(int dev, uint32_t** p) {
 
 template <typename K>
 int raise_smem(int dev, int bit, K kernel, int bytes) {
-  const uint32_t mask = 1u << bit;
-  if (g_dev[dev].attr_done.load(std::memory_order_acquire) & mask) return MOE_OK;
+  const uint64_t mask = uint64_t(1) << (bit & 63);
+  std::atomic<uint64_t>& word = g_dev[dev].attr_done[bit >> 6];
+  if (word.load(std::memory_order_acquire) & mask) return MOE_OK;
   MOE_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
-  g_dev[dev].attr_done.fetch_or(mask, std::memory_order_acq_rel);
+  word.fetch_or(mask, std::memory_order_acq_rel);
   return MOE_OK;
 }
 
@@ -111,7 +113,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// Row-major [rows, cols] matrix, box = box_rows x (128 bytes), 128-byte swizzle.
+// Row-major [rows, cols] matrix, box = box_rows x (128 bytes), 128-byte swizzle (matches the
+// kernels' shared-memory descriptors).
 int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, int64_t cols, int box_rows,
               const char* what) {
   auto enc = get_encode();
@@ -137,23 +140,75 @@ bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // ------------------------------------------------------------------ GEMM launch
-enum KernelBit {
-  kBitS1F16 = 0, kBitS1BF16, kBitS2PadF16, kBitS2PadBF16, kBitS2CombF16, kBitS2CombBF16,
-  kBitS1I8F16, kBitS1I8BF16, kBitS2CombI8F16, kBitS2CombI8BF16
-};
+// Tile configurations: accumulator width per block x blocks per work unit.
+//   kTile256    BN = 256, one block per unit, two accumulator slots, 4 x 48 KiB stages (default:
+//               fastest measured on cfg3, the decode-like T=128 case and the int8 route)
+//   kTile256x2  BN = 256, block groups of up to two blocks of one expert, 3 x 64 KiB stages
+//   kTile512    BN = 512, one block per unit, one slot, 2 x 80 KiB stages
+// MOE_B200_TILE = 512 | 256x2 | 256 overrides the default for experiments.
+enum TileCfg { kTile512 = 0, kTile256x2 = 1, kTile256 = 2 };
 
-template <int MODE, typename OutT, bool I8>
-int launch_gemm(int dev, int bit, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8>;
-  MOE_TRY(raise_smem(dev, bit, kern, kSmemBytes));
+TileCfg tile_cfg() {
+  static const TileCfg t = [] {
+    const char* v = getenv("MOE_B200_TILE");
+    if (v && strcmp(v, "512") == 0) return kTile512;
+    if (v && strcmp(v, "256x2") == 0) return kTile256x2;
+    return kTile256;
+  }();
+  return t;
+}
+int cfg_bn(TileCfg c) { return c == kTile512 ? 512 : 256; }
+int cfg_gmax(TileCfg c) { return c == kTile256x2 ? 2 : 1; }
+
+// How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu. Default tma: on B200 the
+// TMA tile load of pre-stacked rows measured faster than gathering token rows with cp.async inside
+// Stage1 (cfg3: 5.1 ms vs 6.4 ms per call), the stacking gather costing 0.11 ms.
+bool a_path_lsu() {
+  static const bool v = [] {
+    const char* e = getenv("MOE_B200_A_PATH");
+    return e && strcmp(e, "lsu") == 0;
+  }();
+  return v;
+}
+
+template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AMODE>
+int launch_gemm(int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
+                int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AMODE>;
+  constexpr int tcfg = BN == 512 ? 0 : (GMAX == 2 ? 1 : 2);
+  constexpr int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * 3 + tcfg) * 3 + AMODE;
+  static_assert(bit < 128, "attribute bit out of range");
+  constexpr int smem = Ring<BN, GMAX>::kSmemBytes;
+  MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
   const int grid = max_tiles < sms ? max_tiles : sms;
   if (grid <= 0) return MOE_OK;
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(a, b0, b1, args);
+  kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, args);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
+}
+
+// One grouped GEMM stage with the chosen tile configuration and A path.
+template <int MODE, typename OutT, bool I8, int AMODE>
+int launch_stage(TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                 const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  switch (c) {
+    case kTile256x2: return launch_gemm<MODE, OutT, I8, 256, 2, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
+    case kTile256: return launch_gemm<MODE, OutT, I8, 256, 1, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
+    default: return launch_gemm<MODE, OutT, I8, 512, 1, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
+  }
+}
+
+// Stage dispatch over the runtime element type and A path.
+template <int MODE, bool I8, int AMODE_TMA, int AMODE_LSU>
+int launch_stage_rt(int dtype, bool lsu, TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0,
+                    const CUtensorMap& b1, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  if (dtype == MOE_F16)
+    return lsu ? launch_stage<MODE, __half, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
+               : launch_stage<MODE, __half, I8, AMODE_TMA>(c, dev, a, b0, b1, args, max_tiles, stream);
+  return lsu ? launch_stage<MODE, __nv_bfloat16, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
+             : launch_stage<MODE, __nv_bfloat16, I8, AMODE_TMA>(c, dev, a, b0, b1, args, max_tiles, stream);
 }
 
 // ------------------------------------------------------------------ align
@@ -198,11 +253,12 @@ int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t b
 
 // Workspace carving for the token-major paths.
 struct FusedLayout {
-  size_t counts, gs, go, gpo, meta, gidx, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
+  size_t counts, gs, go, gpo, meta, gidx, groups, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
   int64_t P_max, nblk_max;
 };
 
 FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8) {
+  const bool lsu = a_path_lsu();
   FusedLayout L{};
   const int64_t R = T * topk;
   L.P_max = moe_max_padded_rows(R, E, kBM);
@@ -219,10 +275,14 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.gpo = take(sizeof(int) * (E + 1));
   L.meta = take(sizeof(int) * 4);
   L.gidx = take(sizeof(int) * (size_t)L.nblk_max);
+  L.groups = take(sizeof(int) * (size_t)(L.nblk_max + 1));  // block groups + their count
   L.sorted = take(sizeof(int) * (size_t)L.P_max);
   L.slot = take(sizeof(int) * (size_t)R);
-  L.xs = take((int8 ? 1 : 2) * (size_t)L.P_max * H);
-  L.xscale = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
+  // activations: LSU path gathers token rows in the GEMM (int8: tokens quantised in place first);
+  // TMA path stacks gathered rows first
+  const size_t a_rows = lsu ? (size_t)T : (size_t)L.P_max;
+  L.xs = take(lsu ? (int8 ? a_rows * H : 0) : (int8 ? 1 : 2) * a_rows * H);
+  L.xscale = take(int8 ? sizeof(float) * a_rows : 0);
   L.u = take(2 * (size_t)L.P_max * I);
   L.uq = take(int8 ? (size_t)L.P_max * I : 0);
   L.uscale = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
@@ -276,10 +336,13 @@ int moe_device_status(void* stream, int clear, uint32_t* status_out) {
 }
 
 // ---------------------------------------------------------------------------- run_kernel
+// Workspace: U [P, I] (the reference's cached up_logits) + block groups [P/128] + group count.
+static size_t run_kernel_u_bytes(int64_t P, int64_t I) { return round_up(static_cast<size_t>(P) * I * 2, 256); }
+
 size_t moe_run_kernel_workspace_bytes(int64_t P, int64_t I, int dtype) {
   (void)dtype;
   if (P <= 0 || I <= 0) return 0;
-  return round_up(static_cast<size_t>(P) * I * 2, 256);
+  return run_kernel_u_bytes(P, I) + round_up(sizeof(int32_t) * static_cast<size_t>(P / kBM + 1), 256);
 }
 
 int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const void* down_w, const void* routed,
@@ -306,42 +369,53 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
     return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
   if (!workspace || workspace_bytes < moe_run_kernel_workspace_bytes(P, I, dtype))
     return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", moe_run_kernel_workspace_bytes(P, I, dtype));
-  if (!aligned16(workspace)) return fail(MOE_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0)
+    return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
   if (E * I > (int64_t(1) << 31) - 1 || E * H > (int64_t(1) << 31) - 1)
     return fail(MOE_ERR_INVALID_ARG, "experts x rows exceeds the TMA coordinate range");
   int dev;
   MOE_TRY(current_device(&dev));
   uint32_t* status;
   MOE_TRY(device_status_ptr(dev, &status));
+  void* U = workspace;
+  int32_t* groups = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + run_kernel_u_bytes(P, I));
+  int32_t* ngroups = groups + nblk;
+  const TileCfg tc = tile_cfg();
+  const int bn = cfg_bn(tc), gmax = cfg_gmax(tc);
 
   CUtensorMap tA, tG, tU, tUA, tD;
   MOE_TRY(make_tmap(&tA, x, 2, P, H, kBM, "stacked_expert_tokens"));
-  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, kBN / 2, "gate_w"));
-  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, kBN / 2, "up_w"));
-  MOE_TRY(make_tmap(&tUA, workspace, 2, P, I, kBM, "workspace"));
-  MOE_TRY(make_tmap(&tD, down_w, 2, E * H, I, kBN, "down_w"));
+  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, bn / 2, "gate_w"));
+  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, bn / 2, "up_w"));
+  MOE_TRY(make_tmap(&tUA, U, 2, P, I, kBM, "workspace"));
+  MOE_TRY(make_tmap(&tD, down_w, 2, E * H, I, kMmaN, "down_w"));
+
+  if (gmax > 1) {  // pair each expert's blocks (from group_padded_offsets)
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, gmax, groups, ngroups);
+    MOE_CUDA(cudaGetLastError());
+  }
 
   GemmArgs a1{};
   a1.K = (int)H;
   a1.N = (int)I;
-  a1.n_tiles = (int)((I + kBN / 2 - 1) / (kBN / 2));
-  a1.nblk = (int)nblk;
+  a1.n_tiles = (int)((I + bn / 2 - 1) / (bn / 2));
+  a1.ngroups = gmax > 1 ? -1 : (int)nblk;
+  a1.ngroups_dev = ngroups;
+  a1.groups = gmax > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
   a1.b_rows_per_expert = (int)I;
   a1.b1_row_offset = 0;
-  a1.U = workspace;
+  a1.U = U;
   a1.ldu = (int)I;
   a1.status = status;
 
-  GemmArgs a2{};
+  GemmArgs a2 = a1;
   a2.K = (int)I;
   a2.N = (int)H;
-  a2.n_tiles = (int)((H + kBN - 1) / kBN);
-  a2.nblk = (int)nblk;
-  a2.E = (int)E;
-  a2.block_expert = gidx;
+  a2.n_tiles = (int)((H + bn - 1) / bn);
   a2.b_rows_per_expert = (int)H;
+  a2.U = nullptr;
   a2.out = out;
   a2.ldo = (int)H;
   a2.group_sizes = gs;
@@ -350,16 +424,15 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a2.routed = routed;
   a2.routed_dtype = routed_dtype == MOE_F32 ? 0 : 1;
   a2.R = (int)R;
-  a2.status = status;
 
+  const bool lsu = a_path_lsu();
+  a1.a_ptr = x;
+  a1.a_row_bytes = H * 2;
+  a2.a_ptr = U;
+  a2.a_row_bytes = I * 2;
   const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
-  if (dtype == MOE_F16) {
-    MOE_TRY((launch_gemm<kStage1, __half, false>(dev, kBitS1F16, tA, tG, tU, a1, tiles1, s)));
-    MOE_TRY((launch_gemm<kStage2Pad, __half, false>(dev, kBitS2PadF16, tUA, tD, tD, a2, tiles2, s)));
-  } else {
-    MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, false>(dev, kBitS1BF16, tA, tG, tU, a1, tiles1, s)));
-    MOE_TRY((launch_gemm<kStage2Pad, __nv_bfloat16, false>(dev, kBitS2PadBF16, tUA, tD, tD, a2, tiles2, s)));
-  }
+  MOE_TRY((launch_stage_rt<kStage1, false, kATma, kALsu>(dtype, lsu, tc, dev, tA, tG, tU, a1, tiles1, s)));
+  MOE_TRY((launch_stage_rt<kStage2Pad, false, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tD, tD, a2, tiles2, s)));
   return MOE_OK;
 }
 
@@ -439,18 +512,40 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   int32_t* slot = reinterpret_cast<int32_t*>(ws + L.slot);
   void* xs = ws + L.xs;
   void* U = ws + L.u;
+  int32_t* groups = reinterpret_cast<int32_t*>(ws + L.groups);
+  int32_t* ngroups = groups + L.nblk_max;
+  const TileCfg tc = tile_cfg();
+  const int bn = cfg_bn(tc), gmax = cfg_gmax(tc);
 
   // 1. routing metadata
   prof_record(0, s);
   MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s));
+  if (gmax > 1) {
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, gmax, groups, ngroups);
+    MOE_CUDA(cudaGetLastError());
+  }
   prof_record(1, s);
 
-  // 2. gather token rows into the expert-grouped layout (+ per-token int8 quantisation),
-  //    zero the output the Stage2 epilogue accumulates into
+  // 2. activations: the LSU path reads token rows straight from hidden_states inside Stage1
+  //    (int8: after a per-token quantisation); the TMA path stacks the gathered rows first and
+  //    zeroes the combine target (the LSU path zeroes it in Stage1's epilogue warps)
+  const bool lsu = a_path_lsu();
   const int gblocks = sms * 4;
   float* amax = int8 ? reinterpret_cast<float*>(ws + L.amax) : nullptr;
   float* xscale = int8 ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
-  if (dtype == MOE_F16) {
+  if (lsu) {
+    if (int8) {
+      if (dtype == MOE_F16)
+        quantize_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), T, (int)H, nullptr,
+                                                                nullptr, static_cast<int8_t*>(xs), xscale);
+      else
+        quantize_rows_q8_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T,
+                                                                       (int)H, nullptr, nullptr,
+                                                                       static_cast<int8_t*>(xs), xscale);
+      MOE_CUDA(cudaGetLastError());
+      MOE_CUDA(cudaMemsetAsync(amax, 0, sizeof(float) * (size_t)L.P_max, s));
+    }
+  } else if (dtype == MOE_F16) {
     if (int8)
       gather_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
                                                             (int)H, static_cast<int8_t*>(xs), xscale,
@@ -459,6 +554,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       gather_rows_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
                                                          (int)H, static_cast<__half*>(xs), static_cast<__half*>(out),
                                                          (int)T, nullptr, 0);
+    MOE_CUDA(cudaGetLastError());
   } else {
     if (int8)
       gather_rows_q8_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
@@ -468,24 +564,32 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       gather_rows_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<__nv_bfloat16*>(xs),
           static_cast<__nv_bfloat16*>(out), (int)T, nullptr, 0);
+    MOE_CUDA(cudaGetLastError());
   }
-  MOE_CUDA(cudaGetLastError());
   prof_record(2, s);
 
   // 3. Stage1 (gate/up GEMM + SiLU*up) and 4. Stage2 (down GEMM * topk weight, combine)
   const int elt = int8 ? 1 : 2;
+  const void* a1_src = lsu ? (int8 ? static_cast<const void*>(xs) : x) : xs;
+  void* a2_src = int8 ? (void*)(ws + L.uq) : U;
   CUtensorMap tA, tW13, tUA, tW2;
-  MOE_TRY(make_tmap(&tA, xs, elt, L.P_max, H, kBM, "gathered hidden_states"));
-  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, kBN / 2, "w_gate_up"));
-  MOE_TRY(make_tmap(&tUA, int8 ? (void*)(ws + L.uq) : U, elt, L.P_max, I, kBM, "intermediate"));
-  MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kBN, "w_down"));
+  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, bn / 2, "w_gate_up"));
+  MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kMmaN, "w_down"));
+  if (lsu) {
+    tA = tW13;  // unused by the LSU A path
+    tUA = tW2;
+  } else {
+    MOE_TRY(make_tmap(&tA, xs, elt, L.P_max, H, kBM, "gathered hidden_states"));
+    MOE_TRY(make_tmap(&tUA, a2_src, elt, L.P_max, I, kBM, "intermediate"));
+  }
 
   GemmArgs a1{};
   a1.K = (int)H;
   a1.N = (int)I;
-  a1.n_tiles = (int)((I + kBN / 2 - 1) / (kBN / 2));
-  a1.nblk = -1;
-  a1.nblk_dev = meta + 1;
+  a1.n_tiles = (int)((I + bn / 2 - 1) / (bn / 2));
+  a1.ngroups = -1;
+  a1.ngroups_dev = gmax > 1 ? ngroups : meta + 1;
+  a1.groups = gmax > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
   a1.b_rows_per_expert = (int)(2 * I);
@@ -497,13 +601,21 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a1.b1_scale = w13_scale;
   a1.row_amax = amax;
   a1.status = status;
+  a1.a_ptr = a1_src;
+  a1.a_row_bytes = H * elt;
+  a1.sorted_route_ids = sorted;
+  a1.R = (int)R;
+  a1.topk = (int)topk;
+  a1.zero_ptr = lsu ? out : nullptr;
+  a1.zero_bytes = lsu ? T * H * 2 : 0;
 
   GemmArgs a2{};
   a2.K = (int)I;
   a2.N = (int)H;
-  a2.n_tiles = (int)((H + kBN - 1) / kBN);
-  a2.nblk = -1;
-  a2.nblk_dev = meta + 1;
+  a2.n_tiles = (int)((H + bn - 1) / bn);
+  a2.ngroups = -1;
+  a2.ngroups_dev = gmax > 1 ? ngroups : meta + 1;
+  a2.groups = gmax > 1 ? groups : nullptr;
   a2.E = (int)E;
   a2.block_expert = gidx;
   a2.b_rows_per_expert = (int)H;
@@ -517,25 +629,18 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a2.a_scale = int8 ? reinterpret_cast<const float*>(ws + L.uscale) : nullptr;
   a2.b0_scale = w2_scale;
   a2.status = status;
+  a2.a_ptr = a2_src;
+  a2.a_row_bytes = I * elt;
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
-    if (dtype == MOE_F16) {
-      MOE_TRY((launch_gemm<kStage1, __half, false>(dev, kBitS1F16, tA, tW13, tW13, a1, max_tiles1, s)));
-      prof_record(3, s);
-      MOE_TRY((launch_gemm<kStage2Comb, __half, false>(dev, kBitS2CombF16, tUA, tW2, tW2, a2, max_tiles2, s)));
-    } else {
-      MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, false>(dev, kBitS1BF16, tA, tW13, tW13, a1, max_tiles1, s)));
-      prof_record(3, s);
-      MOE_TRY((launch_gemm<kStage2Comb, __nv_bfloat16, false>(dev, kBitS2CombBF16, tUA, tW2, tW2, a2, max_tiles2, s)));
-    }
+    MOE_TRY((launch_stage_rt<kStage1, false, kATma, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    prof_record(3, s);
+    MOE_TRY((launch_stage_rt<kStage2Comb, false, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(4, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
-    if (dtype == MOE_F16)
-      MOE_TRY((launch_gemm<kStage1, __half, true>(dev, kBitS1I8F16, tA, tW13, tW13, a1, max_tiles1, s)));
-    else
-      MOE_TRY((launch_gemm<kStage1, __nv_bfloat16, true>(dev, kBitS1I8BF16, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, true, kATma, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
     prof_record(3, s);
     if (dtype == MOE_F16)
       quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
@@ -547,10 +652,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
           reinterpret_cast<float*>(ws + L.uscale));
     MOE_CUDA(cudaGetLastError());
     prof_record(4, s);
-    if (dtype == MOE_F16)
-      MOE_TRY((launch_gemm<kStage2Comb, __half, true>(dev, kBitS2CombI8F16, tUA, tW2, tW2, a2, max_tiles2, s)));
-    else
-      MOE_TRY((launch_gemm<kStage2Comb, __nv_bfloat16, true>(dev, kBitS2CombI8BF16, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, true, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(5, s);
   }
   return MOE_OK;

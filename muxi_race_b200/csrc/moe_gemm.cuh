@@ -4,17 +4,25 @@
 // One CTA per SM (192 threads):
 //   warp 0      TMA producer: streams A (token rows) and B (expert weight rows) k-blocks into a
 //               STAGES-deep ring of 128B-swizzled shared-memory buffers;
-//   warp 1      owns TMEM (512 columns = two 128x256 fp32/int32 accumulators) and one lane issues
-//               tcgen05.mma for each k-block, committing to the ring's "empty" barriers;
-//   warps 2..5  epilogue: tcgen05.ld the finished accumulator (warp w reads TMEM lanes
+//   warp 1      owns TMEM (512 columns = two 128 x 256 fp32/int32 accumulator slots); one lane
+//               issues tcgen05.mma for each k-block and commits to the ring's "empty" barriers;
+//   warps 2..5  epilogue: tcgen05.ld a finished accumulator (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), apply the fused epilogue, store to global, and hand
-//               the accumulator back, so the epilogue of tile i overlaps the main loop of tile i+1.
+//               the slot back, so epilogues overlap the main loop of the next tile.
 //
-// Tiles are 128 rows (one routing block = one expert) x 256 accumulator columns, k-blocks are
-// 128 bytes wide (64 fp16/bf16 or 128 int8 elements), four MMAs of K = 128 bytes / 4 each.
-// Tile t covers routing block t / n_tiles and column tile t % n_tiles: all column tiles of a block
-// run back to back (the A block is re-read from L2) and the blocks of one expert are adjacent
-// (its weight tile is re-read from L2, not HBM).
+// Work unit = (block group, column tile). A block group is up to GMAX consecutive 128-row
+// routing blocks of ONE expert: every k-block of the expert's weight tile is loaded once and
+// multiplied against all the group's A blocks (one accumulator slot per block), so an expert
+// with 129..256 routed rows streams its weights through L2 -> SM once instead of twice. On B200
+// the bound for these weight-streaming GEMMs is the L2 -> SM intake, so bytes moved per output
+// are what the tiling minimises. Column tiles of one group run back to back (the group's A rows
+// are re-read from L2, not HBM).
+//
+// Tiles: 128 rows per block x BN accumulator columns (BN = 256: two accumulator slots, so an
+// epilogue overlaps the next tile's main loop, or one block group of two blocks; BN = 512: one
+// slot, two N = 256 MMAs per k-step sharing the A block). k-blocks are 128 bytes wide (64
+// fp16/bf16 or 128 int8 elements, 128-byte swizzle): measured on B200, halving the k-block width
+// (more, smaller TMA requests for the same bytes in flight) costs 20% or more.
 //
 // Modes (the epilogue is the only difference):
 //   kStage1     D = [gate | up] halves of 128 columns each; U = silu(gate) * up, stored to the
@@ -33,27 +41,35 @@
 
 namespace moe {
 
-constexpr int kBM = 128;           // rows per tile = routing block size
-constexpr int kBN = 256;           // accumulator columns per tile (MMA N)
-constexpr int kKBytes = 128;       // k-block width in bytes (one 128B swizzle atom)
-constexpr int kStages = 4;         // smem ring depth
-constexpr int kThreads = 192;      // 6 warps
-constexpr int kABytes = kBM * kKBytes;        // 16 KiB
-constexpr int kBBytes = kBN * kKBytes;        // 32 KiB
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kTmemCols = 2 * kBN;            // double-buffered accumulator
-constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+constexpr int kBM = 128;       // rows per block = routing block size
+constexpr int kMmaN = 256;     // N of one tcgen05.mma
+constexpr int kKBytes = 128;   // k-block width in bytes (one 128B swizzle atom)
+constexpr int kThreads = 192;  // 6 warps
+constexpr int kABytes = kBM * kKBytes;  // 16 KiB per A block per stage
+constexpr int kTmemCols = 512;
+constexpr int kRingBudget = 200 * 1024;
+
+template <int BN, int GMAX> struct Ring {
+  static_assert(BN == 256 || BN == 512, "accumulator width");
+  static_assert(GMAX >= 1 && GMAX * BN <= kTmemCols, "a block group must fit in TMEM");
+  static constexpr int kBBytes = BN * kKBytes;
+  static constexpr int kStageBytes = GMAX * kABytes + kBBytes;  // A blocks then B
+  static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
+  static constexpr int kSlots = kTmemCols / BN;                 // accumulator slots
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+};
 
 enum GemmMode : int { kStage1 = 0, kStage2Pad = 1, kStage2Comb = 2 };
 
 struct GemmArgs {
   int K;                      // reduction length in elements
   int N;                      // valid output columns per expert (I for Stage1, H for Stage2)
-  int n_tiles;                // column tiles per block
-  int nblk;                   // routing blocks, or -1: read *nblk_dev (device-resident count)
-  const int* nblk_dev;
+  int n_tiles;                // column tiles per block group
+  int ngroups;                // block groups, or -1: read *ngroups_dev (device-resident count)
+  const int* ngroups_dev;
+  const int* groups;          // [ngroups] first_block * 2 + (blocks - 1); NULL: group g = block g
   int E;
-  const int* block_expert;    // [nblk] expert of each 128-row block (group_idx_for_bx)
+  const int* block_expert;    // expert of each 128-row block (group_idx_for_bx)
   int b_rows_per_expert;      // rows of one expert in the B tensor map(s)
   int b1_row_offset;          // Stage1: row offset of the "up" half inside one expert of map B1
 
@@ -64,7 +80,7 @@ struct GemmArgs {
   // Stage2 output: out [rows or tokens, ldo]
   void* out;
   int ldo;
-  // Stage2Pad: reference metadata and routed weights (fp32 or 16-bit)
+  // Stage2Pad: reference metadata and routed weights
   const int* group_sizes;
   const int* group_offsets;
   const int* group_padded_offsets;
@@ -81,8 +97,33 @@ struct GemmArgs {
   const float* b1_scale;      // [E * b_rows_per_expert] (up rows, Stage1)
   float* row_amax;            // Stage1 int8: per-row amax of U (for requantisation), may be null
 
+  // A operand through the LSU path (AMODE 1 / 2): row-major rows of a_row_bytes bytes
+  const void* a_ptr;
+  long long a_row_bytes;
+  // Stage1 only: the epilogue warps zero this buffer first (the Stage2 combine target)
+  void* zero_ptr;
+  long long zero_bytes;
+
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
+
+// How the A operand reaches shared memory:
+//   kATma     one TMA box per block (rows = padded rows of the A tensor map)
+//   kALsu     cp.async by the producer warp, row p of a_ptr (identity)
+//   kAGather  cp.async by the producer warp, row sorted_route_ids[p] / topk of a_ptr (the token
+//             row of each routed row: the gathered-row load, no stacked copy of the tokens);
+//             padding rows are zero-filled
+enum AMode : int { kATma = 0, kALsu = 1, kAGather = 2 };
+
+// Source row of padded row p for the A operand, -1 for padding.
+template <int AMODE>
+__device__ __forceinline__ long long a_source_row(const GemmArgs& args, int p) {
+  if (AMODE == kAGather) {
+    const int route = args.sorted_route_ids[p];
+    return (route >= 0 && route < args.R) ? static_cast<long long>(route / args.topk) : -1;
+  }
+  return p;
+}
 
 // ------------------------------------------------------------------ element helpers
 template <typename T> struct Elt;
@@ -121,33 +162,174 @@ __device__ __forceinline__ float load_weight(const void* w, int dtype, int i) {
 // silu(g) * u = g / (1 + e^-g) * u; the exponential is CUDA's __expf.
 __device__ __forceinline__ float silu_mul(float g, float u) { return g * __frcp_rn(1.0f + __expf(-g)) * u; }
 
+// Work unit decode: first block, block count, column tile and expert of tile `tile`.
+template <int GMAX>
+__device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& fb, int& nb, int& nt, int& e) {
+  const int g = tile / args.n_tiles;
+  nt = tile - g * args.n_tiles;
+  if (GMAX == 1 || args.groups == nullptr) {
+    fb = g;
+    nb = 1;
+  } else {
+    const int pk = args.groups[g];
+    fb = pk >> 1;
+    nb = (pk & 1) + 1;
+  }
+  e = args.block_expert[fb];
+  return e >= 0 && e < args.E;
+}
+
+// ------------------------------------------------------------------ epilogue of one block
+template <int MODE, typename OutT, bool IS_I8, int BN, int AMODE>
+__device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_row, int mb, int nt, int e,
+                                               int row_in_tile) {
+  const int p = mb * kBM + row_in_tile;  // padded row of this thread
+  if (MODE == kStage1) {
+    OutT* U = reinterpret_cast<OutT*>(args.U);
+    const int n0 = nt * (BN / 2);
+    float sa = 1.0f;
+    if (IS_I8) {
+      const long long src = a_source_row<AMODE>(args, p);
+      sa = src >= 0 ? args.a_scale[src] : 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < BN / 2; c += 32) {
+      const int col0 = n0 + c;
+      if (col0 >= args.N) break;
+      uint32_t g[32], u[32];
+      tmem_ld_32x32b_x32(t_row + c, g);
+      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+      tmem_ld_wait();
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        float g0, g1, u0, u1;
+        if (IS_I8) {
+          const int cc = min(col0 + j, args.N - 2);
+          const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
+          g0 = static_cast<float>(static_cast<int>(g[j])) * sa * args.b0_scale[wrow + cc];
+          g1 = static_cast<float>(static_cast<int>(g[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
+          u0 = static_cast<float>(static_cast<int>(u[j])) * sa * args.b1_scale[wrow + args.b1_row_offset + cc];
+          u1 = static_cast<float>(static_cast<int>(u[j + 1])) * sa * args.b1_scale[wrow + args.b1_row_offset + cc + 1];
+        } else {
+          g0 = __uint_as_float(g[j]);
+          g1 = __uint_as_float(g[j + 1]);
+          u0 = __uint_as_float(u[j]);
+          u1 = __uint_as_float(u[j + 1]);
+        }
+        const float h0 = silu_mul(g0, u0), h1 = silu_mul(g1, u1);
+        if (IS_I8 && col0 + j < args.N) amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
+        packed[j / 2] = Elt<OutT>::pack2(h0, h1);
+      }
+      OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        if (col0 + v * 8 < args.N)
+          *reinterpret_cast<uint4*>(dst + v * 8) =
+              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      }
+    }
+    if (IS_I8 && args.row_amax) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
+  } else {
+    const int n0 = nt * BN;
+    float scale = 0.0f;
+    bool valid = false;
+    int token = 0;
+    if (MODE == kStage2Pad) {
+      const int local = p - args.group_padded_offsets[e];
+      valid = local >= 0 && local < args.group_sizes[e];
+      if (valid) {
+        int route = args.group_offsets[e] + local;
+        route = max(0, min(route, args.R - 1));  // reference clamp (SUB/submission.py:935-947)
+        scale = load_weight(args.routed, args.routed_dtype, route);
+      }
+    } else {
+      const int route = args.sorted_route_ids[p];
+      valid = route >= 0 && route < args.R;
+      if (valid) {
+        token = route / args.topk;
+        scale = load_weight(args.routed, args.routed_dtype, route);
+      }
+    }
+    float sa = 1.0f;
+    if (IS_I8) sa = args.a_scale[p];
+    OutT* out = reinterpret_cast<OutT*>(args.out);
+    const size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      const int col0 = n0 + c;
+      if (col0 >= args.N) break;
+      uint32_t d[32];
+      tmem_ld_32x32b_x32(t_row + c, d);
+      tmem_ld_wait();
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        float d0, d1;
+        if (IS_I8) {
+          const int cc = min(col0 + j, args.N - 2);
+          const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
+          d0 = static_cast<float>(static_cast<int>(d[j])) * sa * args.b0_scale[wrow + cc];
+          d1 = static_cast<float>(static_cast<int>(d[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
+        } else {
+          d0 = __uint_as_float(d[j]);
+          d1 = __uint_as_float(d[j + 1]);
+        }
+        packed[j / 2] = valid ? Elt<OutT>::pack2(d0 * scale, d1 * scale) : 0u;
+      }
+      if (MODE == kStage2Pad) {
+        OutT* dst = out + orow * args.ldo + col0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          if (col0 + v * 8 < args.N)
+            *reinterpret_cast<uint4*>(dst + v * 8) =
+                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      } else if (valid) {
+        OutT* dst = out + orow * args.ldo + col0;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          if (col0 + v * 8 < args.N)
+            red_add_v4(dst + v * 8, make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]));
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the kernel
-template <int MODE, typename OutT, bool IS_I8>
+template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
+  using RingT = Ring<BN, GMAX>;
+  constexpr int kStages = RingT::kStages;
+  constexpr int kStageBytes = RingT::kStageBytes;
+  constexpr int kBBytes = RingT::kBBytes;
+  constexpr int kSlots = RingT::kSlots;
+  constexpr int kHalves = BN / kMmaN;  // MMAs per k-step per block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* smA = smem;
-  uint8_t* smB = smem + kStages * kABytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* full_bar = bars;                      // [kStages]
-  uint64_t* empty_bar = bars + kStages;           // [kStages]
-  uint64_t* tfull_bar = bars + 2 * kStages;       // [2]
-  uint64_t* tempty_bar = bars + 2 * kStages + 2;  // [2]
-  uint64_t* drain_bar = bars + 2 * kStages + 4;   // [1] MMA warp: all issued MMAs retired
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  uint64_t* full_bar = bars;                                // [kStages]
+  uint64_t* empty_bar = bars + kStages;                     // [kStages]
+  uint64_t* tfull_bar = bars + 2 * kStages;                 // [kSlots] per accumulator slot
+  uint64_t* tempty_bar = bars + 2 * kStages + kSlots;       // [kSlots]
+  uint64_t* drain_bar = bars + 2 * kStages + 2 * kSlots;    // [1] MMA warp: all issued MMAs retired
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  auto stage_a = [&](int s, int j) { return smem + s * kStageBytes + j * kABytes; };
+  auto stage_b = [&](int s) { return smem + s * kStageBytes + GMAX * kABytes; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
+      // TMA A: lane 0's expect_tx arrive; LSU A: plus one arrive per producer lane
+      mbar_init(&full_bar[s], AMODE == kATma ? 1 : 33);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kSlots; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 4);  // one arrive per epilogue warp
     }
@@ -156,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
+    if (AMODE == kATma) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB0);
     if (MODE == kStage1) tma_prefetch_desc(&tmB1);
   }
@@ -169,59 +351,103 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int nblk = args.nblk >= 0 ? args.nblk : *args.nblk_dev;
-  const int num_tiles = nblk * args.n_tiles;
+  const int ngroups = args.ngroups >= 0 ? args.ngroups : *args.ngroups_dev;
+  const int num_tiles = ngroups * args.n_tiles;
   const int num_kb = (args.K * (IS_I8 ? 1 : 2) + kKBytes - 1) / kKBytes;
   constexpr int kKElems = IS_I8 ? kKBytes : kKBytes / 2;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
-    if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_last();    // token rows: re-read by every column tile
-      const uint64_t pol_b = l2_policy_evict_normal();  // weights: re-read by the expert's other blocks
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      int issued_parity[kStages];  // parity of the last load issued into each stage, -1 = none
+    // ---------------------------------------------------------------- producer
+    // Lane 0 issues the TMA loads (B always, A with kATma); with an LSU A path all 32 lanes
+    // gather the A rows with cp.async, 16 bytes at a time, into the 128B-swizzled layout.
+    const uint64_t pol_a = l2_policy_evict_last();  // token rows: re-read by every column tile
+    const uint64_t pol_b = l2_policy_evict_normal();
+    const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int issued_parity[kStages];  // parity of the last load issued into each stage, -1 = none
 #pragma unroll
-      for (int s = 0; s < kStages; ++s) issued_parity[s] = -1;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile / args.n_tiles;
-        const int nt = tile - mb * args.n_tiles;
-        const int e = args.block_expert[mb];
-        if (e < 0 || e >= args.E) continue;
-        const int arow = mb * kBM;
-        int brow0, brow1;
-        if (MODE == kStage1) {
-          brow0 = e * args.b_rows_per_expert + nt * (kBN / 2);
-          brow1 = e * args.b_rows_per_expert + args.b1_row_offset + nt * (kBN / 2);
-        } else {
-          brow0 = e * args.b_rows_per_expert + nt * kBN;
-          brow1 = 0;
+    for (int s = 0; s < kStages; ++s) issued_parity[s] = -1;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int fb, nb, nt, e;
+      if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+      int brow0, brow1 = 0;
+      if (MODE == kStage1) {
+        brow0 = e * args.b_rows_per_expert + nt * (BN / 2);
+        brow1 = e * args.b_rows_per_expert + args.b1_row_offset + nt * (BN / 2);
+      } else {
+        brow0 = e * args.b_rows_per_expert + nt * BN;
+      }
+      // this lane's A rows (lane + 32 i of each block) as byte pointers, null = zero fill
+      const char* arow[GMAX][4];
+      if (AMODE != kATma) {
+#pragma unroll
+        for (int j = 0; j < GMAX; ++j)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            arow[j][i] = nullptr;
+            if (j < nb) {
+              const long long src = a_source_row<AMODE>(args, (fb + j) * kBM + lane + 32 * i);
+              if (src >= 0) arow[j][i] = static_cast<const char*>(args.a_ptr) + src * args.a_row_bytes;
+            }
+          }
+      }
+      const uint32_t tx = static_cast<uint32_t>((AMODE == kATma ? nb * kABytes : 0) + kBBytes);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status)) {
+          ok = false;
+          break;
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status)) {
-            ok = false;
-            break;
+        const int kx = kb * kKElems;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&full_bar[stage], tx);
+          if (AMODE == kATma)
+            for (int j = 0; j < nb; ++j)
+              tma_load_2d(stage_a(stage, j), &tmA, &full_bar[stage], kx, (fb + j) * kBM, pol_a);
+          if (MODE == kStage1) {  // gate rows, then up rows: BN/2 each
+            tma_load_2d(stage_b(stage), &tmB0, &full_bar[stage], kx, brow0, pol_b);
+            tma_load_2d(stage_b(stage) + kBBytes / 2, &tmB1, &full_bar[stage], kx, brow1, pol_b);
+          } else {  // BN rows as boxes of 256
+#pragma unroll
+            for (int h = 0; h < kHalves; ++h)
+              tma_load_2d(stage_b(stage) + h * (kMmaN * kKBytes), &tmB0, &full_bar[stage], kx, brow0 + h * kMmaN,
+                          pol_b);
           }
-          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
-          const int kx = kb * kKElems;
-          tma_load_2d(smA + stage * kABytes, &tmA, &full_bar[stage], kx, arow, pol_a);
-          if (MODE == kStage1) {
-            tma_load_2d(smB + stage * kBBytes, &tmB0, &full_bar[stage], kx, brow0, pol_b);
-            tma_load_2d(smB + stage * kBBytes + kBBytes / 2, &tmB1, &full_bar[stage], kx, brow1, pol_b);
-          } else {
-            tma_load_2d(smB + stage * kBBytes, &tmB0, &full_bar[stage], kx, brow0, pol_b);
+        }
+        if (AMODE != kATma) {
+          const long long kbyte0 = static_cast<long long>(kb) * kKBytes;
+#pragma unroll
+          for (int j = 0; j < GMAX; ++j) {
+            if (j >= nb) break;
+            const uint32_t dst0 = smem_u32(stage_a(stage, j));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = lane + 32 * i;
+              const char* src = arow[j][i];
+#pragma unroll
+              for (int c = 0; c < kKBytes / 16; ++c) {
+                const long long kbyte = kbyte0 + c * 16;
+                const bool in = src != nullptr && kbyte < a_k_bytes;
+                // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
+                cp_async_16(dst0 + r * kKBytes + ((c ^ (r & 7)) << 4), in ? src + kbyte : args.a_ptr, in ? 16u : 0u);
+              }
+            }
           }
-          issued_parity[stage] = static_cast<int>(phase);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          cp_async_mbar_arrive(&full_bar[stage]);
+          mbar_arrive(&full_bar[stage]);
+        }
+        issued_parity[stage] = static_cast<int>(phase);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
-      // Drain: every load this thread issued must have landed before the CTA may exit. On the
-      // normal path these phases completed long ago; after an abort this bounds the wait.
+    }
+    // Drain: every copy this warp issued must have landed before the CTA may exit. On the
+    // normal path these phases completed long ago; after an abort this bounds the wait.
+    if (AMODE != kATma) cp_async_wait_all();
+    if (lane == 0) {
 #pragma unroll
       for (int s = 0; s < kStages; ++s)
         if (issued_parity[s] >= 0) mbar_wait_drain(&full_bar[s], static_cast<uint32_t>(issued_parity[s]));
@@ -229,35 +455,52 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kBN) : idesc_f16(Elt<OutT>::kBF16, kBM, kBN);
+      const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kMmaN) : idesc_f16(Elt<OutT>::kBF16, kBM, kMmaN);
       int stage = 0;
       uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      uint32_t slot_cnt = 0;  // accumulator slots handed out so far (slot = cnt % kSlots)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int mb = tile / args.n_tiles;
-        const int e = args.block_expert[mb];
-        if (e < 0 || e >= args.E) continue;
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, args.status)) break;
+        int fb, nb, nt, e;
+        if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        uint32_t d_tmem[GMAX];
+        int slot[GMAX];
+#pragma unroll
+        for (int j = 0; j < GMAX; ++j) {
+          if (j >= nb || !ok) break;
+          slot[j] = static_cast<int>(slot_cnt % kSlots);
+          const uint32_t use = slot_cnt / kSlots;  // times this slot was used before
+          if (!mbar_wait(&tempty_bar[slot[j]], (use & 1u) ^ 1u, abort_flag, args.status)) ok = false;
+          d_tmem[j] = tmem_base + static_cast<uint32_t>(slot[j] * BN);
+          ++slot_cnt;
+        }
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smA + stage * kABytes);
-          const uint32_t b_addr = smem_u32(smB + stage * kBBytes);
+          if (AMODE != kATma) fence_proxy_async_smem();  // A arrived through the generic proxy
+          const uint32_t b_addr = smem_u32(stage_b(stage));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
-            const uint64_t bd = smem_desc_sw128(b_addr + k * 32);
-            if (IS_I8)
-              mma_i8(d_tmem, ad, bd, idesc, (kb | k) != 0);
-            else
-              mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          for (int j = 0; j < GMAX; ++j) {
+            if (j >= nb) break;
+            const uint32_t a_addr = smem_u32(stage_a(stage, j));
+#pragma unroll
+            for (int k = 0; k < kKBytes / 32; ++k) {
+              const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
+#pragma unroll
+              for (int h = 0; h < kHalves; ++h) {
+                const uint64_t bd = smem_desc_sw128(b_addr + h * (kMmaN * kKBytes) + k * 32);
+                const uint32_t d = d_tmem[j] + static_cast<uint32_t>(h * kMmaN);
+                if (IS_I8)
+                  mma_i8(d, ad, bd, idesc, (kb | k) != 0);
+                else
+                  mma_f16(d, ad, bd, idesc, (kb | k) != 0);
+              }
+            }
           }
           tc_commit(&empty_bar[stage]);  // frees this smem stage once the MMAs have read it
           if (++stage == kStages) {
@@ -266,11 +509,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        tc_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
-        if (++acc == 2) {
-          acc = 0;
-          acc_phase ^= 1u;
-        }
+#pragma unroll
+        for (int j = 0; j < GMAX; ++j)
+          if (j < nb) tc_commit(&tfull_bar[slot[j]]);  // accumulators ready for the epilogue
       }
       // Drain: all MMAs this thread issued retire before TMEM is released.
       tc_commit(drain_bar);
@@ -278,140 +519,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
-    const int q = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int mb = tile / args.n_tiles;
-      const int nt = tile - mb * args.n_tiles;
-      const int e = args.block_expert[mb];
-      if (e < 0 || e >= args.E) {
+    if (MODE == kStage1 && args.zero_ptr != nullptr) {
+      // clear the Stage2 combine target while the first tile's main loop runs
+      uint4* z = static_cast<uint4*>(args.zero_ptr);
+      const long long n16 = args.zero_bytes / 16;
+      const long long t = static_cast<long long>(blockIdx.x) * (kThreads - 64) + (threadIdx.x - 64);
+      for (long long i2 = t; i2 < n16; i2 += static_cast<long long>(gridDim.x) * (kThreads - 64))
+        z[i2] = make_uint4(0, 0, 0, 0);
+    }
+    uint32_t slot_cnt = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int fb, nb, nt, e;
+      if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) {
         if (lane == 0 && args.status) atomicOr(args.status, kStatusBadExpert);
         continue;
       }
-      if (!mbar_wait(&tfull_bar[acc], acc_phase, abort_flag, args.status)) break;
-      tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * kBN);
-      const int p = mb * kBM + row_in_tile;  // padded row of this thread
-
-      if (MODE == kStage1) {
-        OutT* U = reinterpret_cast<OutT*>(args.U);
-        const int n0 = nt * (kBN / 2);
-        float sa = 1.0f;
-        if (IS_I8) sa = args.a_scale[p];
-        float amax = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < kBN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(t_row + c, g);
-          tmem_ld_32x32b_x32(t_row + kBN / 2 + c, u);
-          tmem_ld_wait();
-          const int col0 = n0 + c;
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float g0, g1, u0, u1;
-            if (IS_I8) {
-              const int cc = min(col0 + j, args.N - 2);
-              const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
-              g0 = static_cast<float>(static_cast<int>(g[j])) * sa * args.b0_scale[wrow + cc];
-              g1 = static_cast<float>(static_cast<int>(g[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
-              u0 = static_cast<float>(static_cast<int>(u[j])) * sa * args.b1_scale[wrow + args.b1_row_offset + cc];
-              u1 = static_cast<float>(static_cast<int>(u[j + 1])) * sa *
-                   args.b1_scale[wrow + args.b1_row_offset + cc + 1];
-            } else {
-              g0 = __uint_as_float(g[j]);
-              g1 = __uint_as_float(g[j + 1]);
-              u0 = __uint_as_float(u[j]);
-              u1 = __uint_as_float(u[j + 1]);
-            }
-            const float h0 = silu_mul(g0, u0), h1 = silu_mul(g1, u1);
-            if (IS_I8 && col0 + j < args.N) amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
-            packed[j / 2] = Elt<OutT>::pack2(h0, h1);
-          }
-          OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            if (col0 + v * 8 < args.N)
-              *reinterpret_cast<uint4*>(dst + v * 8) =
-                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          }
+      for (int j = 0; j < nb; ++j) {
+        const int slot = static_cast<int>(slot_cnt % kSlots);
+        const uint32_t use = slot_cnt / kSlots;
+        if (!mbar_wait(&tfull_bar[slot], use & 1u, abort_flag, args.status)) {
+          ok = false;
+          break;
         }
-        if (IS_I8 && args.row_amax)
-          atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));  // amax >= 0
-      } else {
-        // Stage2: per-row scale
-        const int n0 = nt * kBN;
-        float scale = 0.0f;
-        bool valid = false;
-        int token = 0;
-        if (MODE == kStage2Pad) {
-          const int local = p - args.group_padded_offsets[e];
-          valid = local >= 0 && local < args.group_sizes[e];
-          if (valid) {
-            int route = args.group_offsets[e] + local;
-            route = max(0, min(route, args.R - 1));  // reference clamp (SUB/submission.py:935-947)
-            scale = load_weight(args.routed, args.routed_dtype, route);
-          }
-        } else {
-          const int route = args.sorted_route_ids[p];
-          valid = route >= 0 && route < args.R;
-          if (valid) {
-            token = route / args.topk;
-            scale = load_weight(args.routed, args.routed_dtype, route);
-          }
-        }
-        float sa = 1.0f;
-        if (IS_I8) sa = args.a_scale[p];
-        OutT* out = reinterpret_cast<OutT*>(args.out);
-        const size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
-#pragma unroll 1
-        for (int c = 0; c < kBN; c += 32) {
-          const int col0 = n0 + c;
-          if (col0 >= args.N) break;
-          uint32_t d[32];
-          tmem_ld_32x32b_x32(t_row + c, d);
-          tmem_ld_wait();
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            float d0, d1;
-            if (IS_I8) {
-              const int cc = min(col0 + j, args.N - 2);
-              const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
-              d0 = static_cast<float>(static_cast<int>(d[j])) * sa * args.b0_scale[wrow + cc];
-              d1 = static_cast<float>(static_cast<int>(d[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
-            } else {
-              d0 = __uint_as_float(d[j]);
-              d1 = __uint_as_float(d[j + 1]);
-            }
-            packed[j / 2] = valid ? Elt<OutT>::pack2(d0 * scale, d1 * scale) : 0u;
-          }
-          if (MODE == kStage2Pad) {
-            OutT* dst = out + orow * args.ldo + col0;
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col0 + v * 8 < args.N)
-                *reinterpret_cast<uint4*>(dst + v * 8) =
-                    make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          } else if (valid) {
-            OutT* dst = out + orow * args.ldo + col0;
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col0 + v * 8 < args.N)
-                red_add_v4(dst + v * 8,
-                           make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]));
-          }
-        }
-      }
-      // hand the accumulator back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (++acc == 2) {
-        acc = 0;
-        acc_phase ^= 1u;
+        tc_fence_after();
+        const uint32_t t_row =
+            tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * BN);
+        epilogue_block<MODE, OutT, IS_I8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile);
+        // hand the slot back to the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[slot]);
+        ++slot_cnt;
       }
     }
   }
@@ -422,6 +563,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+// ------------------------------------------------------------------ block groups
+// Pairs the routing blocks of each expert: expert e owns blocks [gpo[e]/128, gpo[e+1]/128); they
+// become ceil(n/gmax) groups of up to gmax consecutive blocks, in expert order. One CTA of 1024
+// threads walks the experts in chunks of 1024 with a running base.
+__global__ void __launch_bounds__(1024)
+    build_groups_kernel(const int32_t* __restrict__ group_padded_offsets, int E, int gmax, int32_t* __restrict__ groups,
+                        int32_t* __restrict__ ngroups_out) {
+  __shared__ int s_warp[32];
+  __shared__ int s_base;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (tid == 0) s_base = 0;
+  __syncthreads();
+  for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+    const int e = e0 + tid;
+    int b0 = 0, nblk = 0;
+    if (e < E) {
+      b0 = group_padded_offsets[e] / kBM;
+      nblk = group_padded_offsets[e + 1] / kBM - b0;
+    }
+    const int ng = (nblk + gmax - 1) / gmax;
+    int incl = ng;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_warp[w] = incl;
+    __syncthreads();
+    if (w == 0) {
+      int v = s_warp[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += x;
+      }
+      s_warp[lane] = v;
+    }
+    __syncthreads();
+    const int base = s_base + incl - ng + (w > 0 ? s_warp[w - 1] : 0);
+    for (int g = 0; g < ng; ++g) {
+      const int nb = min(gmax, nblk - g * gmax);
+      groups[base + g] = (b0 + g * gmax) * 2 + (nb - 1);
+    }
+    __syncthreads();
+    if (tid == 0) s_base += s_warp[31];
+    __syncthreads();
+  }
+  if (tid == 0) *ngroups_out = s_base;
 }
 
 }  // namespace moe

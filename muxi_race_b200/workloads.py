@@ -46,6 +46,10 @@ CONFIGS = {
     "cfg3_t128": MoeConfig("cfg3_t128", 128, 7168, 2048, 256, 8, torch.float16, note="decode-like"),
     "cfg4": MoeConfig("cfg4", 4096, 7168, 2048, 256, 8, torch.float16, int8=True, note="W8A8 of cfg3"),
     "cfg5": MoeConfig("cfg5", 32768, 7168, 2048, 256, 8, torch.float16, zipf_s=1.1, note="EP, Zipf-skewed"),
+    # profiling case: cfg3's per-expert shape (about 128 rows per expert) with 32 experts, so a full
+    # ncu capture holds ~3 GB on the device instead of 24 GB
+    "cfg3_e32": MoeConfig("cfg3_e32", 512, 7168, 2048, 32, 8, torch.float16, note="cfg3 shape, 32 experts"),
+    "cfg4_e32": MoeConfig("cfg4_e32", 512, 7168, 2048, 32, 8, torch.float16, int8=True, note="cfg4 shape, 32 experts"),
 }
 
 

@@ -166,7 +166,8 @@ def quantize_rows_ref(w: torch.Tensor):
     """amax/127 per row, round half away from zero, clamp +-127 (submission_v322_int8_v2.py:186-203)."""
     wf = w.to(torch.float32)
     amax = wf.abs().amax(dim=-1)
-    inv = torch.where(amax > 0, 127.0 / amax, torch.zeros_like(amax))
+    # a true fp32 division (``127.0 / tensor`` in torch is reciprocal-then-multiply)
+    inv = torch.where(amax > 0, torch.full_like(amax, 127.0) / amax, torch.zeros_like(amax))
     v = wf * inv.unsqueeze(-1)
     # exact round-half-away-from-zero: v - trunc(v) is exact in fp32, so no double rounding
     t = torch.trunc(v)

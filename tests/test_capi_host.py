@@ -39,8 +39,9 @@ def test_version_and_pure_host_queries():
     assert lib.moe_max_padded_rows(1, 8, 128) == 128
     assert lib.moe_max_padded_rows(128, 8, 128) == 1152
     assert lib.moe_max_padded_rows(32768, 256, 128) == 65280
-    assert lib.moe_run_kernel_workspace_bytes(256, 2048, _lib.MOE_F16) == 256 * 2048 * 2
-    assert lib.moe_fused_workspace_bytes(4096, 8, 256, 7168, 2048, _lib.MOE_F16) > 65280 * (7168 + 2048) * 2
+    assert lib.moe_run_kernel_workspace_bytes(256, 2048, _lib.MOE_F16) == 256 * 2048 * 2 + 256
+    # the Stage1 intermediate U [P_max, I] dominates (token rows are gathered inside Stage1)
+    assert lib.moe_fused_workspace_bytes(4096, 8, 256, 7168, 2048, _lib.MOE_F16) >= 65280 * 2048 * 2
 
 
 def test_invalid_arguments_fail_before_any_launch():
