@@ -16,8 +16,11 @@ roofline = Stage1 (the dominant kernel): algorithmic bytes / measured average la
          measured HBM copy bandwidth (MEASURED_PEAKS.json);
 cpu_baseline = the oracle (a port of the reference's PyTorch operator) on the host cores, on a
          bounded sample of experts, rank 0 at N=1 only.
-With --gpus N > 1 every rank runs an independent replica of the workload (weak scaling, no
-collective on the data path) and value sums the ranks' FLOPs over the slowest rank's time.
+With --gpus N > 1 the step is the expert-parallel fused MoE (muxi_race_b200.ep): the 256 experts
+are sharded E/N per GPU (load-balanced placement from a calibration routing sample) and tokens are
+dispatched and combined with NCCL all-to-all. Default: weak scaling, 4096 tokens per rank (N = 1 is
+exactly cfg3, N = 8 is the 32768-token cfg5 size); --config cfg5: strong scaling, 32768 tokens in
+total with the Zipf-skewed routing. value = all ranks' algorithmic FLOPs / the slowest rank's time.
 --impl reference times the reference's CPU operator (the oracle port) instead.
 """
 from __future__ import annotations
@@ -172,6 +175,8 @@ def cpu_sample(cfg, ids_cpu, w_cpu, x_cpu, budget_s: float, seed: int = 0):
 
 # ----------------------------------------------------------------------------- our arm
 def bench_ours(args, world, rank, local):
+    if world > 1:
+        return bench_ep(args, world, rank, local)
     import muxi_race_b200 as m
     from muxi_race_b200 import _lib
     from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
@@ -220,7 +225,6 @@ def bench_ours(args, world, rank, local):
     _lib.set_profile_events(None)
     end.record(stream)
     torch.cuda.synchronize()
-    clock_info = clocks.stop()
     barrier(world)
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world)
@@ -261,6 +265,7 @@ def bench_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+    clock_info = clocks.stop()  # sampled across both timed regions
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
     d2h = out_h.numel() * out_h.element_size()
     assert m.device_status() == 0, "device status flagged an error during timing"
@@ -323,6 +328,136 @@ def bench_ours(args, world, rank, local):
         }
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+# ----------------------------------------------------------------------------- expert parallel
+def bench_ep(args, world, rank, local):
+    import torch.distributed as dist
+
+    import muxi_race_b200 as m
+    from muxi_race_b200 import _lib
+    from muxi_race_b200.ep import ExpertParallelMoE, ExpertPlacement
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
+
+    dev = torch.device("cuda", local)
+    cfg = CONFIGS[args.config]
+    strong = args.config == "cfg5"
+    T_rank = cfg.T // world if strong else cfg.T
+    peaks, peak_kind = load_peaks()
+
+    # load-balanced placement from a calibration sample (same on every rank)
+    cal_ids, _ = make_routing(cfg, seed=999, device=dev, T=8192)
+    loads = torch.bincount(cal_ids.flatten().long(), minlength=cfg.E).float().cpu().tolist()
+    placement = ExpertPlacement.balanced(loads, world)
+    mine = placement.local_experts(rank)
+    w13, w2 = make_weights(cfg, seed=0, device=dev, experts=mine)
+    x = make_hidden(cfg, seed=1 + rank, device=dev, T=T_rank)
+    ids, tw = make_routing(cfg, seed=2 + rank, device=dev, T=T_rank)
+    moe = ExpertParallelMoE(w13, w2, placement)
+
+    for _ in range(args.warmup):
+        moe(x, ids, tw)
+    torch.cuda.synchronize()
+    assert m.device_status() == 0, "device status flagged an error during warm-up"
+
+    stream = torch.cuda.current_stream(dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    for row in evs:
+        for e in row:
+            e.record(stream)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev) if rank == 0 else None
+    torch.cuda.synchronize()
+    barrier(world)
+    if clocks:
+        clocks.start()
+    start.record(stream)
+    for k in range(args.steps):
+        _lib.set_profile_events(evs[k])
+        moe(x, ids, tw)
+    _lib.set_profile_events(None)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+
+    def stage_ms(a, b):
+        return sum(evs[k][a].elapsed_time(evs[k][b]) for k in range(args.steps)) / args.steps
+
+    local_ms = {"align": stage_ms(0, 1), "gather": stage_ms(1, 2), "stage1": stage_ms(2, 3), "stage2": stage_ms(3, 4)}
+    local_ms["exchange_and_rest"] = start.elapsed_time(end) / args.steps - sum(local_ms.values())
+
+    # algorithmic work: all ranks' routed rows; this rank's local Stage1 rows and experts
+    tot = torch.tensor([float(T_rank * cfg.topk)], dtype=torch.float64, device=dev)
+    dist.all_reduce(tot)
+    flops_total = 2.0 * float(tot.item()) * 3 * cfg.H * cfg.I
+    recv_ids = moe.last_recv_ids
+    local_routes = int((recv_ids >= 0).sum().item())
+    local_active = int(torch.unique(recv_ids[recv_ids >= 0]).numel())
+    s1_flops = 2.0 * local_routes * 2 * cfg.I * cfg.H
+    s1_bytes = local_active * 2 * cfg.I * cfg.H * 2 + local_routes * cfg.H * 2 + local_routes * cfg.I * 2
+    s1_s = local_ms["stage1"] * 1e-3
+    t_mem = s1_bytes / (peaks["hbm_gbs"] * 1e9)
+    t_cmp = s1_flops / (peaks["bf16_tflops"] * 1e12)
+    if t_cmp >= t_mem:
+        roofline = {"bound": "tensor", "achieved": round(s1_flops / s1_s / 1e12, 1), "peak": peaks["bf16_tflops"],
+                    "unit": "TFLOP/s", "frac": round(s1_flops / s1_s / 1e12 / peaks["bf16_tflops"], 4)}
+    else:
+        roofline = {"bound": "hbm", "achieved": round(s1_bytes / s1_s / 1e9, 1), "peak": peaks["hbm_gbs"],
+                    "unit": "GB/s", "frac": round(s1_bytes / s1_s / 1e9 / peaks["hbm_gbs"], 4)}
+    roofline.update({"kernel": "stage1 (rank 0's local fused MoE)", "traffic": None, "peak_kind": peak_kind,
+                     "algorithmic_bytes": s1_bytes, "algorithmic_flops": s1_flops})
+
+    # end to end: host inputs in, output back, every step
+    x_h, ids_h, tw_h = x.cpu().pin_memory(), ids.cpu().pin_memory(), tw.cpu().pin_memory()
+    out_h = torch.empty((T_rank, cfg.H), dtype=cfg.dtype).pin_memory()
+    x_d, ids_d, tw_d = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(tw)
+
+    def e2e_step():
+        x_d.copy_(x_h, non_blocking=True)
+        ids_d.copy_(ids_h, non_blocking=True)
+        tw_d.copy_(tw_h, non_blocking=True)
+        out_h.copy_(moe(x_d, ids_d, tw_d), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+    clock_info = clocks.stop() if clocks else None  # sampled across both timed regions
+    assert m.device_status() == 0, "device status flagged an error during timing"
+    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
+    d2h = out_h.numel() * out_h.element_size()
+    send, recv = moe.last_counts
+
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(flops_total / (ms * 1e-3) / 1e12, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded; weights N(0,1/fan_in), hidden N(0,1), softmax-top-k of N(0,1) logits"
+                    + (" + log-Zipf(1.1) expert bias)" if cfg.zipf_s else ")"),
+            "config": {"workload": f"expert-parallel fused MoE, {cfg.name} shapes H={cfg.H} I={cfg.I} E={cfg.E} "
+                                   f"top-{cfg.topk}, {T_rank} tokens per rank, {T_rank * world} in total",
+                       "tokens_per_rank": T_rank, "parallelism": f"ep{world}", "experts_per_rank": len(mine),
+                       "placement": "balanced (greedy LPT from an 8192-token calibration sample)",
+                       "l2": "inputs larger than L2 (expert weights streamed per step)"},
+            "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
+            "rank0_stage_ms": {k: round(v, 4) for k, v in local_ms.items()},
+            "rank0_rows": {"send": send, "recv": recv, "local_routes": local_routes, "local_active_experts": local_active},
+            "roofline": roofline,
+            "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * 12,
+            "clocks": clock_info,
+        }), flush=True)
 
 
 # ----------------------------------------------------------------------------- reference arm

@@ -168,6 +168,37 @@ MOE_API int moe_fused_int8(const void* hidden_states, const void* w13_q, const f
                    int64_t num_experts, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Expert-parallel building blocks (no reference counterpart: the reference runs on one GPU;
+ * these wrap the NCCL all-to-all exchange that muxi_race_b200/ep.py issues through
+ * torch.distributed). Experts are owned by ranks: expert_rank [E], expert_local [E] int32.
+ *
+ * moe_ep_plan: pairs (token t, rank r) such that t routes to an expert of r, sorted by r then t.
+ *   send_counts [W], send_offsets [W+1] int32; send_pairs [T*W] int32 (t*W + r of each send row);
+ *   pair_slot [T*W] int32 (send row of pair t*W + r, or -1); meta [4] int32 = {n, n, n, 0},
+ *   n = number of send rows. workspace >= moe_ep_plan_workspace_bytes(T, W).
+ * moe_ep_pack: send row p < n gets the token row (send_x [T*W, H] dtype), its top-k expert ids
+ *   rewritten to the destination's local ids or -1 (send_ids [T*W, topk] int32) and its weights
+ *   (send_w [T*W, topk] fp32).
+ * moe_ep_combine: out[t] = sum over r of y[pair_slot[t*W + r]] (y [n, H] dtype, fp32 sum).
+ * Requirements: 1 <= W <= 1024, H % 8 == 0.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API size_t moe_ep_plan_workspace_bytes(int64_t num_tokens, int64_t world);
+
+MOE_API int moe_ep_plan(const void* topk_ids, int ids_dtype, int64_t num_tokens, int64_t topk,
+                        const int32_t* expert_rank, int64_t num_experts, int64_t world, int32_t* send_counts,
+                        int32_t* send_offsets, int32_t* send_pairs, int32_t* pair_slot, int32_t* meta,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+MOE_API int moe_ep_pack(const void* hidden_states, const void* topk_ids, int ids_dtype, const void* topk_weights,
+                        int weights_dtype, const int32_t* expert_rank, const int32_t* expert_local,
+                        int64_t num_experts, const int32_t* send_pairs, const int32_t* meta, int64_t num_tokens,
+                        int64_t hidden, int64_t topk, int64_t world, int dtype, void* send_x, int32_t* send_ids,
+                        float* send_w, void* stream);
+
+MOE_API int moe_ep_combine(const void* y, const int32_t* pair_slot, int64_t num_tokens, int64_t hidden,
+                           int64_t world, int dtype, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@
 #include <string>
 
 #include "../../include/moe_b200.h"
+#include "ep_kernels.cuh"
 #include "gather_quant.cuh"
 #include "moe_gemm.cuh"
 #include "route_align.cuh"
@@ -699,6 +700,102 @@ int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, con
                    void* stream) {
   return fused_common(true, x, w13_q, w13_scale, w2_q, w2_scale, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
                       dtype, workspace, workspace_bytes, stream);
+}
+
+// ---------------------------------------------------------------------------- expert parallel
+size_t moe_ep_plan_workspace_bytes(int64_t T, int64_t W) {
+  if (T <= 0 || W <= 0) return 256;
+  return round_up(sizeof(int32_t) * static_cast<size_t>(T * W), 256) + round_up(sizeof(int32_t) * (W + 1), 256) +
+         moe_align_workspace_bytes(T * W, W);
+}
+
+int moe_ep_plan(const void* ids, int ids_dtype, int64_t T, int64_t topk, const int32_t* expert_rank, int64_t E,
+                int64_t W, int32_t* send_counts, int32_t* send_offsets, int32_t* send_pairs, int32_t* pair_slot,
+                int32_t* meta, void* workspace, size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (W < 1 || W > kAlignMaxExperts) return fail(MOE_ERR_INVALID_ARG, "world must be in [1, %d]", kAlignMaxExperts);
+  if (T < 0 || topk < 1 || E < 1) return fail(MOE_ERR_INVALID_ARG, "bad token/topk/expert count");
+  if (T * W > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens * world exceeds int32");
+  if (ids_dtype != MOE_I32 && ids_dtype != MOE_I64) return fail(MOE_ERR_INVALID_ARG, "topk_ids must be int32 or int64");
+  if (!send_counts || !send_offsets || !meta || (T > 0 && (!ids || !expert_rank || !send_pairs || !pair_slot)))
+    return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (!workspace || workspace_bytes < moe_ep_plan_workspace_bytes(T, W))
+    return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", moe_ep_plan_workspace_bytes(T, W));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* keys = reinterpret_cast<int32_t*>(ws);
+  int32_t* padded = reinterpret_cast<int32_t*>(ws + round_up(sizeof(int32_t) * static_cast<size_t>(T * W), 256));
+  int* counts = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(padded) + round_up(sizeof(int32_t) * (W + 1), 256));
+  if (T > 0) {
+    const int threads = 256;
+    const int64_t n = T * W;
+    const int blocks = static_cast<int>((n + threads - 1) / threads < 4096 ? (n + threads - 1) / threads : 4096);
+    if (ids_dtype == MOE_I32)
+      ep_pair_keys_kernel<int32_t><<<blocks, threads, 0, s>>>(static_cast<const int32_t*>(ids), (int)T, (int)topk,
+                                                              expert_rank, (int)E, (int)W, keys);
+    else
+      ep_pair_keys_kernel<int64_t><<<blocks, threads, 0, s>>>(static_cast<const int64_t*>(ids), (int)T, (int)topk,
+                                                              expert_rank, (int)E, (int)W, keys);
+    MOE_CUDA(cudaGetLastError());
+  }
+  // block size 1: padded offsets equal the plain offsets; no block map
+  MOE_TRY(launch_align(keys, MOE_I32, T * W, W, 1, send_counts, send_offsets, padded, nullptr, send_pairs, pair_slot,
+                       meta, counts, s));
+  return MOE_OK;
+}
+
+int moe_ep_pack(const void* x, const void* ids, int ids_dtype, const void* tw, int w_dtype, const int32_t* expert_rank,
+                const int32_t* expert_local, int64_t E, const int32_t* send_pairs, const int32_t* meta, int64_t T,
+                int64_t H, int64_t topk, int64_t W, int dtype, void* send_x, int32_t* send_ids, float* send_w,
+                void* stream) {
+  t_last_error.clear();
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (H <= 0 || H % 8 != 0) return fail(MOE_ERR_INVALID_ARG, "hidden must be a positive multiple of 8");
+  if (ids_dtype != MOE_I32 && ids_dtype != MOE_I64) return fail(MOE_ERR_INVALID_ARG, "topk_ids must be int32 or int64");
+  if (w_dtype != MOE_F32 && w_dtype != MOE_F16 && w_dtype != MOE_BF16)
+    return fail(MOE_ERR_INVALID_ARG, "topk_weights must be fp32, fp16 or bf16");
+  if (T == 0) return MOE_OK;
+  if (!x || !ids || !tw || !expert_rank || !expert_local || !send_pairs || !meta || !send_x || !send_ids || !send_w)
+    return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (!aligned16(x) || !aligned16(send_x)) return fail(MOE_ERR_ALIGNMENT, "rows must be 16-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int wd = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
+#define MOE_EP_PACK(TT, IT)                                                                                       \
+  ep_pack_kernel<TT, IT><<<sms * 4, 256, 0, s>>>(static_cast<const TT*>(x), static_cast<const IT*>(ids), tw, wd,  \
+                                                 expert_rank, expert_local, (int)E, send_pairs, meta, (int)H,     \
+                                                 (int)topk, (int)W, static_cast<TT*>(send_x), send_ids, send_w)
+  if (dtype == MOE_F16) {
+    if (ids_dtype == MOE_I32) MOE_EP_PACK(__half, int32_t); else MOE_EP_PACK(__half, int64_t);
+  } else {
+    if (ids_dtype == MOE_I32) MOE_EP_PACK(__nv_bfloat16, int32_t); else MOE_EP_PACK(__nv_bfloat16, int64_t);
+  }
+#undef MOE_EP_PACK
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_ep_combine(const void* y, const int32_t* pair_slot, int64_t T, int64_t H, int64_t W, int dtype, void* out,
+                   void* stream) {
+  t_last_error.clear();
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (H <= 0 || H % 8 != 0 || W < 1) return fail(MOE_ERR_INVALID_ARG, "bad hidden or world");
+  if (T == 0) return MOE_OK;
+  if (!pair_slot || !out) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MOE_F16)
+    ep_combine_kernel<__half><<<sms * 8, 256, 0, s>>>(static_cast<const __half*>(y), pair_slot, (int)T, (int)H, (int)W,
+                                                      static_cast<__half*>(out));
+  else
+    ep_combine_kernel<__nv_bfloat16><<<sms * 8, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(y), pair_slot, (int)T,
+                                                             (int)H, (int)W, static_cast<__nv_bfloat16*>(out));
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
 }
 
 }  // extern "C"

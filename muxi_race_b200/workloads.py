@@ -59,16 +59,19 @@ def _gen(device, seed: int) -> torch.Generator:
     return g
 
 
-def make_weights(cfg: MoeConfig, seed: int = 0, device="cuda", experts: int | None = None):
-    """w_gate_up [E, 2I, H] (gate rows then up rows) and w_down [E, H, I] in cfg.dtype."""
-    E = cfg.E if experts is None else experts
-    g = _gen(device, seed)
-    w13 = torch.empty((E, 2 * cfg.I, cfg.H), dtype=cfg.dtype, device=device)
-    w2 = torch.empty((E, cfg.H, cfg.I), dtype=cfg.dtype, device=device)
-    # fill one expert at a time in fp32 to bound the temporary
-    for e in range(E):
-        w13[e].copy_(torch.randn((2 * cfg.I, cfg.H), generator=g, device=device) * (cfg.H ** -0.5))
-        w2[e].copy_(torch.randn((cfg.H, cfg.I), generator=g, device=device) * (cfg.I ** -0.5))
+def make_weights(cfg: MoeConfig, seed: int = 0, device="cuda", experts=None):
+    """w_gate_up [n, 2I, H] (gate rows then up rows) and w_down [n, H, I] in cfg.dtype.
+
+    ``experts``: the global expert ids to build (default all E). Every expert has its own seed, so
+    a rank of an expert-parallel group builds exactly its slice of the global weights.
+    """
+    ids = list(range(cfg.E)) if experts is None else list(experts)
+    w13 = torch.empty((len(ids), 2 * cfg.I, cfg.H), dtype=cfg.dtype, device=device)
+    w2 = torch.empty((len(ids), cfg.H, cfg.I), dtype=cfg.dtype, device=device)
+    for i, e in enumerate(ids):  # one expert at a time in fp32 to bound the temporary
+        g = _gen(device, seed * 1_000_003 + e)
+        w13[i].copy_(torch.randn((2 * cfg.I, cfg.H), generator=g, device=device) * (cfg.H ** -0.5))
+        w2[i].copy_(torch.randn((cfg.H, cfg.I), generator=g, device=device) * (cfg.I ** -0.5))
     return w13, w2
 
 
@@ -77,7 +80,10 @@ def make_hidden(cfg: MoeConfig, seed: int = 1, device="cuda", T: int | None = No
     return torch.randn((T, cfg.H), generator=_gen(device, seed), device=device).to(cfg.dtype)
 
 
-def zipf_bias(E: int, s: float, seed: int, device="cpu") -> torch.Tensor:
+ZIPF_SEED = 1000  # the expert popularity order is a property of the model, shared by every rank
+
+
+def zipf_bias(E: int, s: float, seed: int = ZIPF_SEED, device="cpu") -> torch.Tensor:
     ranks = torch.randperm(E, generator=_gen("cpu", seed)).to(torch.float64) + 1.0
     pmf = ranks.pow(-s)
     pmf = pmf / pmf.sum()
@@ -89,7 +95,7 @@ def make_routing(cfg: MoeConfig, seed: int = 2, device="cuda", T: int | None = N
     T = cfg.T if T is None else T
     logits = torch.randn((T, cfg.E), generator=_gen(device, seed), device=device)
     if cfg.zipf_s > 0:
-        logits = logits + zipf_bias(cfg.E, cfg.zipf_s, seed + 1000, device)
+        logits = logits + zipf_bias(cfg.E, cfg.zipf_s, device=device)
     probs = torch.softmax(logits, dim=-1)
     vals, ids = torch.topk(probs, cfg.topk, dim=-1)
     weights = vals / vals.sum(dim=-1, keepdim=True)

@@ -173,7 +173,7 @@ def quantize_rows_ref(w: torch.Tensor):
     t = torch.trunc(v)
     q = t + torch.where((v - t).abs() >= 0.5, torch.sign(v), torch.zeros_like(v))
     q = q.clamp(-127, 127).to(torch.int8)
-    return q, amax / 127.0
+    return q, amax / torch.full_like(amax, 127.0)
 
 
 def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights,
