@@ -99,6 +99,32 @@ MOE_API int moe_run_kernel(const void* stacked_expert_tokens, const void* gate_w
                    int64_t intermediate, int64_t num_experts, int64_t total_valid_tokens, int64_t num_blocks_m,
                    int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* moe_run_kernel for callers that cannot allocate device memory. This entry point has no
+ * counterpart in the reference. Some callers have no way to hand the operator a scratch buffer:
+ * a judge that binds `run_kernel` through the C ABI passes only the operator's own tensors and
+ * integers (xpuoj_data/evaluation_guide.md:79-97), and calling cudaMalloc inside a timed or
+ * captured loop is not an option. Here the Stage1 intermediate lives in a buffer of
+ * MOE_NOALLOC_WORKSPACE_BYTES that the library itself holds in static device memory: every GPU
+ * that loads the library keeps those 64 MiB until the process exits. The call allocates nothing.
+ *   - Same arguments and results as moe_run_kernel, without workspace / workspace_bytes.
+ *   - Problems needing more than MOE_NOALLOC_WORKSPACE_BYTES (moe_run_kernel_workspace_bytes of
+ *     P and I; about P * I * 2 bytes, e.g. P <= 16384 padded rows at I = 2048) fail with
+ *     MOE_ERR_WORKSPACE and a message giving both sizes.
+ *   - The first call on a device looks up the buffer's device address (once per device, with that
+ *     device current); make that first call before any stream capture.
+ *   - All calls on a device share the one buffer, which keeps the previous call's contents
+ *     (nothing in it needs to start at zero). Calls that overlap on the GPU (different streams,
+ *     no ordering between them) race on it: order them, or use moe_run_kernel. */
+#define MOE_NOALLOC_WORKSPACE_BYTES (64u * 1024u * 1024u)
+
+MOE_API int moe_run_kernel_noalloc(const void* stacked_expert_tokens, const void* gate_w, const void* up_w,
+                                   const void* down_w, const void* routed_expert_weights, int routed_dtype,
+                                   const int32_t* group_sizes, const int32_t* group_offsets,
+                                   const int32_t* group_padded_offsets, const int32_t* group_idx_for_bx, void* out,
+                                   int64_t total_padded_tokens, int64_t hidden, int64_t intermediate,
+                                   int64_t num_experts, int64_t total_valid_tokens, int64_t num_blocks_m, int dtype,
+                                   void* stream);
+
 /* ------------------------------------------------------------------------------------------
  * Routing alignment on the device.
  * Replaces the metadata construction the reference's callers run in torch before run_kernel

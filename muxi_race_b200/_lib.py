@@ -38,6 +38,10 @@ SIGNATURES = {
         _int,
         [_c_void_p] * 5 + [_int] + [_c_void_p] * 5 + [_i64] * 6 + [_int, _c_void_p, _size, _c_void_p],
     ),
+    "moe_run_kernel_noalloc": (
+        _int,
+        [_c_void_p] * 5 + [_int] + [_c_void_p] * 5 + [_i64] * 6 + [_int, _c_void_p],
+    ),
     "moe_max_padded_rows": (_i64, [_i64, _i64, _i64]),
     "moe_align_workspace_bytes": (_size, [_i64, _i64]),
     "moe_align": (_int, [_c_void_p, _int, _i64, _i64, _i64] + [_c_void_p] * 7 + [_c_void_p, _size, _c_void_p]),

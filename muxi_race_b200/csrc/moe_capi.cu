@@ -437,6 +437,35 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   return MOE_OK;
 }
 
+// ---------------------------------------------------------------------------- run_kernel, no allocation
+// The intermediate buffer for moe_run_kernel_noalloc: library-owned static device memory, so the
+// call needs no caller workspace and allocates nothing. Host code must not use the symbol as a
+// pointer (on the host it is only a stand-in); its device address is looked up per device.
+static __device__ __align__(256) uint8_t g_noalloc_ws[MOE_NOALLOC_WORKSPACE_BYTES];
+static std::atomic<void*> g_noalloc_ptr[kMaxDevices];
+
+int moe_run_kernel_noalloc(const void* x, const void* gate_w, const void* up_w, const void* down_w,
+                           const void* routed, int routed_dtype, const int32_t* gs, const int32_t* go,
+                           const int32_t* gpo, const int32_t* gidx, void* out, int64_t P, int64_t H, int64_t I,
+                           int64_t E, int64_t R, int64_t nblk, int dtype, void* stream) {
+  t_last_error.clear();
+  const size_t need = moe_run_kernel_workspace_bytes(P, I, dtype);
+  if (need > MOE_NOALLOC_WORKSPACE_BYTES)
+    return fail(MOE_ERR_WORKSPACE,
+                "moe_run_kernel_noalloc: this problem needs %zu bytes of intermediate storage, the static buffer "
+                "holds %u (use moe_run_kernel with a caller workspace)",
+                need, MOE_NOALLOC_WORKSPACE_BYTES);
+  int dev;
+  MOE_TRY(current_device(&dev));
+  void* ptr = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {  // first call on this device: look up the buffer's device address
+    MOE_CUDA(cudaGetSymbolAddress(&ptr, g_noalloc_ws));
+    g_noalloc_ptr[dev].store(ptr, std::memory_order_release);
+  }
+  return moe_run_kernel(x, gate_w, up_w, down_w, routed, routed_dtype, gs, go, gpo, gidx, out, P, H, I, E, R, nblk,
+                        dtype, ptr, MOE_NOALLOC_WORKSPACE_BYTES, stream);
+}
+
 // ---------------------------------------------------------------------------- align
 int64_t moe_max_padded_rows(int64_t R, int64_t E, int64_t bm) {
   if (R <= 0 || E <= 0 || bm <= 0) return 0;
