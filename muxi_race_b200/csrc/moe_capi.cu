@@ -141,29 +141,25 @@ bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0;
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // ------------------------------------------------------------------ GEMM launch
-// Tile configurations: accumulator width per block x blocks per work unit.
-//   kTile256    BN = 256, one block per unit, two accumulator slots, 4 x 48 KiB stages (default:
-//               fastest measured on cfg3, the decode-like T=128 case and the int8 route)
-//   kTile256x2  BN = 256, block groups of up to two blocks of one expert, 3 x 64 KiB stages
-//   kTile512    BN = 512, one block per unit, one slot, 2 x 80 KiB stages
-// MOE_B200_TILE = 512 | 256x2 | 256 overrides the default for experiments.
-enum TileCfg { kTile512 = 0, kTile256x2 = 1, kTile256 = 2 };
+// Tile configurations: accumulator width per block, blocks per work unit, A / B ring depths.
+// MOE_B200_TILE selects one by name for experiments; the default is the fastest measured.
+enum TileCfg { kT256A4B5 = 0, kT256x2A2B4, kT512A2B3, kNumTileCfg };
+const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a2b4", "512a2b3"};
 
 TileCfg tile_cfg() {
   static const TileCfg t = [] {
     const char* v = getenv("MOE_B200_TILE");
-    if (v && strcmp(v, "512") == 0) return kTile512;
-    if (v && strcmp(v, "256x2") == 0) return kTile256x2;
-    return kTile256;
+    if (v)
+      for (int i = 0; i < kNumTileCfg; ++i)
+        if (strcmp(v, kTileNames[i]) == 0) return static_cast<TileCfg>(i);
+    return kT256A4B5;
   }();
   return t;
 }
-int cfg_bn(TileCfg c) { return c == kTile512 ? 512 : 256; }
-int cfg_gmax(TileCfg c) { return c == kTile256x2 ? 2 : 1; }
+int cfg_bn(TileCfg c) { return c == kT512A2B3 ? 512 : 256; }
+int cfg_gmax(TileCfg c) { return c == kT256x2A2B4 ? 2 : 1; }
 
-// How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu. Default tma: on B200 the
-// TMA tile load of pre-stacked rows measured faster than gathering token rows with cp.async inside
-// Stage1 (cfg3: 5.1 ms vs 6.4 ms per call), the stacking gather costing 0.11 ms.
+// How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu.
 bool a_path_lsu() {
   static const bool v = [] {
     const char* e = getenv("MOE_B200_A_PATH");
@@ -172,14 +168,12 @@ bool a_path_lsu() {
   return v;
 }
 
-template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AMODE>
-int launch_gemm(int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1, const GemmArgs& args,
-                int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AMODE>;
-  constexpr int tcfg = BN == 512 ? 0 : (GMAX == 2 ? 1 : 2);
-  constexpr int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * 3 + tcfg) * 3 + AMODE;
-  static_assert(bit < 128, "attribute bit out of range");
-  constexpr int smem = Ring<BN, GMAX>::kSmemBytes;
+template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE>
+int launch_gemm(int dev, int tcfg, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE>;
+  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3 + AMODE;
+  constexpr int smem = Ring<BN, GMAX, AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
@@ -190,26 +184,29 @@ int launch_gemm(int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUte
   return MOE_OK;
 }
 
-// One grouped GEMM stage with the chosen tile configuration and A path.
+// One grouped GEMM stage with the chosen tile configuration.
 template <int MODE, typename OutT, bool I8, int AMODE>
 int launch_stage(TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                  const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   switch (c) {
-    case kTile256x2: return launch_gemm<MODE, OutT, I8, 256, 2, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
-    case kTile256: return launch_gemm<MODE, OutT, I8, 256, 1, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
-    default: return launch_gemm<MODE, OutT, I8, 512, 1, AMODE>(dev, a, b0, b1, args, max_tiles, stream);
+    case kT256x2A2B4:
+      return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+    case kT512A2B3:
+      return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+    default:
+      return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
   }
 }
 
 // Stage dispatch over the runtime element type and A path.
-template <int MODE, bool I8, int AMODE_TMA, int AMODE_LSU>
+template <int MODE, bool I8, int AMODE_LSU>
 int launch_stage_rt(int dtype, bool lsu, TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0,
                     const CUtensorMap& b1, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   if (dtype == MOE_F16)
     return lsu ? launch_stage<MODE, __half, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
-               : launch_stage<MODE, __half, I8, AMODE_TMA>(c, dev, a, b0, b1, args, max_tiles, stream);
+               : launch_stage<MODE, __half, I8, kATma>(c, dev, a, b0, b1, args, max_tiles, stream);
   return lsu ? launch_stage<MODE, __nv_bfloat16, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
-             : launch_stage<MODE, __nv_bfloat16, I8, AMODE_TMA>(c, dev, a, b0, b1, args, max_tiles, stream);
+             : launch_stage<MODE, __nv_bfloat16, I8, kATma>(c, dev, a, b0, b1, args, max_tiles, stream);
 }
 
 // ------------------------------------------------------------------ align
@@ -279,8 +276,8 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.groups = take(sizeof(int) * (size_t)(L.nblk_max + 1));  // block groups + their count
   L.sorted = take(sizeof(int) * (size_t)L.P_max);
   L.slot = take(sizeof(int) * (size_t)R);
-  // activations: LSU path gathers token rows in the GEMM (int8: tokens quantised in place first);
-  // TMA path stacks gathered rows first
+  // token rows: stacked per expert (TMA A path) or read in place (LSU gather; int8 quantised
+  // per token first)
   const size_t a_rows = lsu ? (size_t)T : (size_t)L.P_max;
   L.xs = take(lsu ? (int8 ? a_rows * H : 0) : (int8 ? 1 : 2) * a_rows * H);
   L.xscale = take(int8 ? sizeof(float) * a_rows : 0);
@@ -432,8 +429,8 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a2.a_ptr = U;
   a2.a_row_bytes = I * 2;
   const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
-  MOE_TRY((launch_stage_rt<kStage1, false, kATma, kALsu>(dtype, lsu, tc, dev, tA, tG, tU, a1, tiles1, s)));
-  MOE_TRY((launch_stage_rt<kStage2Pad, false, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tD, tD, a2, tiles2, s)));
+  MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc, dev, tA, tG, tU, a1, tiles1, s)));
+  MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc, dev, tUA, tD, tD, a2, tiles2, s)));
   return MOE_OK;
 }
 
@@ -556,9 +553,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   }
   prof_record(1, s);
 
-  // 2. activations: the LSU path reads token rows straight from hidden_states inside Stage1
-  //    (int8: after a per-token quantisation); the TMA path stacks the gathered rows first and
-  //    zeroes the combine target (the LSU path zeroes it in Stage1's epilogue warps)
+  // 2. activations: the TMA A path stacks the gathered token rows (int8: quantised per token)
+  //    and zeroes the combine target; the LSU path gathers token rows inside Stage1 (int8: after
+  //    an in-place per-token quantisation) and Stage1's epilogue warps zero the combine target
   const bool lsu = a_path_lsu();
   const int gblocks = sms * 4;
   float* amax = int8 ? reinterpret_cast<float*>(ws + L.amax) : nullptr;
@@ -605,8 +602,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   CUtensorMap tA, tW13, tUA, tW2;
   MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, bn / 2, "w_gate_up"));
   MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kMmaN, "w_down"));
-  if (lsu) {
-    tA = tW13;  // unused by the LSU A path
+  if (lsu) {  // the LSU path does not use the A tensor maps
+    tA = tW13;
     tUA = tW2;
   } else {
     MOE_TRY(make_tmap(&tA, xs, elt, L.P_max, H, kBM, "gathered hidden_states"));
@@ -664,13 +661,13 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
-    MOE_TRY((launch_stage_rt<kStage1, false, kATma, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
     prof_record(3, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, false, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(4, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
-    MOE_TRY((launch_stage_rt<kStage1, true, kATma, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
     prof_record(3, s);
     if (dtype == MOE_F16)
       quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
@@ -682,7 +679,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
           reinterpret_cast<float*>(ws + L.uscale));
     MOE_CUDA(cudaGetLastError());
     prof_record(4, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, true, kATma, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(5, s);
   }
   return MOE_OK;

@@ -2,8 +2,8 @@
 // warp-specialised tcgen05 kernel template for sm_100a.
 //
 // One CTA per SM (192 threads):
-//   warp 0      TMA producer: streams A (token rows) and B (expert weight rows) k-blocks into a
-//               STAGES-deep ring of 128B-swizzled shared-memory buffers;
+//   warp 0      TMA producer: streams A (token rows) and B (expert weight rows) k-blocks into two
+//               rings of 128B-swizzled shared-memory buffers (A and B have separate depths);
 //   warp 1      owns TMEM (512 columns = two 128 x 256 fp32/int32 accumulator slots); one lane
 //               issues tcgen05.mma for each k-block and commits to the ring's "empty" barriers;
 //   warps 2..5  epilogue: tcgen05.ld a finished accumulator (warp w reads TMEM lanes
@@ -44,19 +44,26 @@ namespace moe {
 constexpr int kBM = 128;       // rows per block = routing block size
 constexpr int kMmaN = 256;     // N of one tcgen05.mma
 constexpr int kKBytes = 128;   // k-block width in bytes (one 128B swizzle atom)
-constexpr int kThreads = 192;  // 6 warps
+constexpr int kThreads = 224;  // 7 warps
 constexpr int kABytes = kBM * kKBytes;  // 16 KiB per A block per stage
 constexpr int kTmemCols = 512;
-constexpr int kRingBudget = 200 * 1024;
+constexpr int kRingMax = 224 * 1024;
 
-template <int BN, int GMAX> struct Ring {
+// Shared-memory rings: A (token rows, mostly L2 hits) and B (expert weights, streamed from HBM)
+// have separate depths, so the weight stream can run further ahead than the A stream.
+template <int BN, int GMAX, int AST, int BST> struct Ring {
   static_assert(BN == 256 || BN == 512, "accumulator width");
   static_assert(GMAX >= 1 && GMAX * BN <= kTmemCols, "a block group must fit in TMEM");
+  static constexpr int kAStageBytes = GMAX * kABytes;
   static constexpr int kBBytes = BN * kKBytes;
-  static constexpr int kStageBytes = GMAX * kABytes + kBBytes;  // A blocks then B
-  static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
-  static constexpr int kSlots = kTmemCols / BN;                 // accumulator slots
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + 256 /*barriers*/;
+  static constexpr int kAStages = AST;
+  static constexpr int kBStages = BST;
+  static constexpr int kRingBytes = AST * kAStageBytes + BST * kBBytes;
+  static_assert(kRingBytes <= kRingMax, "ring exceeds shared memory");
+  static constexpr int kSlots = kTmemCols / BN;  // accumulator slots
+  static constexpr int kRowTabBytes = GMAX * 128 * 8;  // LSU A path: source row offsets of a group
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kRingBytes + 512 /*barriers*/ + kRowTabBytes;
+  static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may opt in to");
 };
 
 enum GemmMode : int { kStage1 = 0, kStage2Pad = 1, kStage2Comb = 2 };
@@ -97,10 +104,10 @@ struct GemmArgs {
   const float* b1_scale;      // [E * b_rows_per_expert] (up rows, Stage1)
   float* row_amax;            // Stage1 int8: per-row amax of U (for requantisation), may be null
 
-  // A operand through the LSU path (AMODE 1 / 2): row-major rows of a_row_bytes bytes
+  // A operand through the LSU path (kALsu / kAGather): rows of a_row_bytes bytes at a_ptr
   const void* a_ptr;
   long long a_row_bytes;
-  // Stage1 only: the epilogue warps zero this buffer first (the Stage2 combine target)
+  // Stage1 with kAGather: the epilogue warps first zero this buffer (the Stage2 combine target)
   void* zero_ptr;
   long long zero_bytes;
 
@@ -109,10 +116,11 @@ struct GemmArgs {
 
 // How the A operand reaches shared memory:
 //   kATma     one TMA box per block (rows = padded rows of the A tensor map)
-//   kALsu     cp.async by the producer warp, row p of a_ptr (identity)
-//   kAGather  cp.async by the producer warp, row sorted_route_ids[p] / topk of a_ptr (the token
-//             row of each routed row: the gathered-row load, no stacked copy of the tokens);
-//             padding rows are zero-filled
+//   kALsu     cp.async by a producer warp, row p of a_ptr
+//   kAGather  cp.async by a producer warp, row sorted_route_ids[p] / topk of a_ptr: each routed
+//             row reads its token row directly (no stacked copy); padding rows are zero-filled
+// The LSU warp maps 8 lanes to the eight 16-byte chunks of one 128-byte row segment, so every
+// instruction moves four whole segments; it is a second load path next to the TMA unit.
 enum AMode : int { kATma = 0, kALsu = 1, kAGather = 2 };
 
 // Source row of padded row p for the A operand, -1 for padding.
@@ -297,37 +305,44 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AMODE>
+template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  using RingT = Ring<BN, GMAX>;
-  constexpr int kStages = RingT::kStages;
-  constexpr int kStageBytes = RingT::kStageBytes;
+  using RingT = Ring<BN, GMAX, AST, BST>;
+  constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kSlots = RingT::kSlots;
   constexpr int kHalves = BN / kMmaN;  // MMAs per k-step per block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
-  uint64_t* full_bar = bars;                                // [kStages]
-  uint64_t* empty_bar = bars + kStages;                     // [kStages]
-  uint64_t* tfull_bar = bars + 2 * kStages;                 // [kSlots] per accumulator slot
-  uint64_t* tempty_bar = bars + 2 * kStages + kSlots;       // [kSlots]
-  uint64_t* drain_bar = bars + 2 * kStages + 2 * kSlots;    // [1] MMA warp: all issued MMAs retired
+  uint8_t* ring_b = smem;                            // [BST][kBBytes]
+  uint8_t* ring_a = smem + BST * kBBytes;            // [AST][GMAX][kABytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RingT::kRingBytes);
+  uint64_t* fullA = bars;                            // [AST]
+  uint64_t* emptyA = fullA + AST;                    // [AST]
+  uint64_t* fullB = emptyA + AST;                    // [BST]
+  uint64_t* emptyB = fullB + BST;                    // [BST]
+  uint64_t* tfull_bar = emptyB + BST;                // [kSlots] per accumulator slot
+  uint64_t* tempty_bar = tfull_bar + kSlots;         // [kSlots]
+  uint64_t* drain_bar = tempty_bar + kSlots;         // [1] MMA warp: all issued MMAs retired
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  auto stage_a = [&](int s, int j) { return smem + s * kStageBytes + j * kABytes; };
-  auto stage_b = [&](int s) { return smem + s * kStageBytes + GMAX * kABytes; };
+  long long* row_tab = reinterpret_cast<long long*>(smem + RingT::kRingBytes + 512);  // [GMAX][128]
+  auto stage_a = [&](int s, int j) { return ring_a + s * kAStageBytes + j * kABytes; };
+  auto stage_b = [&](int s) { return ring_b + s * kBBytes; };
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      // TMA A: lane 0's expect_tx arrive; LSU A: plus one arrive per producer lane
-      mbar_init(&full_bar[s], AMODE == kATma ? 1 : 33);
-      mbar_init(&empty_bar[s], 1);
+    for (int s = 0; s < AST; ++s) {
+      mbar_init(&fullA[s], AMODE == kATma ? 1 : 32);  // TMA: expect_tx arrive; LSU: one per lane
+      mbar_init(&emptyA[s], 1);
+    }
+    for (int s = 0; s < BST; ++s) {
+      mbar_init(&fullB[s], 1);
+      mbar_init(&emptyB[s], 1);
     }
     for (int a = 0; a < kSlots; ++a) {
       mbar_init(&tfull_bar[a], 1);
@@ -356,108 +371,108 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_kb = (args.K * (IS_I8 ? 1 : 2) + kKBytes - 1) / kKBytes;
   constexpr int kKElems = IS_I8 ? kKBytes : kKBytes / 2;
 
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer
-    // Lane 0 issues the TMA loads (B always, A with kATma); with an LSU A path all 32 lanes
-    // gather the A rows with cp.async, 16 bytes at a time, into the 128B-swizzled layout.
-    const uint64_t pol_a = l2_policy_evict_last();  // token rows: re-read by every column tile
-    const uint64_t pol_b = l2_policy_evict_normal();
-    const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    int issued_parity[kStages];  // parity of the last load issued into each stage, -1 = none
+  if (warp == 0 || warp == 6) {
+    // ---------------------------------------------------------------- producers
+    // Warp 0 lane 0 streams B (weights) into the B ring by TMA; warp 6 streams A (token rows)
+    // into the A ring, by TMA from lane 0 (kATma) or by cp.async from all 32 lanes (LSU paths).
+    // Each waits only for its own ring, so B runs up to BST k-blocks ahead of the MMA and A up
+    // to AST, independently.
+    const bool is_b = warp == 0;
+    const bool active = is_b ? lane == 0 : (AMODE != kATma || lane == 0);
+    if (active) {
+      const int depth = is_b ? BST : AST;
+      uint64_t* full = is_b ? fullB : fullA;
+      uint64_t* empty = is_b ? emptyB : emptyA;
+      const uint64_t pol = is_b ? l2_policy_evict_normal()
+                                : l2_policy_evict_last();  // token rows: re-read by every column tile
+      const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
+      int st = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int par[AST > BST ? AST : BST];  // parity of the last load issued into each slot, -1 = none
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) issued_parity[s] = -1;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int fb, nb, nt, e;
-      if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
-      int brow0, brow1 = 0;
-      if (MODE == kStage1) {
-        brow0 = e * args.b_rows_per_expert + nt * (BN / 2);
-        brow1 = e * args.b_rows_per_expert + args.b1_row_offset + nt * (BN / 2);
-      } else {
-        brow0 = e * args.b_rows_per_expert + nt * BN;
-      }
-      // this lane's A rows (lane + 32 i of each block) as byte pointers, null = zero fill
-      const char* arow[GMAX][4];
-      if (AMODE != kATma) {
-#pragma unroll
-        for (int j = 0; j < GMAX; ++j)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            arow[j][i] = nullptr;
-            if (j < nb) {
-              const long long src = a_source_row<AMODE>(args, (fb + j) * kBM + lane + 32 * i);
-              if (src >= 0) arow[j][i] = static_cast<const char*>(args.a_ptr) + src * args.a_row_bytes;
+      for (int s = 0; s < (AST > BST ? AST : BST); ++s) par[s] = -1;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int fb, nb, nt, e;
+        if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        int brow0, brow1 = 0;
+        if (MODE == kStage1) {
+          brow0 = e * args.b_rows_per_expert + nt * (BN / 2);
+          brow1 = e * args.b_rows_per_expert + args.b1_row_offset + nt * (BN / 2);
+        } else {
+          brow0 = e * args.b_rows_per_expert + nt * BN;
+        }
+        if (!is_b && AMODE != kATma) {
+          // byte offsets of this group's source rows, -1 = zero fill
+          __syncwarp();
+          for (int j = 0; j < nb; ++j)
+            for (int r = lane; r < kBM; r += 32) {
+              const long long src = a_source_row<AMODE>(args, (fb + j) * kBM + r);
+              row_tab[j * kBM + r] = src >= 0 ? src * args.a_row_bytes : -1;
             }
-          }
-      }
-      const uint32_t tx = static_cast<uint32_t>((AMODE == kATma ? nb * kABytes : 0) + kBBytes);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status)) {
-          ok = false;
-          break;
+          __syncwarp();
         }
-        const int kx = kb * kKElems;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&full_bar[stage], tx);
-          if (AMODE == kATma)
-            for (int j = 0; j < nb; ++j)
-              tma_load_2d(stage_a(stage, j), &tmA, &full_bar[stage], kx, (fb + j) * kBM, pol_a);
-          if (MODE == kStage1) {  // gate rows, then up rows: BN/2 each
-            tma_load_2d(stage_b(stage), &tmB0, &full_bar[stage], kx, brow0, pol_b);
-            tma_load_2d(stage_b(stage) + kBBytes / 2, &tmB1, &full_bar[stage], kx, brow1, pol_b);
-          } else {  // BN rows as boxes of 256
-#pragma unroll
-            for (int h = 0; h < kHalves; ++h)
-              tma_load_2d(stage_b(stage) + h * (kMmaN * kKBytes), &tmB0, &full_bar[stage], kx, brow0 + h * kMmaN,
-                          pol_b);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int kx = kb * kKElems;
+          bool got = mbar_wait(&empty[st], ph ^ 1u, abort_flag, args.status);
+          if (!is_b && AMODE != kATma) got = __all_sync(0xffffffffu, got);  // the warp stays converged
+          if (!got) {
+            ok = false;
+            break;
           }
-        }
-        if (AMODE != kATma) {
-          const long long kbyte0 = static_cast<long long>(kb) * kKBytes;
+          if (is_b) {
+            mbar_arrive_expect_tx(&full[st], kBBytes);
+            if (MODE == kStage1) {  // gate rows, then up rows: BN/2 each
+              tma_load_2d(stage_b(st), &tmB0, &full[st], kx, brow0, pol);
+              tma_load_2d(stage_b(st) + kBBytes / 2, &tmB1, &full[st], kx, brow1, pol);
+            } else {  // BN rows as boxes of 256
 #pragma unroll
-          for (int j = 0; j < GMAX; ++j) {
-            if (j >= nb) break;
-            const uint32_t dst0 = smem_u32(stage_a(stage, j));
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = lane + 32 * i;
-              const char* src = arow[j][i];
-#pragma unroll
-              for (int c = 0; c < kKBytes / 16; ++c) {
-                const long long kbyte = kbyte0 + c * 16;
-                const bool in = src != nullptr && kbyte < a_k_bytes;
-                // 128-byte swizzle: 16-byte chunk c of row r sits at chunk c ^ (r % 8)
-                cp_async_16(dst0 + r * kKBytes + ((c ^ (r & 7)) << 4), in ? src + kbyte : args.a_ptr, in ? 16u : 0u);
+              for (int h = 0; h < kHalves; ++h)
+                tma_load_2d(stage_b(st) + h * (kMmaN * kKBytes), &tmB0, &full[st], kx, brow0 + h * kMmaN, pol);
+            }
+          } else if (AMODE == kATma) {
+            mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * kABytes));
+            for (int j = 0; j < nb; ++j) tma_load_2d(stage_a(st, j), &tmA, &full[st], kx, (fb + j) * kBM, pol);
+          } else {
+            const int c = lane & 7;  // 16-byte chunk of the 128-byte k-block row segment
+            const long long kbyte = static_cast<long long>(kb) * kKBytes + c * 16;
+            const bool k_in = kbyte < a_k_bytes;
+            const char* a_base = static_cast<const char*>(args.a_ptr);
+            for (int j = 0; j < nb; ++j) {
+              const uint32_t dst0 = smem_u32(stage_a(st, j));
+#pragma unroll 8
+              for (int i = 0; i < kBM / 4; ++i) {
+                const int r = (lane >> 3) + 4 * i;
+                const long long off = row_tab[j * kBM + r];
+                const bool in = k_in && off >= 0;
+                // 128-byte swizzle: chunk c of row r sits at chunk c ^ (r % 8)
+                cp_async_16(dst0 + r * kKBytes + ((c ^ (r & 7)) << 4), in ? a_base + off + kbyte : a_base,
+                            in ? 16u : 0u);
               }
             }
+            cp_async_mbar_arrive(&full[st]);
+            mbar_arrive(&full[st]);
           }
-          cp_async_mbar_arrive(&full_bar[stage]);
-          mbar_arrive(&full_bar[stage]);
-        }
-        issued_parity[stage] = static_cast<int>(phase);
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+          par[st] = static_cast<int>(ph);
+          if (++st == depth) {
+            st = 0;
+            ph ^= 1u;
+          }
         }
       }
-    }
-    // Drain: every copy this warp issued must have landed before the CTA may exit. On the
-    // normal path these phases completed long ago; after an abort this bounds the wait.
-    if (AMODE != kATma) cp_async_wait_all();
-    if (lane == 0) {
-#pragma unroll
-      for (int s = 0; s < kStages; ++s)
-        if (issued_parity[s] >= 0) mbar_wait_drain(&full_bar[s], static_cast<uint32_t>(issued_parity[s]));
+      // Drain: every copy this lane issued must have landed before the CTA may exit. On the
+      // normal path these phases completed long ago; after an abort this bounds the wait.
+      if (!is_b && AMODE != kATma) cp_async_wait_all();
+      if (is_b || AMODE == kATma)
+        for (int s = 0; s < depth; ++s)
+          if (par[s] >= 0) mbar_wait_drain(&full[s], static_cast<uint32_t>(par[s]));
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kMmaN) : idesc_f16(Elt<OutT>::kBF16, kBM, kMmaN);
-      int stage = 0;
-      uint32_t phase = 0;
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pb = 0;
       uint32_t slot_cnt = 0;  // accumulator slots handed out so far (slot = cnt % kSlots)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
@@ -477,17 +492,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, abort_flag, args.status)) {
+          if (!mbar_wait(&fullB[sb], pb, abort_flag, args.status) ||
+              !mbar_wait(&fullA[sa], pa, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (AMODE != kATma) fence_proxy_async_smem();  // A arrived through the generic proxy
-          const uint32_t b_addr = smem_u32(stage_b(stage));
+          const uint32_t b_addr = smem_u32(stage_b(sb));
 #pragma unroll
           for (int j = 0; j < GMAX; ++j) {
             if (j >= nb) break;
-            const uint32_t a_addr = smem_u32(stage_a(stage, j));
+            const uint32_t a_addr = smem_u32(stage_a(sa, j));
 #pragma unroll
             for (int k = 0; k < kKBytes / 32; ++k) {
               const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
@@ -502,10 +518,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          tc_commit(&empty_bar[stage]);  // frees this smem stage once the MMAs have read it
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1u;
+          tc_commit(&emptyB[sb]);  // frees the ring slots once the MMAs have read them
+          tc_commit(&emptyA[sa]);
+          if (++sb == BST) {
+            sb = 0;
+            pb ^= 1u;
+          }
+          if (++sa == AST) {
+            sa = 0;
+            pa ^= 1u;
           }
         }
         if (!ok) break;
@@ -525,9 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // clear the Stage2 combine target while the first tile's main loop runs
       uint4* z = static_cast<uint4*>(args.zero_ptr);
       const long long n16 = args.zero_bytes / 16;
-      const long long t = static_cast<long long>(blockIdx.x) * (kThreads - 64) + (threadIdx.x - 64);
-      for (long long i2 = t; i2 < n16; i2 += static_cast<long long>(gridDim.x) * (kThreads - 64))
-        z[i2] = make_uint4(0, 0, 0, 0);
+      const long long t0 = static_cast<long long>(blockIdx.x) * 128 + (threadIdx.x - 64);
+      for (long long i2 = t0; i2 < n16; i2 += static_cast<long long>(gridDim.x) * 128) z[i2] = make_uint4(0, 0, 0, 0);
     }
     uint32_t slot_cnt = 0;
     bool ok = true;
