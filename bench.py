@@ -131,6 +131,17 @@ def barrier(world):
         dist.barrier()
 
 
+def gather_over_ranks(v: float, world: int) -> list:
+    if world == 1:
+        return [v]
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [round(float(x.item()), 4) for x in out]
+
+
 def max_over_ranks(v: float, world: int) -> float:
     if world == 1:
         return v
@@ -380,6 +391,11 @@ def bench_ep(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    rank_ms = gather_over_ranks(start.elapsed_time(end) / args.steps, world)
+    # per-step wall on the device: from one step's first stage event to the next step's
+    steps_ms = [evs[k][0].elapsed_time(evs[k + 1][0]) for k in range(args.steps - 1)]
+    rank_step_max = gather_over_ranks(max(steps_ms) if steps_ms else 0.0, world)
+    rank_step_med = gather_over_ranks(statistics.median(steps_ms) if steps_ms else 0.0, world)
 
     def stage_ms(a, b):
         return sum(evs[k][a].elapsed_time(evs[k][b]) for k in range(args.steps)) / args.steps
@@ -451,6 +467,7 @@ def bench_ep(args, world, rank, local):
                        "l2": "inputs larger than L2 (expert weights streamed per step)"},
             "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
             "rank0_stage_ms": {k: round(v, 4) for k, v in local_ms.items()},
+            "rank_ms": rank_ms, "rank_step_ms_median": rank_step_med, "rank_step_ms_max": rank_step_max,
             "rank0_rows": {"send": send, "recv": recv, "local_routes": local_routes, "local_active_experts": local_active},
             "roofline": roofline,
             "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),

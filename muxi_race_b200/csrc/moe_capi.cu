@@ -61,7 +61,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   std::atomic<int> sms{0};
   std::atomic<uint32_t*> status{nullptr};
-  std::atomic<uint64_t> attr_done[2] = {};  // bit per kernel whose smem attribute has been raised
+  std::atomic<uint64_t> attr_done[4] = {};  // bit per kernel whose smem attribute has been raised
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -129,9 +129,15 @@ int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, i
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * elt_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBytes / elt_bytes), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
+  static const CUtensorMapL2promotion promo = [] {
+    const char* v = getenv("MOE_B200_L2_PROMO");  // experiments: none | 64 | 128 | 256 (default)
+    if (v && strcmp(v, "none") == 0) return CU_TENSOR_MAP_L2_PROMOTION_NONE;
+    if (v && strcmp(v, "64") == 0) return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+    if (v && strcmp(v, "128") == 0) return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+    return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  }();
   CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                   CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, (int)r);
   return MOE_OK;
 }
@@ -143,8 +149,8 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // ------------------------------------------------------------------ GEMM launch
 // Tile configurations: accumulator width per block, blocks per work unit, A / B ring depths.
 // MOE_B200_TILE selects one by name for experiments; the default is the fastest measured.
-enum TileCfg { kT256A4B5 = 0, kT256x2A2B4, kT512A2B3, kNumTileCfg };
-const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a2b4", "512a2b3"};
+enum TileCfg { kT256A4B5 = 0, kT256x2A2B4, kT512A2B3, kT256A2B2C2, kT256A2B6, kNumTileCfg };
+const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a2b4", "512a2b3", "256a2b2c2", "256a2b6"};
 
 TileCfg tile_cfg() {
   static const TileCfg t = [] {
@@ -168,18 +174,24 @@ bool a_path_lsu() {
   return v;
 }
 
-template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE>
+template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS = 1>
 int launch_gemm(int dev, int tcfg, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                 const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE>;
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS>;
+  static const int evict_first = [] {
+    const char* v = getenv("MOE_B200_B_EVICT_FIRST");  // experiments: 1 = evict_first for weights
+    return v && strcmp(v, "1") == 0 ? 1 : 0;
+  }();
+  GemmArgs args_l = args;
+  args_l.b_evict_first = evict_first;
   const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3 + AMODE;
-  constexpr int smem = Ring<BN, GMAX, AST, BST>::kSmemBytes;
+  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
-  const int grid = max_tiles < sms ? max_tiles : sms;
+  const int grid = max_tiles < sms * CPS ? max_tiles : sms * CPS;
   if (grid <= 0) return MOE_OK;
-  kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, args);
+  kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, args_l);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }
@@ -193,6 +205,10 @@ int launch_stage(TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0
       return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
     case kT512A2B3:
       return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+    case kT256A2B2C2:
+      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2>(dev, c, a, b0, b1, args, max_tiles, stream);
+    case kT256A2B6:
+      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 6, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
     default:
       return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
   }

@@ -18,6 +18,11 @@
 // are what the tiling minimises. Column tiles of one group run back to back (the group's A rows
 // are re-read from L2, not HBM).
 //
+// CTAs per SM (CPS): measured on B200, one CTA completes about one TMA box per ~340 ns whatever
+// its size (16 KiB boxes: ~48 GB/s per SM from L2), while a second CTA on the SM doubles the rate.
+// With CPS = 2 each CTA takes half the shared memory and half of TMEM (one 256-column slot), and
+// the two CTAs' epilogues and main loops overlap each other.
+//
 // Tiles: 128 rows per block x BN accumulator columns (BN = 256: two accumulator slots, so an
 // epilogue overlaps the next tile's main loop, or one block group of two blocks; BN = 512: one
 // slot, two N = 256 MMAs per k-step sharing the A block). k-blocks are 128 bytes wide (64
@@ -51,19 +56,22 @@ constexpr int kRingMax = 224 * 1024;
 
 // Shared-memory rings: A (token rows, mostly L2 hits) and B (expert weights, streamed from HBM)
 // have separate depths, so the weight stream can run further ahead than the A stream.
-template <int BN, int GMAX, int AST, int BST> struct Ring {
+template <int BN, int GMAX, int AST, int BST, int CPS = 1> struct Ring {
   static_assert(BN == 256 || BN == 512, "accumulator width");
-  static_assert(GMAX >= 1 && GMAX * BN <= kTmemCols, "a block group must fit in TMEM");
+  static_assert(CPS == 1 || CPS == 2, "CTAs per SM");
+  static constexpr int kTmemColsCta = kTmemCols / CPS;  // TMEM columns this CTA allocates
+  static_assert(GMAX >= 1 && GMAX * BN <= kTmemColsCta, "a block group must fit in TMEM");
   static constexpr int kAStageBytes = GMAX * kABytes;
   static constexpr int kBBytes = BN * kKBytes;
   static constexpr int kAStages = AST;
   static constexpr int kBStages = BST;
   static constexpr int kRingBytes = AST * kAStageBytes + BST * kBBytes;
   static_assert(kRingBytes <= kRingMax, "ring exceeds shared memory");
-  static constexpr int kSlots = kTmemCols / BN;  // accumulator slots
+  static constexpr int kSlots = kTmemColsCta / BN;  // accumulator slots
   static constexpr int kRowTabBytes = GMAX * 128 * 8;  // LSU A path: source row offsets of a group
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kRingBytes + 512 /*barriers*/ + kRowTabBytes;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may opt in to");
+  static_assert(CPS == 1 || kSmemBytes + 1024 <= 233472 / 2, "two CTAs must fit in one SM's shared memory");
 };
 
 enum GemmMode : int { kStage1 = 0, kStage2Pad = 1, kStage2Comb = 2 };
@@ -110,6 +118,8 @@ struct GemmArgs {
   // Stage1 with kAGather: the epilogue warps first zero this buffer (the Stage2 combine target)
   void* zero_ptr;
   long long zero_bytes;
+
+  int b_evict_first;          // weight loads with the L2 evict_first policy
 
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
@@ -305,11 +315,11 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS>
+__global__ void __launch_bounds__(kThreads, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  using RingT = Ring<BN, GMAX, AST, BST>;
+  using RingT = Ring<BN, GMAX, AST, BST, CPS>;
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kSlots = RingT::kSlots;
@@ -358,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (MODE == kStage1) tma_prefetch_desc(&tmB1);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, RingT::kTmemColsCta);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -383,8 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int depth = is_b ? BST : AST;
       uint64_t* full = is_b ? fullB : fullA;
       uint64_t* empty = is_b ? emptyB : emptyA;
-      const uint64_t pol = is_b ? l2_policy_evict_normal()
-                                : l2_policy_evict_last();  // token rows: re-read by every column tile
+      // weights: evict_normal (args.b_evict_first: evict_first); token rows: evict_last (re-read by
+      // every column tile)
+      const uint64_t pol = is_b ? (args.b_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal())
+                                : l2_policy_evict_last();
       const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
       int st = 0;
       uint32_t ph = 0;
@@ -581,7 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, RingT::kTmemColsCta);
   }
 }
 
