@@ -477,6 +477,78 @@ def bench_ep(args, world, rank, local):
         }), flush=True)
 
 
+# ----------------------------------------------------------------------------- contest cases
+# The reference's own benchmark shapes (初审材料/源代码/benchmark/remote_bench.py:21-29, cases 1-3) and
+# its published C500 times for them: v755 on the judge (xpuoj_data/oj_submission_record_v755_8033.json,
+# README.md:62-66) and the judge's PyTorch baseline T_b (OJ_最终提交_SPJ报告.md:11,22,33).
+CONTEST = {
+    1: dict(experts=16, hidden=2048, intermediate=8192, valid=2272, high_experts=8, low_size=124,
+            c500_ms=2.544, c500_torch_ms=11.251),
+    2: dict(experts=32, hidden=7168, intermediate=2048, valid=4544, high_experts=22, low_size=112,
+            c500_ms=4.520, c500_torch_ms=18.610),
+    3: dict(experts=64, hidden=7168, intermediate=2048, valid=9088, high_experts=23, low_size=127,
+            c500_ms=8.926, c500_torch_ms=35.875),
+}
+
+
+def contest_group_sizes(c):
+    """remote_bench.py:60-75: low-size experts and high experts, interleaved."""
+    high, low = c["high_experts"], c["experts"] - c["high_experts"]
+    sizes = [c["low_size"]] * low
+    q, r = divmod(c["valid"] - sum(sizes), high)
+    sizes += [q + (i < r) for i in range(high)]
+    return sizes[::2] + sizes[1::2]
+
+
+def bench_run_kernel(args):
+    """The reference drop-in (run_kernel) on the reference's own contest cases, one GPU."""
+    import math
+
+    import muxi_race_b200 as m
+
+    c = CONTEST[args.case]
+    dev = torch.device("cuda", 0)
+    E, H, I = c["experts"], c["hidden"], c["intermediate"]
+    gs = torch.tensor(contest_group_sizes(c), dtype=torch.int32)
+    go = torch.cat([torch.zeros(1, dtype=torch.int32), torch.cumsum(gs, 0, dtype=torch.int32)])
+    padded = (gs + 127) // 128 * 128
+    gpo = torch.cat([torch.zeros(1, dtype=torch.int32), torch.cumsum(padded, 0, dtype=torch.int32)])
+    gidx = torch.repeat_interleave(torch.arange(E, dtype=torch.int32), padded // 128)
+    P = int(gpo[-1])
+    g = torch.Generator(device=dev).manual_seed(args.case)
+    x = torch.randn((P, H), generator=g, device=dev).half()
+    gate = (torch.randn((E, I, H), generator=g, device=dev) / math.sqrt(I)).half()
+    up = (torch.randn((E, I, H), generator=g, device=dev) / math.sqrt(I)).half()
+    down = (torch.randn((E, H, I), generator=g, device=dev) / math.sqrt(H)).half()
+    routed = torch.rand((c["valid"],), generator=g, device=dev)
+    meta = [t.to(dev) for t in (gs, go, gpo, gidx)]
+    out = torch.empty((P, H), dtype=torch.float16, device=dev)
+    for _ in range(args.warmup):
+        m.run_kernel(x, gate, up, down, routed, *meta, out)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        m.run_kernel(x, gate, up, down, routed, *meta, out)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    flops = 2.0 * c["valid"] * 3 * H * I
+    wbytes = E * 3 * H * I * 2
+    peaks, kind = load_peaks()
+    print(json.dumps({
+        "metric": f"run_kernel ms/call, contest case {args.case}", "value": round(ms, 4), "unit": "ms",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
+        "config": {"workload": f"reference drop-in run_kernel, contest case {args.case}: E={E} H={H} I={I} "
+                               f"valid rows={c['valid']} padded rows={P}", "dtype": "fp16"},
+        "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+        "roofline_ms": round(max(flops / (peaks['bf16_tflops'] * 1e12), (wbytes + 2 * P * H * 2) / (peaks["hbm_gbs"] * 1e9)) * 1e3, 4),
+        "reference_c500": {"ms": c["c500_ms"], "judge_torch_ms": c["c500_torch_ms"],
+                           "note": "published MetaX C500 times of the reference's final operator and the judge's "
+                                   "PyTorch baseline on the same shapes (different hardware)"},
+    }), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def bench_reference(args, world, rank):
     """The reference's CPU operator (oracle port of its PyTorch implementation) on the host cores."""
@@ -524,8 +596,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
+                    help="run_kernel: the reference drop-in on the reference's contest case --case")
+    ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.path == "run_kernel":
+        bench_run_kernel(args)
+        return
     if args.impl == "reference":
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         bench_reference(args, world, rank)

@@ -149,21 +149,26 @@ size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 // ------------------------------------------------------------------ GEMM launch
 // Tile configurations: accumulator width per block, blocks per work unit, A / B ring depths.
 // MOE_B200_TILE selects one by name for experiments; the default is the fastest measured.
-enum TileCfg { kT256A4B5 = 0, kT256x2A2B4, kT512A2B3, kT256A2B2C2, kT256A2B6, kNumTileCfg };
-const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a2b4", "512a2b3", "256a2b2c2", "256a2b6"};
+enum TileCfg { kT256A4B5 = 0, kT256x2A3B4, kT512A2B3, kT256A2B2C2, kT256A6B4, kNumTileCfg };
+const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a3b4", "512a2b3", "256a2b2c2", "256a6b4"};
 
-TileCfg tile_cfg() {
-  static const TileCfg t = [] {
-    const char* v = getenv("MOE_B200_TILE");
-    if (v)
-      for (int i = 0; i < kNumTileCfg; ++i)
-        if (strcmp(v, kTileNames[i]) == 0) return static_cast<TileCfg>(i);
-    return kT256A4B5;
-  }();
-  return t;
+// Per stage: Stage1 (K = H long, one token block per unit) measured fastest with 256a4b5; Stage2
+// (K = I short) with two-block groups, whose single weight stream per expert removes the DRAM
+// re-reads of experts spanning two blocks (cfg3 Stage2 1.38 vs 1.56 ms). MOE_B200_TILE sets both
+// stages, MOE_B200_TILE1 / MOE_B200_TILE2 one stage each.
+TileCfg parse_tile(const char* v, TileCfg dflt) {
+  if (v)
+    for (int i = 0; i < kNumTileCfg; ++i)
+      if (strcmp(v, kTileNames[i]) == 0) return static_cast<TileCfg>(i);
+  return dflt;
+}
+TileCfg tile_cfg(int stage) {
+  static const TileCfg t1 = parse_tile(getenv("MOE_B200_TILE1"), parse_tile(getenv("MOE_B200_TILE"), kT256A4B5));
+  static const TileCfg t2 = parse_tile(getenv("MOE_B200_TILE2"), parse_tile(getenv("MOE_B200_TILE"), kT256x2A3B4));
+  return stage == 1 ? t1 : t2;
 }
 int cfg_bn(TileCfg c) { return c == kT512A2B3 ? 512 : 256; }
-int cfg_gmax(TileCfg c) { return c == kT256x2A2B4 ? 2 : 1; }
+int cfg_gmax(TileCfg c) { return c == kT256x2A3B4 ? 2 : 1; }
 
 // How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu.
 bool a_path_lsu() {
@@ -185,7 +190,7 @@ int launch_gemm(int dev, int tcfg, const CUtensorMap& a, const CUtensorMap& b0, 
   GemmArgs args_l = args;
   args_l.b_evict_first = evict_first;
   const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3 + AMODE;
-  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS>::kSmemBytes;
+  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
@@ -201,14 +206,17 @@ template <int MODE, typename OutT, bool I8, int AMODE>
 int launch_stage(TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                  const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   switch (c) {
-    case kT256x2A2B4:
-      return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+    case kT256x2A3B4:  // the LSU A path's row table does not fit next to this ring: 2-deep A there
+      if constexpr (AMODE == kATma)
+        return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+      else
+        return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
     case kT512A2B3:
       return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
     case kT256A2B2C2:
       return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2>(dev, c, a, b0, b1, args, max_tiles, stream);
-    case kT256A2B6:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 6, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+    case kT256A6B4:
+      return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
     default:
       return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
   }
@@ -394,28 +402,28 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   void* U = workspace;
   int32_t* groups = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + run_kernel_u_bytes(P, I));
   int32_t* ngroups = groups + nblk;
-  const TileCfg tc = tile_cfg();
-  const int bn = cfg_bn(tc), gmax = cfg_gmax(tc);
+  const TileCfg tc1 = tile_cfg(1), tc2 = tile_cfg(2);
+  const int bn1 = cfg_bn(tc1), gmax1 = cfg_gmax(tc1), bn2 = cfg_bn(tc2), gmax2 = cfg_gmax(tc2);
 
   CUtensorMap tA, tG, tU, tUA, tD;
   MOE_TRY(make_tmap(&tA, x, 2, P, H, kBM, "stacked_expert_tokens"));
-  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, bn / 2, "gate_w"));
-  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, bn / 2, "up_w"));
+  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, bn1 / 2, "gate_w"));
+  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, bn1 / 2, "up_w"));
   MOE_TRY(make_tmap(&tUA, U, 2, P, I, kBM, "workspace"));
   MOE_TRY(make_tmap(&tD, down_w, 2, E * H, I, kMmaN, "down_w"));
 
-  if (gmax > 1) {  // pair each expert's blocks (from group_padded_offsets)
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, gmax, groups, ngroups);
+  if (gmax1 > 1 || gmax2 > 1) {  // pair each expert's blocks (from group_padded_offsets)
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
   }
 
   GemmArgs a1{};
   a1.K = (int)H;
   a1.N = (int)I;
-  a1.n_tiles = (int)((I + bn / 2 - 1) / (bn / 2));
-  a1.ngroups = gmax > 1 ? -1 : (int)nblk;
+  a1.n_tiles = (int)((I + bn1 / 2 - 1) / (bn1 / 2));
+  a1.ngroups = gmax1 > 1 ? -1 : (int)nblk;
   a1.ngroups_dev = ngroups;
-  a1.groups = gmax > 1 ? groups : nullptr;
+  a1.groups = gmax1 > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
   a1.b_rows_per_expert = (int)I;
@@ -427,7 +435,9 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   GemmArgs a2 = a1;
   a2.K = (int)I;
   a2.N = (int)H;
-  a2.n_tiles = (int)((H + bn - 1) / bn);
+  a2.n_tiles = (int)((H + bn2 - 1) / bn2);
+  a2.ngroups = gmax2 > 1 ? -1 : (int)nblk;
+  a2.groups = gmax2 > 1 ? groups : nullptr;
   a2.b_rows_per_expert = (int)H;
   a2.U = nullptr;
   a2.out = out;
@@ -445,8 +455,8 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a2.a_ptr = U;
   a2.a_row_bytes = I * 2;
   const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
-  MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc, dev, tA, tG, tU, a1, tiles1, s)));
-  MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc, dev, tUA, tD, tD, a2, tiles2, s)));
+  MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc1, dev, tA, tG, tU, a1, tiles1, s)));
+  MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc2, dev, tUA, tD, tD, a2, tiles2, s)));
   return MOE_OK;
 }
 
@@ -557,14 +567,14 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   void* U = ws + L.u;
   int32_t* groups = reinterpret_cast<int32_t*>(ws + L.groups);
   int32_t* ngroups = groups + L.nblk_max;
-  const TileCfg tc = tile_cfg();
-  const int bn = cfg_bn(tc), gmax = cfg_gmax(tc);
+  const TileCfg tc1 = tile_cfg(1), tc2 = tile_cfg(2);
+  const int bn1 = cfg_bn(tc1), gmax1 = cfg_gmax(tc1), bn2 = cfg_bn(tc2), gmax2 = cfg_gmax(tc2);
 
   // 1. routing metadata
   prof_record(0, s);
   MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s));
-  if (gmax > 1) {
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, gmax, groups, ngroups);
+  if (gmax1 > 1 || gmax2 > 1) {
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
   }
   prof_record(1, s);
@@ -616,7 +626,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   const void* a1_src = lsu ? (int8 ? static_cast<const void*>(xs) : x) : xs;
   void* a2_src = int8 ? (void*)(ws + L.uq) : U;
   CUtensorMap tA, tW13, tUA, tW2;
-  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, bn / 2, "w_gate_up"));
+  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, bn1 / 2, "w_gate_up"));
   MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kMmaN, "w_down"));
   if (lsu) {  // the LSU path does not use the A tensor maps
     tA = tW13;
@@ -629,10 +639,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   GemmArgs a1{};
   a1.K = (int)H;
   a1.N = (int)I;
-  a1.n_tiles = (int)((I + bn / 2 - 1) / (bn / 2));
+  a1.n_tiles = (int)((I + bn1 / 2 - 1) / (bn1 / 2));
   a1.ngroups = -1;
-  a1.ngroups_dev = gmax > 1 ? ngroups : meta + 1;
-  a1.groups = gmax > 1 ? groups : nullptr;
+  a1.ngroups_dev = gmax1 > 1 ? ngroups : meta + 1;
+  a1.groups = gmax1 > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
   a1.b_rows_per_expert = (int)(2 * I);
@@ -655,10 +665,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   GemmArgs a2{};
   a2.K = (int)I;
   a2.N = (int)H;
-  a2.n_tiles = (int)((H + bn - 1) / bn);
+  a2.n_tiles = (int)((H + bn2 - 1) / bn2);
   a2.ngroups = -1;
-  a2.ngroups_dev = gmax > 1 ? ngroups : meta + 1;
-  a2.groups = gmax > 1 ? groups : nullptr;
+  a2.ngroups_dev = gmax2 > 1 ? ngroups : meta + 1;
+  a2.groups = gmax2 > 1 ? groups : nullptr;
   a2.E = (int)E;
   a2.block_expert = gidx;
   a2.b_rows_per_expert = (int)H;
@@ -677,13 +687,13 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
-    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, tA, tW13, tW13, a1, max_tiles1, s)));
     prof_record(3, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(4, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
-    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc1, dev, tA, tW13, tW13, a1, max_tiles1, s)));
     prof_record(3, s);
     if (dtype == MOE_F16)
       quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
@@ -695,7 +705,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
           reinterpret_cast<float*>(ws + L.uscale));
     MOE_CUDA(cudaGetLastError());
     prof_record(4, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc2, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
     prof_record(5, s);
   }
   return MOE_OK;

@@ -56,7 +56,7 @@ constexpr int kRingMax = 224 * 1024;
 
 // Shared-memory rings: A (token rows, mostly L2 hits) and B (expert weights, streamed from HBM)
 // have separate depths, so the weight stream can run further ahead than the A stream.
-template <int BN, int GMAX, int AST, int BST, int CPS = 1> struct Ring {
+template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false> struct Ring {
   static_assert(BN == 256 || BN == 512, "accumulator width");
   static_assert(CPS == 1 || CPS == 2, "CTAs per SM");
   static constexpr int kTmemColsCta = kTmemCols / CPS;  // TMEM columns this CTA allocates
@@ -68,7 +68,7 @@ template <int BN, int GMAX, int AST, int BST, int CPS = 1> struct Ring {
   static constexpr int kRingBytes = AST * kAStageBytes + BST * kBBytes;
   static_assert(kRingBytes <= kRingMax, "ring exceeds shared memory");
   static constexpr int kSlots = kTmemColsCta / BN;  // accumulator slots
-  static constexpr int kRowTabBytes = GMAX * 128 * 8;  // LSU A path: source row offsets of a group
+  static constexpr int kRowTabBytes = ROWTAB ? GMAX * 128 * 8 : 0;  // LSU A path: source row offsets
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kRingBytes + 512 /*barriers*/ + kRowTabBytes;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may opt in to");
   static_assert(CPS == 1 || kSmemBytes + 1024 <= 233472 / 2, "two CTAs must fit in one SM's shared memory");
@@ -319,7 +319,7 @@ template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BS
 __global__ void __launch_bounds__(kThreads, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  using RingT = Ring<BN, GMAX, AST, BST, CPS>;
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma>;
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kSlots = RingT::kSlots;

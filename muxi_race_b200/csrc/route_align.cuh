@@ -16,8 +16,9 @@
 // Three launches, all bit-exact (integer counting, no floating point, no order-dependent atomics
 // in the placement):
 //   count    one warp per chunk of routes builds a per-chunk histogram (shared-memory atomics);
-//   scan     one CTA turns chunk histograms into per-chunk exclusive bases, sums and scans the
-//            expert totals, writes the offsets, block->expert map and padding sentinels;
+//   scan     one CTA turns the (expert-major) chunk histograms into per-chunk exclusive bases,
+//            one warp per expert row, then scans the expert totals and writes the offsets, the
+//            block->expert map and the padding sentinels;
 //   scatter  one warp per chunk walks its routes in order, 32 at a time; __match_any_sync groups
 //            equal ids, the rank inside a group is the popcount of lower lanes, so every route
 //            lands at base[e] + (routes to e before it).
@@ -47,11 +48,12 @@ __global__ void __launch_bounds__(kAlignWarps * 32)
       if (id >= 0 && id < E) atomicAdd(&h[id], 1);
     }
     __syncwarp();
-    for (int e = lane; e < E; e += 32) counts[static_cast<size_t>(c) * E + e] = h[e];
+    for (int e = lane; e < E; e += 32) counts[static_cast<size_t>(e) * n_chunks + c] = h[e];  // expert-major
   }
 }
 
-// One CTA of 1024 threads. counts[c][e] becomes the exclusive prefix over chunks.
+// One CTA of 1024 threads. counts[e][c] (expert-major) becomes the exclusive prefix over chunks:
+// each warp scans one expert's chunk row at a time, each lane a contiguous segment of it.
 __global__ void __launch_bounds__(1024)
     align_scan_kernel(int* __restrict__ counts, int n_chunks, int E, int block_m, int R, int32_t* __restrict__ group_sizes,
                       int32_t* __restrict__ group_offsets, int32_t* __restrict__ group_padded_offsets,
@@ -61,21 +63,34 @@ __global__ void __launch_bounds__(1024)
   __shared__ int s_pad[kAlignMaxExperts];
   __shared__ int s_wsum[2][32];
   const int tid = threadIdx.x;
+  const int lane = tid & 31, w = tid >> 5;
   // 1. per-expert totals and per-chunk exclusive bases
-  for (int e = tid; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      int* p = counts + static_cast<size_t>(c) * E + e;
-      const int v = *p;
-      *p = run;
+  const int seg = (n_chunks + 31) / 32;
+  for (int e = w; e < E; e += 32) {
+    int* row = counts + static_cast<size_t>(e) * n_chunks;
+    const int c0 = min(lane * seg, n_chunks), c1 = min(c0 + seg, n_chunks);
+    int sum = 0;
+    for (int c = c0; c < c1; ++c) sum += row[c];
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - sum;
+    for (int c = c0; c < c1; ++c) {
+      const int v = row[c];
+      row[c] = run;
       run += v;
     }
-    s_tot[e] = run;
-    s_pad[e] = (run + block_m - 1) / block_m * block_m;
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    if (lane == 0) {
+      s_tot[e] = total;
+      s_pad[e] = (total + block_m - 1) / block_m * block_m;
+    }
   }
   __syncthreads();
   // 2. exclusive scans of totals and padded totals over E <= 1024 (one element per thread)
-  const int lane = tid & 31, w = tid >> 5;
   const int tot = tid < E ? s_tot[tid] : 0;
   const int pad = tid < E ? s_pad[tid] : 0;
   int it = tot, ip = pad;  // inclusive warp scans
@@ -142,7 +157,7 @@ __global__ void __launch_bounds__(kAlignWarps * 32)
   const int c = blockIdx.x * kAlignWarps + w;
   if (c >= n_chunks) return;
   int* b = base + w * E;
-  for (int e = lane; e < E; e += 32) b[e] = counts[static_cast<size_t>(c) * E + e] + group_padded_offsets[e];
+  for (int e = lane; e < E; e += 32) b[e] = counts[static_cast<size_t>(e) * n_chunks + c] + group_padded_offsets[e];
   __syncwarp();
   const unsigned lt_mask = (1u << lane) - 1u;
   const int start = c * chunk;
