@@ -70,6 +70,15 @@ MOE_API int moe_device_status(void* stream, int clear, uint32_t* status_out);
  * Events beyond n are not recorded. events = NULL or n = 0 turns the hook off. */
 MOE_API int moe_set_profile_events(void* const* events, int n);
 
+/* Tuning hook, no reference counterpart (the reference picks TileLang tiles per shape in
+ * _pick_tiles, 初审材料/源代码/submission.py:1990-2079). Selects the grouped-GEMM tile
+ * configuration of `stage` (1 = gate/up, 2 = down, 0 = both) by name for all later calls in the
+ * process, e.g. "256a4b5" (single CTA, 256 accumulator columns, A/B ring depths 4/5) or
+ * "p256a6b8" (CTA pair, cta_group::2); NULL or "auto" restores the per-call choice. Unknown names
+ * return MOE_ERR_INVALID_ARG. Configurations a call cannot run (e.g. shapes that do not split
+ * into whole k-blocks) fall back to the stage's single-CTA default. */
+MOE_API int moe_set_tile(int stage, const char* name);
+
 /* ------------------------------------------------------------------------------------------
  * Reference drop-in: the contest operator.
  * Replaces run_kernel(stacked_expert_tokens, gate_w, up_w, down_w, routed_expert_weights,

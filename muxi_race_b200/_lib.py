@@ -33,6 +33,7 @@ SIGNATURES = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_device_status": (_int, [_c_void_p, _int, ctypes.POINTER(ctypes.c_uint32)]),
     "moe_set_profile_events": (_int, [ctypes.POINTER(_c_void_p), _int]),
+    "moe_set_tile": (_int, [_int, ctypes.c_char_p]),
     "moe_run_kernel_workspace_bytes": (_size, [_i64, _i64, _int]),
     "moe_run_kernel": (
         _int,
@@ -122,3 +123,9 @@ def set_profile_events(events) -> None:
 
 
 _prof_array = None
+
+
+def set_tile(stage: int, name) -> None:
+    """Force the grouped-GEMM tile configuration of `stage` (1, 2, or 0 for both) by name for all
+    later calls of the process; None or "auto" restores the per-call choice."""
+    call("moe_set_tile", int(stage), None if name is None else str(name).encode())

@@ -16,6 +16,7 @@
 #include "ep_kernels.cuh"
 #include "gather_quant.cuh"
 #include "moe_gemm.cuh"
+#include "moe_gemm_pair.cuh"
 #include "route_align.cuh"
 
 namespace moe {
@@ -61,7 +62,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   std::atomic<int> sms{0};
   std::atomic<uint32_t*> status{nullptr};
-  std::atomic<uint64_t> attr_done[4] = {};  // bit per kernel whose smem attribute has been raised
+  std::atomic<uint64_t> attr_done[16] = {};  // bit per kernel whose smem attribute has been raised
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -114,21 +115,31 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// Row-major [rows, cols] matrix, box = box_rows x (128 bytes), 128-byte swizzle (matches the
-// kernels' shared-memory descriptors).
-int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, int64_t cols, int box_rows,
-              const char* what) {
+// A grouped-GEMM tile configuration: accumulator columns per block (bn), blocks per work unit
+// (gmax), A / B ring depths, CTAs per SM and k-blocks per weight box (kpb).
+struct TileInfo {
+  const char* name;
+  int bn, gmax, ast, bst, cps, kpb;
+  int pair;  // 1: CTA-pair kernel (cta_group::2), 256-row units, each CTA loads half the weights
+};
+
+// Tiled map over a tensor of `rank` dimensions (dims[0] innermost, in elements; strides of dims
+// 1..rank-1 in bytes), 128-byte swizzle (matches the kernels' shared-memory descriptors).
+int encode_map(CUtensorMap* map, const void* base, int elt_bytes, int rank, const cuuint64_t* dims,
+               const cuuint64_t* strides, const cuuint32_t* box, const char* what) {
   auto enc = get_encode();
   if (!enc) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return fail(MOE_ERR_ALIGNMENT, "%s is not 16-byte aligned", what);
-  if ((cols * elt_bytes) % 16 != 0) return fail(MOE_ERR_ALIGNMENT, "%s row pitch is not a multiple of 16 bytes", what);
-  if (rows <= 0 || rows > (int64_t(1) << 31) - 1 || cols <= 0 || cols > (int64_t(1) << 31) - 1)
-    return fail(MOE_ERR_INVALID_ARG, "%s has unsupported extent %lld x %lld", what, (long long)rows, (long long)cols);
+  for (int i = 0; i < rank; ++i)
+    if (dims[i] == 0 || dims[i] > (cuuint64_t(1) << 31) - 1)
+      return fail(MOE_ERR_INVALID_ARG, "%s has unsupported extent %llu in dimension %d", what,
+                  (unsigned long long)dims[i], i);
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides[i] % 16 != 0 || strides[i] >= (cuuint64_t(1) << 40))
+      return fail(MOE_ERR_ALIGNMENT, "%s stride %llu is not a multiple of 16 bytes below 2^40", what,
+                  (unsigned long long)strides[i]);
   const CUtensorMapDataType dt = elt_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * elt_bytes)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBytes / elt_bytes), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   static const CUtensorMapL2promotion promo = [] {
     const char* v = getenv("MOE_B200_L2_PROMO");  // experiments: none | 64 | 128 | 256 (default)
     if (v && strcmp(v, "none") == 0) return CU_TENSOR_MAP_L2_PROMOTION_NONE;
@@ -136,39 +147,170 @@ int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, i
     if (v && strcmp(v, "128") == 0) return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
     return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
   }();
-  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  CUresult r = enc(map, dt, rank, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with %d", what, (int)r);
   return MOE_OK;
+}
+
+// Row-major [rows, cols] matrix, box = box_rows x (128 bytes).
+int make_tmap(CUtensorMap* map, const void* base, int elt_bytes, int64_t rows, int64_t cols, int box_rows,
+              const char* what) {
+  if ((cols * elt_bytes) % 16 != 0) return fail(MOE_ERR_ALIGNMENT, "%s row pitch is not a multiple of 16 bytes", what);
+  if (rows <= 0 || cols <= 0) return fail(MOE_ERR_INVALID_ARG, "%s has an empty extent", what);
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * elt_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kKBytes / elt_bytes), static_cast<cuuint32_t>(box_rows)};
+  return encode_map(map, base, elt_bytes, 2, dims, strides, box, what);
 }
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// ------------------------------------------------------------------ GEMM launch
-// Tile configurations: accumulator width per block, blocks per work unit, A / B ring depths.
-// MOE_B200_TILE selects one by name for experiments; the default is the fastest measured.
-enum TileCfg { kT256A4B5 = 0, kT256x2A3B4, kT512A2B3, kT256A2B2C2, kT256A6B4, kNumTileCfg };
-const char* const kTileNames[kNumTileCfg] = {"256a4b5", "256x2a3b4", "512a2b3", "256a2b2c2", "256a6b4"};
+// Tensor maps of one GEMM stage (see moe_gemm_kernel) and how the weight maps are laid out.
+struct StageMaps {
+  CUtensorMap a, a1, b0, b1;
+  int b_split = 0;        // Stage1: gate and up rows as two maps (two boxes per k-block)
+  int gu_swap = 0;        // Stage1 combined map based at the up rows
+  int b1_row_offset = 0;  // Stage1 split: row offset of the up rows inside map b1
+};
 
-// Per stage: Stage1 (K = H long, one token block per unit) measured fastest with 256a4b5; Stage2
-// (K = I short) with two-block groups, whose single weight stream per expert removes the DRAM
-// re-reads of experts spanning two blocks (cfg3 Stage2 1.38 vs 1.56 ms). MOE_B200_TILE sets both
-// stages, MOE_B200_TILE1 / MOE_B200_TILE2 one stage each.
+// A operand: one box per block group (gmax x 128 rows) and one per block.
+int make_a_maps(StageMaps* m, const void* base, int elt, int64_t rows, int64_t K, int gmax, const char* what) {
+  const int box = (gmax > 1 && rows >= gmax * kBM) ? gmax * kBM : kBM;  // fewer rows: no multi-block group
+  MOE_TRY(make_tmap(&m->a, base, elt, rows, K, box, what));
+  if (box != kBM) {
+    MOE_TRY(make_tmap(&m->a1, base, elt, rows, K, kBM, what));
+  } else {
+    m->a1 = m->a;
+  }
+  return MOE_OK;
+}
+
+// Weights of a reduction length K stored as rows of K elements: one box of box_rows rows covers
+// kpb consecutive 128-byte k-blocks (a k-block dimension of stride 128 bytes) when kpb > 1.
+int make_w_map(CUtensorMap* map, const void* w, int elt, int64_t rows, int64_t K, int box_rows, int kpb,
+               const char* what) {
+  if (kpb == 1) return make_tmap(map, w, elt, rows, K, box_rows, what);
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kKBytes / elt), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(K * elt / kKBytes)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K * elt), static_cast<cuuint64_t>(kKBytes)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kKBytes / elt), static_cast<cuuint32_t>(box_rows),
+                             static_cast<cuuint32_t>(kpb)};
+  return encode_map(map, w, elt, 3, dims, strides, box, what);
+}
+
+// Stage1 weights. Gate row r is at gate + r * K * elt and up row r at up + r * K * elt, for
+// r < rows_gu. When the byte distance between the two is a multiple of 16 below 2^40, one map
+// whose third dimension steps from the lower of the two to the other loads a tile's gate and up
+// rows as one box (every address it forms is a row of one of the two tensors); otherwise two maps
+// over split_gate / split_up (split_rows rows each, up rows at split_up_offset inside the second).
+int make_stage1_weights(StageMaps* m, const void* gate, const void* up, int elt, int64_t rows_gu, int64_t K,
+                        const TileInfo& t, const void* split_gate, const void* split_up, int64_t split_rows,
+                        int split_up_offset, const char* what) {
+  const uintptr_t g = reinterpret_cast<uintptr_t>(gate), u = reinterpret_cast<uintptr_t>(up);
+  const uint64_t dist = g < u ? u - g : g - u;
+  const int box_rows = t.bn / 2 < kMmaN ? t.bn / 2 : kMmaN;
+  static const bool force_split = [] {
+    const char* v = getenv("MOE_B200_B_SPLIT");  // experiments / tests: 1 = always two maps
+    return v && strcmp(v, "1") == 0;
+  }();
+  if (!force_split && dist != 0 && dist % 16 == 0 && dist < (uint64_t(1) << 40) && (K * elt) % 16 == 0) {
+    const void* lo = g < u ? gate : up;
+    int rc;
+    if (t.kpb == 1) {
+      const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows_gu), 2};
+      const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K * elt), dist};
+      const cuuint32_t box[3] = {static_cast<cuuint32_t>(kKBytes / elt), static_cast<cuuint32_t>(box_rows), 2};
+      rc = encode_map(&m->b0, lo, elt, 3, dims, strides, box, what);
+    } else {
+      const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kKBytes / elt), static_cast<cuuint64_t>(rows_gu), 2,
+                                  static_cast<cuuint64_t>(K * elt / kKBytes)};
+      const cuuint64_t strides[3] = {static_cast<cuuint64_t>(K * elt), dist, static_cast<cuuint64_t>(kKBytes)};
+      const cuuint32_t box[4] = {static_cast<cuuint32_t>(kKBytes / elt), static_cast<cuuint32_t>(box_rows), 2,
+                                 static_cast<cuuint32_t>(t.kpb)};
+      rc = encode_map(&m->b0, lo, elt, 4, dims, strides, box, what);
+    }
+    if (rc == MOE_OK) {
+      m->b1 = m->b0;
+      m->b_split = 0;
+      m->gu_swap = u < g ? 1 : 0;
+      return MOE_OK;
+    }
+  }
+  MOE_TRY(make_tmap(&m->b0, split_gate, elt, split_rows, K, box_rows, what));
+  MOE_TRY(make_tmap(&m->b1, split_up, elt, split_rows, K, box_rows, what));
+  m->b_split = 1;
+  m->gu_swap = 0;
+  m->b1_row_offset = split_up_offset;
+  return MOE_OK;
+}
+
+// ------------------------------------------------------------------ GEMM launch
+// Tile configurations: accumulator columns per block (BN), blocks per work unit (GMAX), A / B
+// ring depths, CTAs per SM and k-blocks per weight box (KPB). Names: <BN>[x<GMAX>]a<A>b<B>
+// [c<CPS>][k<KPB>]. MOE_B200_TILE selects one by name for experiments (both stages),
+// MOE_B200_TILE1 / MOE_B200_TILE2 one stage each.
+enum TileCfg {
+  kT256A4B5 = 0,
+  kT256x2A3B4,
+  kT512A2B3,
+  kT256A2B2C2,
+  kT256A6B4,
+  kT256A6B2K2,
+  kT128x2A3B4K2,
+  kT128x2A4B3K2,
+  kT128x2A3B8,
+  kT256x2A3B2K2,
+  kTP256A6B8,
+  kTP256A7B7,
+  kTP256A4B10,
+  kNumTileCfg
+};
+constexpr TileInfo kTiles[kNumTileCfg] = {
+    {"256a4b5", 256, 1, 4, 5, 1, 1, 0},     {"256x2a3b4", 256, 2, 3, 4, 1, 1, 0},
+    {"512a2b3", 512, 1, 2, 3, 1, 1, 0},     {"256a2b2c2", 256, 1, 2, 2, 2, 1, 0},
+    {"256a6b4", 256, 1, 6, 4, 1, 1, 0},     {"256a6b2k2", 256, 1, 6, 2, 1, 2, 0},
+    {"128x2a3b4k2", 128, 2, 3, 4, 1, 2, 0}, {"128x2a4b3k2", 128, 2, 4, 3, 1, 2, 0},
+    {"128x2a3b8", 128, 2, 3, 8, 1, 1, 0},   {"256x2a3b2k2", 256, 2, 3, 2, 1, 2, 0},
+    {"p256a6b8", 256, 2, 6, 8, 1, 1, 1},    {"p256a7b7", 256, 2, 7, 7, 1, 1, 1},
+    {"p256a4b10", 256, 2, 4, 10, 1, 1, 1},
+};
+static_assert(kNumTileCfg * 36 <= 64 * 16, "smem attribute bits");
+
+// Defaults per stage, chosen per call from the average number of 128-row blocks per expert
+// (measured on B200): with about 1.8 or more blocks per expert most blocks belong to two-block
+// groups, and the CTA-pair kernel (p256a6b8), whose pair streams each weight tile once for both
+// blocks, is faster (cfg2 Stage1 0.65 vs 0.73 ms, Stage2 0.32 vs 0.36 ms); with fewer, the
+// one-block groups leave half of each pair idle (cfg3 at T = 128: Stage1 3.24 vs 2.32 ms) and the
+// single-CTA kernels win: Stage1 256a4b5, Stage2 256x2a3b4 (two-block groups sharing one weight
+// stream, cfg3 Stage2 1.38 vs 1.56 ms for 256a4b5). MOE_B200_TILE / MOE_B200_TILE1 /
+// MOE_B200_TILE2 override the choice with a configuration name.
 TileCfg parse_tile(const char* v, TileCfg dflt) {
   if (v)
     for (int i = 0; i < kNumTileCfg; ++i)
-      if (strcmp(v, kTileNames[i]) == 0) return static_cast<TileCfg>(i);
+      if (strcmp(v, kTiles[i].name) == 0) return static_cast<TileCfg>(i);
   return dflt;
 }
+constexpr TileCfg kDefaultTile1 = kT256A4B5, kDefaultTile2 = kT256x2A3B4, kDefaultPair = kTP256A6B8;
+constexpr double kPairBlocksPerExpert = 1.8;
+constexpr TileCfg kAuto = kNumTileCfg;
+// Selected configuration per stage (kAuto = per-call choice): environment at first use,
+// moe_set_tile afterwards.
+std::atomic<int> g_tile_sel[2] = {{-1}, {-1}};
 TileCfg tile_cfg(int stage) {
-  static const TileCfg t1 = parse_tile(getenv("MOE_B200_TILE1"), parse_tile(getenv("MOE_B200_TILE"), kT256A4B5));
-  static const TileCfg t2 = parse_tile(getenv("MOE_B200_TILE2"), parse_tile(getenv("MOE_B200_TILE"), kT256x2A3B4));
-  return stage == 1 ? t1 : t2;
+  std::atomic<int>& sel = g_tile_sel[stage == 1 ? 0 : 1];
+  int v = sel.load(std::memory_order_acquire);
+  if (v < 0) {
+    const TileCfg env = parse_tile(getenv(stage == 1 ? "MOE_B200_TILE1" : "MOE_B200_TILE2"),
+                                   parse_tile(getenv("MOE_B200_TILE"), kAuto));
+    int expected = -1;
+    sel.compare_exchange_strong(expected, static_cast<int>(env), std::memory_order_acq_rel);
+    v = sel.load(std::memory_order_acquire);
+  }
+  return static_cast<TileCfg>(v);
 }
-int cfg_bn(TileCfg c) { return c == kT512A2B3 ? 512 : 256; }
-int cfg_gmax(TileCfg c) { return c == kT256x2A3B4 ? 2 : 1; }
 
 // How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu.
 bool a_path_lsu() {
@@ -179,58 +321,146 @@ bool a_path_lsu() {
   return v;
 }
 
-template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS = 1>
-int launch_gemm(int dev, int tcfg, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS>;
+// The configuration a stage runs with for reduction length K (elements of elt bytes), given the
+// average number of 128-row blocks per expert: the environment's choice if any, else the
+// per-call default. A weight box spanning KPB k-blocks needs whole k-blocks (K * elt a multiple
+// of 128 bytes) in multiples of KPB; BN = 128 is a Stage1 tile; the LSU A path (row table in
+// shared memory) runs the single-CTA KPB = 1, BN >= 256 configurations. Anything else falls back
+// to the stage's single-CTA default.
+TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_expert) {
+  const TileCfg single = stage == 1 ? kDefaultTile1 : kDefaultTile2;
+  TileCfg c = tile_cfg(stage);
+  if (c == kAuto) c = (!lsu && blocks_per_expert >= kPairBlocksPerExpert) ? kDefaultPair : single;
+  const TileInfo& t = kTiles[c];
+  if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return single;
+  if (t.bn == 128 && stage != 1) return single;
+  if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair)) return single;
+  return c;
+}
+
+template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB>
+int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB>;
   static const int evict_first = [] {
     const char* v = getenv("MOE_B200_B_EVICT_FIRST");  // experiments: 1 = evict_first for weights
     return v && strcmp(v, "1") == 0 ? 1 : 0;
   }();
   GemmArgs args_l = args;
   args_l.b_evict_first = evict_first;
+  args_l.b_split = m.b_split;
+  args_l.gu_swap = m.gu_swap;
+  if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
   const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3 + AMODE;
-  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma>::kSmemBytes;
+  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma, KPB>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
   const int grid = max_tiles < sms * CPS ? max_tiles : sms * CPS;
   if (grid <= 0) return MOE_OK;
-  kern<<<grid, kThreads, smem, stream>>>(a, b0, b1, args_l);
+  kern<<<grid, kThreads, smem, stream>>>(m.a, m.a1, m.b0, m.b1, args_l);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+// CTA-pair kernel: clusters of two CTAs, one pair per two SMs (as many as can be resident).
+template <int MODE, typename OutT, bool I8, int AST, int BST>
+int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST>;
+  static const int evict_first = [] {
+    const char* v = getenv("MOE_B200_B_EVICT_FIRST");
+    return v && strcmp(v, "1") == 0 ? 1 : 0;
+  }();
+  GemmArgs args_l = args;
+  args_l.b_evict_first = evict_first;
+  args_l.b_split = 1;
+  args_l.gu_swap = 0;
+  args_l.b1_row_offset = m.b1_row_offset;
+  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3;
+  constexpr int smem = PairRing<AST, BST>::kSmemBytes;
+  MOE_TRY(raise_smem(dev, bit, kern, smem));
+  static int max_pairs[kMaxDevices] = {};
+  if (max_pairs[dev] == 0) {
+    int sms = 0;
+    MOE_TRY(device_sms(dev, &sms));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = sms / 2;
+    }
+    max_pairs[dev] = n;
+  }
+  const int pairs = max_tiles < max_pairs[dev] ? max_tiles : max_pairs[dev];
+  if (pairs <= 0) return MOE_OK;
+  kern<<<2 * pairs, kThreads, smem, stream>>>(m.a, m.b0, m.b1, args_l);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }
 
 // One grouped GEMM stage with the chosen tile configuration.
 template <int MODE, typename OutT, bool I8, int AMODE>
-int launch_stage(TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                 const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  constexpr bool kTma = AMODE == kATma;
+  constexpr bool kS1 = MODE == kStage1;
   switch (c) {
+    case kT256A4B5:
+      return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
     case kT256x2A3B4:  // the LSU A path's row table does not fit next to this ring: 2-deep A there
-      if constexpr (AMODE == kATma)
-        return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+      if constexpr (kTma)
+        return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
       else
-        return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+        return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
     case kT512A2B3:
-      return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+      return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
     case kT256A2B2C2:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2>(dev, c, a, b0, b1, args, max_tiles, stream);
+      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2, 1>(dev, c, m, args, max_tiles, stream);
     case kT256A6B4:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+      return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+    case kT256A6B2K2:
+      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 6, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kT128x2A3B4K2:
+      if constexpr (kTma && kS1)
+        return launch_gemm<MODE, OutT, I8, 128, 2, 3, 4, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kT128x2A4B3K2:
+      if constexpr (kTma && kS1)
+        return launch_gemm<MODE, OutT, I8, 128, 2, 4, 3, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kT128x2A3B8:
+      if constexpr (kTma && kS1)
+        return launch_gemm<MODE, OutT, I8, 128, 2, 3, 8, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kT256x2A3B2K2:
+      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kTP256A6B8:
+      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 6, 8>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kTP256A7B7:
+      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 7, 7>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kTP256A4B10:
+      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 4, 10>(dev, c, m, args, max_tiles, stream);
+      break;
     default:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE>(dev, c, a, b0, b1, args, max_tiles, stream);
+      break;
   }
+  return fail(MOE_ERR_UNSUPPORTED, "tile configuration %s is not available for this stage", kTiles[c].name);
 }
 
 // Stage dispatch over the runtime element type and A path.
 template <int MODE, bool I8, int AMODE_LSU>
-int launch_stage_rt(int dtype, bool lsu, TileCfg c, int dev, const CUtensorMap& a, const CUtensorMap& b0,
-                    const CUtensorMap& b1, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+int launch_stage_rt(int dtype, bool lsu, TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles,
+                    cudaStream_t stream) {
   if (dtype == MOE_F16)
-    return lsu ? launch_stage<MODE, __half, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
-               : launch_stage<MODE, __half, I8, kATma>(c, dev, a, b0, b1, args, max_tiles, stream);
-  return lsu ? launch_stage<MODE, __nv_bfloat16, I8, AMODE_LSU>(c, dev, a, b0, b1, args, max_tiles, stream)
-             : launch_stage<MODE, __nv_bfloat16, I8, kATma>(c, dev, a, b0, b1, args, max_tiles, stream);
+    return lsu ? launch_stage<MODE, __half, I8, AMODE_LSU>(c, dev, m, args, max_tiles, stream)
+               : launch_stage<MODE, __half, I8, kATma>(c, dev, m, args, max_tiles, stream);
+  return lsu ? launch_stage<MODE, __nv_bfloat16, I8, AMODE_LSU>(c, dev, m, args, max_tiles, stream)
+             : launch_stage<MODE, __nv_bfloat16, I8, kATma>(c, dev, m, args, max_tiles, stream);
 }
 
 // ------------------------------------------------------------------ align
@@ -334,6 +564,19 @@ const char* moe_version(void) { return "muxi_race_b200 0.1.0 (sm_100a)"; }
 
 const char* moe_last_error(void) { return t_last_error.c_str(); }
 
+int moe_set_tile(int stage, const char* name) {
+  t_last_error.clear();
+  if (stage < 0 || stage > 2) return fail(MOE_ERR_INVALID_ARG, "stage must be 0, 1 or 2");
+  TileCfg c = kAuto;
+  if (name != nullptr && strcmp(name, "auto") != 0) {
+    c = parse_tile(name, kAuto);
+    if (c == kAuto) return fail(MOE_ERR_INVALID_ARG, "unknown tile configuration '%s'", name);
+  }
+  for (int st = 1; st <= 2; ++st)
+    if (stage == 0 || stage == st) g_tile_sel[st - 1].store(static_cast<int>(c), std::memory_order_release);
+  return MOE_OK;
+}
+
 int moe_set_profile_events(void* const* events, int n) {
   t_prof_events = n > 0 ? events : nullptr;
   t_prof_n = n > 0 ? n : 0;
@@ -402,15 +645,25 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   void* U = workspace;
   int32_t* groups = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + run_kernel_u_bytes(P, I));
   int32_t* ngroups = groups + nblk;
-  const TileCfg tc1 = tile_cfg(1), tc2 = tile_cfg(2);
-  const int bn1 = cfg_bn(tc1), gmax1 = cfg_gmax(tc1), bn2 = cfg_bn(tc2), gmax2 = cfg_gmax(tc2);
+  const bool lsu = a_path_lsu();
+  const double bpe = static_cast<double>(nblk) / static_cast<double>(E);  // blocks per expert
+  const TileCfg tc1 = usable_cfg(1, H, 2, lsu, bpe), tc2 = usable_cfg(2, I, 2, lsu, bpe);
+  const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
+  const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
 
-  CUtensorMap tA, tG, tU, tUA, tD;
-  MOE_TRY(make_tmap(&tA, x, 2, P, H, kBM, "stacked_expert_tokens"));
-  MOE_TRY(make_tmap(&tG, gate_w, 2, E * I, H, bn1 / 2, "gate_w"));
-  MOE_TRY(make_tmap(&tU, up_w, 2, E * I, H, bn1 / 2, "up_w"));
-  MOE_TRY(make_tmap(&tUA, U, 2, P, I, kBM, "workspace"));
-  MOE_TRY(make_tmap(&tD, down_w, 2, E * H, I, kMmaN, "down_w"));
+  StageMaps m1, m2;
+  if (t1.pair) {  // each CTA of a pair loads 128 token rows and 128 weight rows per k-block
+    MOE_TRY(make_a_maps(&m1, x, 2, P, H, 1, "stacked_expert_tokens"));
+    MOE_TRY(make_tmap(&m1.b0, gate_w, 2, E * I, H, kBM, "gate_w"));
+    MOE_TRY(make_tmap(&m1.b1, up_w, 2, E * I, H, kBM, "up_w"));
+    m1.b1_row_offset = 0;
+  } else {
+    MOE_TRY(make_a_maps(&m1, x, 2, P, H, gmax1, "stacked_expert_tokens"));
+    MOE_TRY(make_stage1_weights(&m1, gate_w, up_w, 2, E * I, H, t1, gate_w, up_w, E * I, 0, "gate_w/up_w"));
+  }
+  MOE_TRY(make_a_maps(&m2, U, 2, P, I, t2.pair ? 1 : gmax2, "workspace"));
+  MOE_TRY(make_w_map(&m2.b0, down_w, 2, E * H, I, t2.pair ? kBM : (bn2 < kMmaN ? bn2 : kMmaN), t2.kpb, "down_w"));
+  m2.b1 = m2.b0;
 
   if (gmax1 > 1 || gmax2 > 1) {  // pair each expert's blocks (from group_padded_offsets)
     build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, groups, ngroups);
@@ -449,14 +702,13 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a2.routed_dtype = routed_dtype == MOE_F32 ? 0 : 1;
   a2.R = (int)R;
 
-  const bool lsu = a_path_lsu();
   a1.a_ptr = x;
   a1.a_row_bytes = H * 2;
   a2.a_ptr = U;
   a2.a_row_bytes = I * 2;
   const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
-  MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc1, dev, tA, tG, tU, a1, tiles1, s)));
-  MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc2, dev, tUA, tD, tD, a2, tiles2, s)));
+  MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc1, dev, m1, a1, tiles1, s)));
+  MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, tiles2, s)));
   return MOE_OK;
 }
 
@@ -567,8 +819,13 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   void* U = ws + L.u;
   int32_t* groups = reinterpret_cast<int32_t*>(ws + L.groups);
   int32_t* ngroups = groups + L.nblk_max;
-  const TileCfg tc1 = tile_cfg(1), tc2 = tile_cfg(2);
-  const int bn1 = cfg_bn(tc1), gmax1 = cfg_gmax(tc1), bn2 = cfg_bn(tc2), gmax2 = cfg_gmax(tc2);
+  const bool lsu = a_path_lsu();
+  const int elt = int8 ? 1 : 2;
+  // expected blocks per expert: routes per expert / 128, plus half a block of padding
+  const double bpe = static_cast<double>(R) / static_cast<double>(E) / kBM + 0.5;
+  const TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe), tc2 = usable_cfg(2, I, elt, lsu, bpe);
+  const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
+  const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
 
   // 1. routing metadata
   prof_record(0, s);
@@ -582,7 +839,6 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   // 2. activations: the TMA A path stacks the gathered token rows (int8: quantised per token)
   //    and zeroes the combine target; the LSU path gathers token rows inside Stage1 (int8: after
   //    an in-place per-token quantisation) and Stage1's epilogue warps zero the combine target
-  const bool lsu = a_path_lsu();
   const int gblocks = sms * 4;
   float* amax = int8 ? reinterpret_cast<float*>(ws + L.amax) : nullptr;
   float* xscale = int8 ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
@@ -622,18 +878,26 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   prof_record(2, s);
 
   // 3. Stage1 (gate/up GEMM + SiLU*up) and 4. Stage2 (down GEMM * topk weight, combine)
-  const int elt = int8 ? 1 : 2;
   const void* a1_src = lsu ? (int8 ? static_cast<const void*>(xs) : x) : xs;
   void* a2_src = int8 ? (void*)(ws + L.uq) : U;
-  CUtensorMap tA, tW13, tUA, tW2;
-  MOE_TRY(make_tmap(&tW13, w13, elt, 2 * E * I, H, bn1 / 2, "w_gate_up"));
-  MOE_TRY(make_tmap(&tW2, w2, elt, E * H, I, kMmaN, "w_down"));
-  if (lsu) {  // the LSU path does not use the A tensor maps
-    tA = tW13;
-    tUA = tW2;
+  StageMaps m1, m2;
+  const uint8_t* w13b = static_cast<const uint8_t*>(w13);
+  if (t1.pair) {  // gate rows and up rows (at +I) of the stacked weights, 128-row boxes
+    MOE_TRY(make_tmap(&m1.b0, w13, elt, 2 * E * I, H, kBM, "w_gate_up"));
+    m1.b1 = m1.b0;
+    m1.b1_row_offset = (int)I;
   } else {
-    MOE_TRY(make_tmap(&tA, xs, elt, L.P_max, H, kBM, "gathered hidden_states"));
-    MOE_TRY(make_tmap(&tUA, a2_src, elt, L.P_max, I, kBM, "intermediate"));
+    MOE_TRY(make_stage1_weights(&m1, w13, w13b + static_cast<size_t>(I) * H * elt, elt, 2 * E * I - I, H, t1, w13,
+                                w13, 2 * E * I, (int)I, "w_gate_up"));
+  }
+  MOE_TRY(make_w_map(&m2.b0, w2, elt, E * H, I, t2.pair ? kBM : (bn2 < kMmaN ? bn2 : kMmaN), t2.kpb, "w_down"));
+  m2.b1 = m2.b0;
+  if (lsu) {  // the LSU path does not use the A tensor maps
+    m1.a = m1.a1 = m1.b0;
+    m2.a = m2.a1 = m2.b0;
+  } else {
+    MOE_TRY(make_a_maps(&m1, xs, elt, L.P_max, H, t1.pair ? 1 : gmax1, "gathered hidden_states"));
+    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
   }
 
   GemmArgs a1{};
@@ -687,13 +951,13 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
-    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
     prof_record(3, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
     prof_record(4, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
-    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc1, dev, tA, tW13, tW13, a1, max_tiles1, s)));
+    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
     prof_record(3, s);
     if (dtype == MOE_F16)
       quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
@@ -705,7 +969,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
           reinterpret_cast<float*>(ws + L.uscale));
     MOE_CUDA(cudaGetLastError());
     prof_record(4, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc2, dev, tUA, tW2, tW2, a2, max_tiles2, s)));
+    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
     prof_record(5, s);
   }
   return MOE_OK;

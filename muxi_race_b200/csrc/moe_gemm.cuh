@@ -1,11 +1,13 @@
 // moe_gemm.cuh — the grouped expert GEMM of the fused MoE, as one persistent,
 // warp-specialised tcgen05 kernel template for sm_100a.
 //
-// One CTA per SM (192 threads):
-//   warp 0      TMA producer: streams A (token rows) and B (expert weight rows) k-blocks into two
-//               rings of 128B-swizzled shared-memory buffers (A and B have separate depths);
-//   warp 1      owns TMEM (512 columns = two 128 x 256 fp32/int32 accumulator slots); one lane
-//               issues tcgen05.mma for each k-block and commits to the ring's "empty" barriers;
+// One CTA per SM (224 threads, 7 warps):
+//   warp 0      lane 0 streams B (expert weight rows) into the B ring by TMA;
+//   warp 6      streams A (token rows) into the A ring: lane 0 by TMA, or all lanes by cp.async
+//               (LSU paths); A and B have separate rings, depths and barriers, so the weight
+//               stream never waits for an A slot;
+//   warp 1      owns TMEM (512 columns of fp32/int32 accumulators); one lane issues tcgen05.mma
+//               for each k-block and commits to the rings' "empty" barriers;
 //   warps 2..5  epilogue: tcgen05.ld a finished accumulator (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), apply the fused epilogue, store to global, and hand
 //               the slot back, so epilogues overlap the main loop of the next tile.
@@ -13,24 +15,27 @@
 // Work unit = (block group, column tile). A block group is up to GMAX consecutive 128-row
 // routing blocks of ONE expert: every k-block of the expert's weight tile is loaded once and
 // multiplied against all the group's A blocks (one accumulator slot per block), so an expert
-// with 129..256 routed rows streams its weights through L2 -> SM once instead of twice. On B200
-// the bound for these weight-streaming GEMMs is the L2 -> SM intake, so bytes moved per output
-// are what the tiling minimises. Column tiles of one group run back to back (the group's A rows
-// are re-read from L2, not HBM).
+// with 129..256 routed rows streams its weights from HBM once instead of twice (two units that
+// read the same weight tile at different times rarely meet in L2: at ~7 TB/s the 126 MB L2 turns
+// over in ~18 us). A two-block group's A rows are contiguous and arrive as one 256-row box.
 //
-// CTAs per SM (CPS): measured on B200, one CTA completes about one TMA box per ~340 ns whatever
-// its size (16 KiB boxes: ~48 GB/s per SM from L2), while a second CTA on the SM doubles the rate.
-// With CPS = 2 each CTA takes half the shared memory and half of TMEM (one 256-column slot), and
-// the two CTAs' epilogues and main loops overlap each other.
+// TMA operations per byte: measured on B200, one CTA completes about one TMA box per ~300-350 ns
+// almost whatever its size (16 KiB boxes: ~48 GB/s per SM from L2; 64 KiB boxes: ~160 GB/s), so
+// the kernel moves few, large boxes: the gate and up rows of a Stage1 weight tile come as one
+// box of a 3-D/4-D tensor map (the gate/up offset is a tensor dimension), and a weight box may
+// span KPB consecutive k-blocks (a k-block dimension of stride 128 bytes), which lands in shared
+// memory exactly as KPB consecutive 128B-swizzled k-block tiles.
 //
-// Tiles: 128 rows per block x BN accumulator columns (BN = 256: two accumulator slots, so an
-// epilogue overlaps the next tile's main loop, or one block group of two blocks; BN = 512: one
-// slot, two N = 256 MMAs per k-step sharing the A block). k-blocks are 128 bytes wide (64
-// fp16/bf16 or 128 int8 elements, 128-byte swizzle): measured on B200, halving the k-block width
-// (more, smaller TMA requests for the same bytes in flight) costs 20% or more.
+// CTAs per SM (CPS): with CPS = 2 each CTA takes half the shared memory and half of TMEM, and the
+// two CTAs' epilogues and main loops overlap each other.
+//
+// Tiles: 128 rows per block x BN accumulator columns (BN = 128 or 256: one N = BN MMA per k-step;
+// BN = 512: two N = 256 MMAs per k-step sharing the A block). Accumulator slots = 512 / BN, a
+// group takes one per block. k-blocks are 128 bytes wide (64 fp16/bf16 or 128 int8 elements,
+// 128-byte swizzle): measured on B200, halving the k-block width costs 20% or more.
 //
 // Modes (the epilogue is the only difference):
-//   kStage1     D = [gate | up] halves of 128 columns each; U = silu(gate) * up, stored to the
+//   kStage1     D = [gate | up] halves of BN/2 columns each; U = silu(gate) * up, stored to the
 //               [rows, I] intermediate (reference Stage1, SUB/submission.py:586-641);
 //   kStage2Pad  out[p, :] = D * routed[route(p)] for valid rows and 0 for pad rows, in the
 //               padded stacked layout (reference Stage2, SUB/submission.py:317-357, 933-947);
@@ -55,14 +60,19 @@ constexpr int kTmemCols = 512;
 constexpr int kRingMax = 224 * 1024;
 
 // Shared-memory rings: A (token rows, mostly L2 hits) and B (expert weights, streamed from HBM)
-// have separate depths, so the weight stream can run further ahead than the A stream.
-template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false> struct Ring {
-  static_assert(BN == 256 || BN == 512, "accumulator width");
+// have separate depths, so the weight stream can run further ahead than the A stream. An A stage
+// holds one k-block of every block of a group; a B stage holds KPB k-blocks of the weight tile,
+// laid out [k-block][BN rows] (Stage1 rows: [gate BN/2 | up BN/2]).
+template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false, int KPB = 1> struct Ring {
+  static_assert(BN == 128 || BN == 256 || BN == 512, "accumulator width");
   static_assert(CPS == 1 || CPS == 2, "CTAs per SM");
+  static_assert(KPB == 1 || (KPB >= 1 && KPB <= 4 && BN <= kMmaN), "k-blocks per weight box");
+  static constexpr int kMN = BN < kMmaN ? BN : kMmaN;  // N of one MMA
   static constexpr int kTmemColsCta = kTmemCols / CPS;  // TMEM columns this CTA allocates
   static_assert(GMAX >= 1 && GMAX * BN <= kTmemColsCta, "a block group must fit in TMEM");
   static constexpr int kAStageBytes = GMAX * kABytes;
-  static constexpr int kBBytes = BN * kKBytes;
+  static constexpr int kBKBytes = BN * kKBytes;  // one k-block of the weight tile
+  static constexpr int kBBytes = KPB * kBKBytes;
   static constexpr int kAStages = AST;
   static constexpr int kBStages = BST;
   static constexpr int kRingBytes = AST * kAStageBytes + BST * kBBytes;
@@ -120,6 +130,10 @@ struct GemmArgs {
   long long zero_bytes;
 
   int b_evict_first;          // weight loads with the L2 evict_first policy
+  // Stage1 weight maps: 0 = tmB0 covers gate and up rows as one tensor (the gate/up offset is a
+  // dimension: one box per stage); 1 = tmB0 gate rows and tmB1 up rows, two 2-D boxes per k-block.
+  int b_split;
+  int gu_swap;                // combined map based at the up rows: the tile holds [up | gate]
 
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
@@ -216,8 +230,9 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       const int col0 = n0 + c;
       if (col0 >= args.N) break;
       uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(t_row + c, g);
-      tmem_ld_32x32b_x32(t_row + BN / 2 + c, u);
+      const uint32_t goff = args.gu_swap ? BN / 2 : 0;  // [gate | up] or [up | gate] columns
+      tmem_ld_32x32b_x32(t_row + goff + c, g);
+      tmem_ld_32x32b_x32(t_row + (BN / 2 - goff) + c, u);
       tmem_ld_wait();
       uint32_t packed[16];
 #pragma unroll
@@ -315,18 +330,29 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS>
+// Tensor maps (all 128B-swizzled, boxes 128 bytes wide in k):
+//   tmA   A rows, box GMAX * 128 rows: a whole group in one box (TMA A path)
+//   tmA1  A rows, box 128 rows: groups with fewer than GMAX blocks (GMAX = 1: the same as tmA)
+//   tmB0  weights. Stage1: one map over the gate and up rows (dimensions {K, rows, gate/up} for
+//         KPB = 1, {k-block elements, rows, gate/up, k-blocks} otherwise), or the gate rows alone
+//         when args.b_split. Stage2: {K, rows} for KPB = 1, {k-block elements, rows, k-blocks}
+//         otherwise.
+//   tmB1  Stage1 with args.b_split: the up rows ({K, rows}).
+template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB>
 __global__ void __launch_bounds__(kThreads, CPS)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-                    const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  using RingT = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma>;
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
+                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+                    const GemmArgs args) {
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma, KPB>;
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
+  constexpr int kBKBytes = RingT::kBKBytes;
+  constexpr int kMN = RingT::kMN;
   constexpr int kSlots = RingT::kSlots;
-  constexpr int kHalves = BN / kMmaN;  // MMAs per k-step per block
+  constexpr int kHalves = BN / kMN;  // MMAs per k-step per block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring_b = smem;                            // [BST][kBBytes]
+  uint8_t* ring_b = smem;                            // [BST][KPB][BN rows x 128 B]
   uint8_t* ring_a = smem + BST * kBBytes;            // [AST][GMAX][kABytes]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RingT::kRingBytes);
   uint64_t* fullA = bars;                            // [AST]
@@ -363,9 +389,12 @@ __global__ void __launch_bounds__(kThreads, CPS)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if (AMODE == kATma) tma_prefetch_desc(&tmA);
+    if (AMODE == kATma) {
+      tma_prefetch_desc(&tmA);
+      if (GMAX > 1) tma_prefetch_desc(&tmA1);
+    }
     tma_prefetch_desc(&tmB0);
-    if (MODE == kStage1) tma_prefetch_desc(&tmB1);
+    if (MODE == kStage1 && args.b_split) tma_prefetch_desc(&tmB1);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, RingT::kTmemColsCta);
@@ -381,40 +410,81 @@ __global__ void __launch_bounds__(kThreads, CPS)
   const int num_kb = (args.K * (IS_I8 ? 1 : 2) + kKBytes - 1) / kKBytes;
   constexpr int kKElems = IS_I8 ? kKBytes : kKBytes / 2;
 
-  if (warp == 0 || warp == 6) {
-    // ---------------------------------------------------------------- producers
-    // Warp 0 lane 0 streams B (weights) into the B ring by TMA; warp 6 streams A (token rows)
-    // into the A ring, by TMA from lane 0 (kATma) or by cp.async from all 32 lanes (LSU paths).
-    // Each waits only for its own ring, so B runs up to BST k-blocks ahead of the MMA and A up
-    // to AST, independently.
-    const bool is_b = warp == 0;
-    const bool active = is_b ? lane == 0 : (AMODE != kATma || lane == 0);
-    if (active) {
-      const int depth = is_b ? BST : AST;
-      uint64_t* full = is_b ? fullB : fullA;
-      uint64_t* empty = is_b ? emptyB : emptyA;
-      // weights: evict_normal (args.b_evict_first: evict_first); token rows: evict_last (re-read by
-      // every column tile)
-      const uint64_t pol = is_b ? (args.b_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal())
-                                : l2_policy_evict_last();
+  if (warp == 0) {
+    // ---------------------------------------------------------------- B producer (weights)
+    // One lane streams the weight tile of each unit, KPB k-blocks per ring stage, up to BST
+    // stages ahead of the MMA. L2 policy evict_normal (args.b_evict_first: evict_first).
+    if (lane == 0) {
+      const uint64_t pol = args.b_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal();
+      int st = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int par[BST];  // parity of the last load issued into each slot, -1 = none
+#pragma unroll
+      for (int s = 0; s < BST; ++s) par[s] = -1;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int fb, nb, nt, e;
+        if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        const int brow = e * args.b_rows_per_expert + nt * (MODE == kStage1 ? BN / 2 : BN);
+        for (int kb0 = 0; kb0 < num_kb; kb0 += KPB) {
+          if (!mbar_wait(&emptyB[st], ph ^ 1u, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* dst = stage_b(st);
+          if (MODE == kStage1 && args.b_split) {  // gate box + up box per k-block
+            const int nk = min(KPB, num_kb - kb0);
+            mbar_arrive_expect_tx(&fullB[st], static_cast<uint32_t>(nk * kBKBytes));
+            for (int j = 0; j < nk; ++j) {
+              const int kx = (kb0 + j) * kKElems;
+              tma_load_2d(dst + j * kBKBytes, &tmB0, &fullB[st], kx, brow, pol);
+              tma_load_2d(dst + j * kBKBytes + kBKBytes / 2, &tmB1, &fullB[st], kx, brow + args.b1_row_offset, pol);
+            }
+          } else {
+            mbar_arrive_expect_tx(&fullB[st], static_cast<uint32_t>(kBBytes));
+            if (MODE == kStage1) {  // gate and up rows of KPB k-blocks in one box
+              if (KPB == 1)
+                tma_load_3d(dst, &tmB0, &fullB[st], kb0 * kKElems, brow, 0, pol);
+              else
+                tma_load_4d(dst, &tmB0, &fullB[st], 0, brow, 0, kb0, pol);
+            } else if (KPB == 1) {
+#pragma unroll
+              for (int h = 0; h < kHalves; ++h)
+                tma_load_2d(dst + h * (kMN * kKBytes), &tmB0, &fullB[st], kb0 * kKElems, brow + h * kMN, pol);
+            } else {
+              tma_load_3d(dst, &tmB0, &fullB[st], 0, brow, kb0, pol);
+            }
+          }
+          par[st] = static_cast<int>(ph);
+          if (++st == BST) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Drain: every load issued must have landed before the CTA may exit. On the normal path
+      // these phases completed long ago; after an abort this bounds the wait.
+      for (int s = 0; s < BST; ++s)
+        if (par[s] >= 0) mbar_wait_drain(&fullB[s], static_cast<uint32_t>(par[s]));
+    }
+  } else if (warp == 6) {
+    // ---------------------------------------------------------------- A producer (token rows)
+    // TMA from lane 0 (kATma; a full group as one box) or cp.async from all 32 lanes (LSU paths),
+    // one k-block per stage, up to AST stages ahead. L2 policy evict_last: every column tile of
+    // the group re-reads these rows.
+    if (AMODE != kATma || lane == 0) {
+      const uint64_t pol = l2_policy_evict_last();
       const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
-      int par[AST > BST ? AST : BST];  // parity of the last load issued into each slot, -1 = none
+      int par[AST];
 #pragma unroll
-      for (int s = 0; s < (AST > BST ? AST : BST); ++s) par[s] = -1;
+      for (int s = 0; s < AST; ++s) par[s] = -1;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int fb, nb, nt, e;
         if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
-        int brow0, brow1 = 0;
-        if (MODE == kStage1) {
-          brow0 = e * args.b_rows_per_expert + nt * (BN / 2);
-          brow1 = e * args.b_rows_per_expert + args.b1_row_offset + nt * (BN / 2);
-        } else {
-          brow0 = e * args.b_rows_per_expert + nt * BN;
-        }
-        if (!is_b && AMODE != kATma) {
+        if (AMODE != kATma) {
           // byte offsets of this group's source rows, -1 = zero fill
           __syncwarp();
           for (int j = 0; j < nb; ++j)
@@ -426,25 +496,19 @@ __global__ void __launch_bounds__(kThreads, CPS)
         }
         for (int kb = 0; kb < num_kb; ++kb) {
           const int kx = kb * kKElems;
-          bool got = mbar_wait(&empty[st], ph ^ 1u, abort_flag, args.status);
-          if (!is_b && AMODE != kATma) got = __all_sync(0xffffffffu, got);  // the warp stays converged
+          bool got = mbar_wait(&emptyA[st], ph ^ 1u, abort_flag, args.status);
+          if (AMODE != kATma) got = __all_sync(0xffffffffu, got);  // the warp stays converged
           if (!got) {
             ok = false;
             break;
           }
-          if (is_b) {
-            mbar_arrive_expect_tx(&full[st], kBBytes);
-            if (MODE == kStage1) {  // gate rows, then up rows: BN/2 each
-              tma_load_2d(stage_b(st), &tmB0, &full[st], kx, brow0, pol);
-              tma_load_2d(stage_b(st) + kBBytes / 2, &tmB1, &full[st], kx, brow1, pol);
-            } else {  // BN rows as boxes of 256
-#pragma unroll
-              for (int h = 0; h < kHalves; ++h)
-                tma_load_2d(stage_b(st) + h * (kMmaN * kKBytes), &tmB0, &full[st], kx, brow0 + h * kMmaN, pol);
-            }
-          } else if (AMODE == kATma) {
-            mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(nb * kABytes));
-            for (int j = 0; j < nb; ++j) tma_load_2d(stage_a(st, j), &tmA, &full[st], kx, (fb + j) * kBM, pol);
+          if (AMODE == kATma) {
+            mbar_arrive_expect_tx(&fullA[st], static_cast<uint32_t>(nb * kABytes));
+            if (GMAX > 1 && nb == GMAX)
+              tma_load_2d(stage_a(st, 0), &tmA, &fullA[st], kx, fb * kBM, pol);
+            else
+              for (int j = 0; j < nb; ++j)
+                tma_load_2d(stage_a(st, j), GMAX > 1 ? &tmA1 : &tmA, &fullA[st], kx, (fb + j) * kBM, pol);
           } else {
             const int c = lane & 7;  // 16-byte chunk of the 128-byte k-block row segment
             const long long kbyte = static_cast<long long>(kb) * kKBytes + c * 16;
@@ -462,27 +526,25 @@ __global__ void __launch_bounds__(kThreads, CPS)
                             in ? 16u : 0u);
               }
             }
-            cp_async_mbar_arrive(&full[st]);
-            mbar_arrive(&full[st]);
+            cp_async_mbar_arrive(&fullA[st]);
+            mbar_arrive(&fullA[st]);
           }
           par[st] = static_cast<int>(ph);
-          if (++st == depth) {
+          if (++st == AST) {
             st = 0;
             ph ^= 1u;
           }
         }
       }
-      // Drain: every copy this lane issued must have landed before the CTA may exit. On the
-      // normal path these phases completed long ago; after an abort this bounds the wait.
-      if (!is_b && AMODE != kATma) cp_async_wait_all();
-      if (is_b || AMODE == kATma)
-        for (int s = 0; s < depth; ++s)
-          if (par[s] >= 0) mbar_wait_drain(&full[s], static_cast<uint32_t>(par[s]));
+      if (AMODE != kATma) cp_async_wait_all();
+      if (AMODE == kATma)
+        for (int s = 0; s < AST; ++s)
+          if (par[s] >= 0) mbar_wait_drain(&fullA[s], static_cast<uint32_t>(par[s]));
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kMmaN) : idesc_f16(Elt<OutT>::kBF16, kBM, kMmaN);
+      const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kMN) : idesc_f16(Elt<OutT>::kBF16, kBM, kMN);
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
       uint32_t slot_cnt = 0;  // accumulator slots handed out so far (slot = cnt % kSlots)
@@ -504,14 +566,18 @@ __global__ void __launch_bounds__(kThreads, CPS)
         if (!ok) break;
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&fullB[sb], pb, abort_flag, args.status) ||
-              !mbar_wait(&fullA[sa], pa, abort_flag, args.status)) {
+          const int kk = kb % KPB;  // k-block inside the current B stage
+          if (kk == 0 && !mbar_wait(&fullB[sb], pb, abort_flag, args.status)) {
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&fullA[sa], pa, abort_flag, args.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (AMODE != kATma) fence_proxy_async_smem();  // A arrived through the generic proxy
-          const uint32_t b_addr = smem_u32(stage_b(sb));
+          const uint32_t b_addr = smem_u32(stage_b(sb)) + static_cast<uint32_t>(kk * kBKBytes);
 #pragma unroll
           for (int j = 0; j < GMAX; ++j) {
             if (j >= nb) break;
@@ -521,8 +587,8 @@ __global__ void __launch_bounds__(kThreads, CPS)
               const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
 #pragma unroll
               for (int h = 0; h < kHalves; ++h) {
-                const uint64_t bd = smem_desc_sw128(b_addr + h * (kMmaN * kKBytes) + k * 32);
-                const uint32_t d = d_tmem[j] + static_cast<uint32_t>(h * kMmaN);
+                const uint64_t bd = smem_desc_sw128(b_addr + h * (kMN * kKBytes) + k * 32);
+                const uint32_t d = d_tmem[j] + static_cast<uint32_t>(h * kMN);
                 if (IS_I8)
                   mma_i8(d, ad, bd, idesc, (kb | k) != 0);
                 else
@@ -530,15 +596,17 @@ __global__ void __launch_bounds__(kThreads, CPS)
               }
             }
           }
-          tc_commit(&emptyB[sb]);  // frees the ring slots once the MMAs have read them
-          tc_commit(&emptyA[sa]);
-          if (++sb == BST) {
-            sb = 0;
-            pb ^= 1u;
-          }
+          tc_commit(&emptyA[sa]);  // frees the A slot once the MMAs have read it
           if (++sa == AST) {
             sa = 0;
             pa ^= 1u;
+          }
+          if (kk == KPB - 1 || kb == num_kb - 1) {  // last k-block of the B stage
+            tc_commit(&emptyB[sb]);
+            if (++sb == BST) {
+              sb = 0;
+              pb ^= 1u;
+            }
           }
         }
         if (!ok) break;

@@ -78,3 +78,15 @@ def test_workload_algorithmic_work():
     assert c.flops() == pytest.approx(2.886e12, rel=1e-3)
     assert c.weight_bytes() == pytest.approx(22.55e9, rel=1e-3)
     assert CONFIGS["cfg4"].weight_bytes() == pytest.approx(11.27e9, rel=1e-3)
+
+
+def test_set_tile_host():
+    """Tile selection is host state: known names and "auto" are accepted, unknown ones refused."""
+    _lib.set_tile(0, "p256a6b8")
+    _lib.set_tile(1, "256a4b5")
+    _lib.set_tile(2, None)
+    _lib.set_tile(0, "auto")
+    with pytest.raises(_lib.MoeError):
+        _lib.set_tile(2, "256a4b5x")
+    with pytest.raises(_lib.MoeError):
+        _lib.set_tile(-1, "auto")
