@@ -338,6 +338,16 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   return c;
 }
 
+// Unit order (see tile_unit): MOE_B200_UNIT_ORDER = expert (default: an expert's groups side by
+// side per column tile) | group (group-major).
+int unit_order() {
+  static const int v = [] {
+    const char* e = getenv("MOE_B200_UNIT_ORDER");
+    return (e && strcmp(e, "group") == 0) ? 0 : 1;
+  }();
+  return v;
+}
+
 template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB>;
@@ -347,6 +357,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   }();
   GemmArgs args_l = args;
   args_l.b_evict_first = evict_first;
+  args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
   if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
@@ -372,6 +383,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   }();
   GemmArgs args_l = args;
   args_l.b_evict_first = evict_first;
+  args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = 1;
   args_l.gu_swap = 0;
   args_l.b1_row_offset = m.b1_row_offset;
@@ -666,7 +678,7 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   m2.b1 = m2.b0;
 
   if (gmax1 > 1 || gmax2 > 1) {  // pair each expert's blocks (from group_padded_offsets)
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, groups, ngroups);
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)nblk, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
   }
 
@@ -679,8 +691,10 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a1.groups = gmax1 > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
+  a1.nblk = (int)nblk;
   a1.b_rows_per_expert = (int)I;
   a1.b1_row_offset = 0;
+  a1.group_padded_offsets = gpo;
   a1.U = U;
   a1.ldu = (int)I;
   a1.status = status;
@@ -831,7 +845,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   prof_record(0, s);
   MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s));
   if (gmax1 > 1 || gmax2 > 1) {
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, groups, ngroups);
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
   }
   prof_record(1, s);
@@ -909,8 +923,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a1.groups = gmax1 > 1 ? groups : nullptr;
   a1.E = (int)E;
   a1.block_expert = gidx;
+  a1.nblk = (int)L.nblk_max;
   a1.b_rows_per_expert = (int)(2 * I);
   a1.b1_row_offset = (int)I;
+  a1.group_padded_offsets = gpo;
   a1.U = U;
   a1.ldu = (int)I;
   a1.a_scale = xscale;
@@ -935,7 +951,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a2.groups = gmax2 > 1 ? groups : nullptr;
   a2.E = (int)E;
   a2.block_expert = gidx;
+  a2.nblk = (int)L.nblk_max;
   a2.b_rows_per_expert = (int)H;
+  a2.group_padded_offsets = gpo;
   a2.out = out;
   a2.ldo = (int)H;
   a2.routed = tw;

@@ -95,6 +95,7 @@ struct GemmArgs {
   const int* groups;          // [ngroups] first_block * 2 + (blocks - 1); NULL: group g = block g
   int E;
   const int* block_expert;    // expert of each 128-row block (group_idx_for_bx)
+  int nblk;                   // 128-row blocks in the A / output row space (units beyond it are skipped)
   int b_rows_per_expert;      // rows of one expert in the B tensor map(s)
   int b1_row_offset;          // Stage1: row offset of the "up" half inside one expert of map B1
 
@@ -130,6 +131,7 @@ struct GemmArgs {
   long long zero_bytes;
 
   int b_evict_first;          // weight loads with the L2 evict_first policy
+  int unit_order;             // 0 = group-major units, 1 = per expert column-tile-major (tile_unit)
   // Stage1 weight maps: 0 = tmB0 covers gate and up rows as one tensor (the gate/up offset is a
   // dimension: one box per stage); 1 = tmB0 gate rows and tmB1 up rows, two 2-D boxes per k-block.
   int b_split;
@@ -194,21 +196,40 @@ __device__ __forceinline__ float load_weight(const void* w, int dtype, int i) {
 // silu(g) * u = g / (1 + e^-g) * u; the exponential is CUDA's __expf.
 __device__ __forceinline__ float silu_mul(float g, float u) { return g * __frcp_rn(1.0f + __expf(-g)) * u; }
 
-// Work unit decode: first block, block count, column tile and expert of tile `tile`.
+// Work unit decode: first block, block count, column tile and expert of unit `tile`.
+// Units are numbered group-major (n_tiles column tiles per group), so a unit's group g0 names its
+// expert. With args.unit_order == 1 the units of one expert are re-ordered column-tile-major:
+// for each column tile, all of the expert's groups in turn. The groups of an expert then read the
+// same weight tile at the same time on neighbouring SMs, so its second and later reads hit L2
+// instead of DRAM. The expert's groups are consecutive, all but the last with gm blocks, so the
+// expert's first group is g0 - (first block of g0 - first block of the expert) / gm. Units whose
+// blocks fall outside [0, nblk) (metadata inconsistent with the row count) are skipped.
 template <int GMAX>
 __device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& fb, int& nb, int& nt, int& e) {
-  const int g = tile / args.n_tiles;
-  nt = tile - g * args.n_tiles;
-  if (GMAX == 1 || args.groups == nullptr) {
-    fb = g;
-    nb = 1;
-  } else {
-    const int pk = args.groups[g];
-    fb = pk >> 1;
-    nb = (pk & 1) + 1;
+  const int g0 = tile / args.n_tiles;
+  const bool grouped = GMAX > 1 && args.groups != nullptr;
+  const int pk = grouped ? args.groups[g0] : 0;
+  const int fb0 = grouped ? (pk >> 1) : g0;
+  e = args.block_expert[fb0];
+  if (e < 0 || e >= args.E) return false;
+  if (!args.unit_order) {
+    nt = tile - g0 * args.n_tiles;
+    fb = fb0;
+    nb = grouped ? (pk & 1) + 1 : 1;
+    return fb >= 0 && fb + nb <= args.nblk;
   }
-  e = args.block_expert[fb];
-  return e >= 0 && e < args.E;
+  const int gm = grouped ? GMAX : 1;
+  const int b0 = args.group_padded_offsets[e] / kBM;
+  const int nbe = args.group_padded_offsets[e + 1] / kBM - b0;
+  const int ng = (nbe + gm - 1) / gm;
+  const int gs = g0 - (fb0 - b0) / gm;
+  const int local = tile - gs * args.n_tiles;
+  if (nbe < 1 || local < 0 || local >= ng * args.n_tiles) return false;  // metadata inconsistent with gidx
+  nt = local / ng;
+  const int j = local - nt * ng;
+  fb = b0 + j * gm;
+  nb = min(gm, nbe - j * gm);
+  return fb >= 0 && fb + nb <= args.nblk;
 }
 
 // ------------------------------------------------------------------ epilogue of one block
@@ -668,10 +689,11 @@ __global__ void __launch_bounds__(kThreads, CPS)
 // ------------------------------------------------------------------ block groups
 // Pairs the routing blocks of each expert: expert e owns blocks [gpo[e]/128, gpo[e+1]/128); they
 // become ceil(n/gmax) groups of up to gmax consecutive blocks, in expert order. One CTA of 1024
-// threads walks the experts in chunks of 1024 with a running base.
+// threads walks the experts in chunks of 1024 with a running base. At most max_groups groups are
+// written (offsets that describe more blocks than the row space holds are cut off there).
 __global__ void __launch_bounds__(1024)
-    build_groups_kernel(const int32_t* __restrict__ group_padded_offsets, int E, int gmax, int32_t* __restrict__ groups,
-                        int32_t* __restrict__ ngroups_out) {
+    build_groups_kernel(const int32_t* __restrict__ group_padded_offsets, int E, int gmax, int max_groups,
+                        int32_t* __restrict__ groups, int32_t* __restrict__ ngroups_out) {
   __shared__ int s_warp[32];
   __shared__ int s_base;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -704,7 +726,7 @@ __global__ void __launch_bounds__(1024)
     }
     __syncthreads();
     const int base = s_base + incl - ng + (w > 0 ? s_warp[w - 1] : 0);
-    for (int g = 0; g < ng; ++g) {
+    for (int g = 0; g < ng && base + g < max_groups; ++g) {
       const int nb = min(gmax, nblk - g * gmax);
       groups[base + g] = (b0 + g * gmax) * 2 + (nb - 1);
     }
@@ -712,7 +734,7 @@ __global__ void __launch_bounds__(1024)
     if (tid == 0) s_base += s_warp[31];
     __syncthreads();
   }
-  if (tid == 0) *ngroups_out = s_base;
+  if (tid == 0) *ngroups_out = min(s_base, max_groups);
 }
 
 }  // namespace moe
