@@ -121,6 +121,7 @@ struct TileInfo {
   const char* name;
   int bn, gmax, ast, bst, cps, kpb;
   int pair;  // 1: CTA-pair kernel (cta_group::2), 256-row units, each CTA loads half the weights
+  int epi;   // epilogue warps (4, or 8: two per TMEM lane quadrant, each half of the columns)
 };
 
 // Tiled map over a tensor of `rank` dimensions (dims[0] innermost, in elements; strides of dims
@@ -266,34 +267,38 @@ enum TileCfg {
   kTP256A6B8,
   kTP256A7B7,
   kTP256A4B10,
+  kT256A4B5E8,
+  kT256x2A3B4E8,
   kNumTileCfg
 };
 constexpr TileInfo kTiles[kNumTileCfg] = {
-    {"256a4b5", 256, 1, 4, 5, 1, 1, 0},     {"256x2a3b4", 256, 2, 3, 4, 1, 1, 0},
-    {"512a2b3", 512, 1, 2, 3, 1, 1, 0},     {"256a2b2c2", 256, 1, 2, 2, 2, 1, 0},
-    {"256a6b4", 256, 1, 6, 4, 1, 1, 0},     {"256a6b2k2", 256, 1, 6, 2, 1, 2, 0},
-    {"128x2a3b4k2", 128, 2, 3, 4, 1, 2, 0}, {"128x2a4b3k2", 128, 2, 4, 3, 1, 2, 0},
-    {"128x2a3b8", 128, 2, 3, 8, 1, 1, 0},   {"256x2a3b2k2", 256, 2, 3, 2, 1, 2, 0},
-    {"p256a6b8", 256, 2, 6, 8, 1, 1, 1},    {"p256a7b7", 256, 2, 7, 7, 1, 1, 1},
-    {"p256a4b10", 256, 2, 4, 10, 1, 1, 1},
+    {"256a4b5", 256, 1, 4, 5, 1, 1, 0, 4},     {"256x2a3b4", 256, 2, 3, 4, 1, 1, 0, 4},
+    {"512a2b3", 512, 1, 2, 3, 1, 1, 0, 4},     {"256a2b2c2", 256, 1, 2, 2, 2, 1, 0, 4},
+    {"256a6b4", 256, 1, 6, 4, 1, 1, 0, 4},     {"256a6b2k2", 256, 1, 6, 2, 1, 2, 0, 4},
+    {"128x2a3b4k2", 128, 2, 3, 4, 1, 2, 0, 4}, {"128x2a4b3k2", 128, 2, 4, 3, 1, 2, 0, 4},
+    {"128x2a3b8", 128, 2, 3, 8, 1, 1, 0, 4},   {"256x2a3b2k2", 256, 2, 3, 2, 1, 2, 0, 4},
+    {"p256a6b8", 256, 2, 6, 8, 1, 1, 1, 4},    {"p256a7b7", 256, 2, 7, 7, 1, 1, 1, 4},
+    {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
+    {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8},
 };
 static_assert(kNumTileCfg * 36 <= 64 * 16, "smem attribute bits");
 
-// Defaults per stage, chosen per call from the average number of 128-row blocks per expert
-// (measured on B200): with about 1.8 or more blocks per expert most blocks belong to two-block
-// groups, and the CTA-pair kernel (p256a6b8), whose pair streams each weight tile once for both
-// blocks, is faster (cfg2 Stage1 0.65 vs 0.73 ms, Stage2 0.32 vs 0.36 ms); with fewer, the
-// one-block groups leave half of each pair idle (cfg3 at T = 128: Stage1 3.24 vs 2.32 ms) and the
-// single-CTA kernels win: Stage1 256a4b5, Stage2 256x2a3b4 (two-block groups sharing one weight
-// stream, cfg3 Stage2 1.38 vs 1.56 ms for 256a4b5). MOE_B200_TILE / MOE_B200_TILE1 /
-// MOE_B200_TILE2 override the choice with a configuration name.
+// Defaults, measured on B200. Stage1: 256a4b5e8 (single CTA, 8 epilogue warps: the SiLU*up
+// epilogue no longer holds up the next unit; cfg2 Stage1 0.52 vs 0.60-0.73 ms). Stage2, chosen per
+// call from the average number of 128-row blocks per expert: from about 1.8 blocks per expert on,
+// most blocks belong to two-block groups and the CTA-pair kernel p256a6b8 (one weight stream per
+// two blocks, a third less shared-memory traffic per output) is fastest (cfg2 Stage2 0.31 vs
+// 0.35 ms); below that, one-block groups would leave half of each pair idle (cfg3 at T = 128:
+// 1.6 vs 1.1 ms) and 256x2a3b4e8 (single CTA, two-block groups sharing one weight stream, 8
+// epilogue warps; cfg4 Stage2 0.83 vs 0.94 ms with 4) is used. MOE_B200_TILE /
+// MOE_B200_TILE1 / MOE_B200_TILE2 or moe_set_tile override the choice with a configuration name.
 TileCfg parse_tile(const char* v, TileCfg dflt) {
   if (v)
     for (int i = 0; i < kNumTileCfg; ++i)
       if (strcmp(v, kTiles[i].name) == 0) return static_cast<TileCfg>(i);
   return dflt;
 }
-constexpr TileCfg kDefaultTile1 = kT256A4B5, kDefaultTile2 = kT256x2A3B4, kDefaultPair = kTP256A6B8;
+constexpr TileCfg kDefaultTile1 = kT256A4B5E8, kDefaultTile2 = kT256x2A3B4E8, kDefaultPair = kTP256A6B8;
 constexpr double kPairBlocksPerExpert = 1.8;
 constexpr TileCfg kAuto = kNumTileCfg;
 // Selected configuration per stage (kAuto = per-call choice): environment at first use,
@@ -322,19 +327,24 @@ bool a_path_lsu() {
 }
 
 // The configuration a stage runs with for reduction length K (elements of elt bytes), given the
-// average number of 128-row blocks per expert: the environment's choice if any, else the
-// per-call default. A weight box spanning KPB k-blocks needs whole k-blocks (K * elt a multiple
-// of 128 bytes) in multiples of KPB; BN = 128 is a Stage1 tile; the LSU A path (row table in
-// shared memory) runs the single-CTA KPB = 1, BN >= 256 configurations. Anything else falls back
-// to the stage's single-CTA default.
+// average number of 128-row blocks per expert: the selected one if any, else the per-call
+// default. A weight box spanning KPB k-blocks needs whole k-blocks (K * elt a multiple of 128
+// bytes) in multiples of KPB; BN = 128 is a Stage1 tile; the LSU A path (row table in shared
+// memory) runs the single-CTA, 4-epilogue-warp, KPB = 1, BN >= 256 configurations. Anything else
+// falls back to 256a4b5 / 256x2a3b4, which run on every path.
 TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_expert) {
-  const TileCfg single = stage == 1 ? kDefaultTile1 : kDefaultTile2;
+  const TileCfg safe = stage == 1 ? kT256A4B5 : kT256x2A3B4;
   TileCfg c = tile_cfg(stage);
-  if (c == kAuto) c = (!lsu && blocks_per_expert >= kPairBlocksPerExpert) ? kDefaultPair : single;
+  if (c == kAuto) {
+    if (stage == 2 && !lsu && blocks_per_expert >= kPairBlocksPerExpert)
+      c = kDefaultPair;
+    else
+      c = stage == 1 ? kDefaultTile1 : kDefaultTile2;
+  }
   const TileInfo& t = kTiles[c];
-  if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return single;
-  if (t.bn == 128 && stage != 1) return single;
-  if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair)) return single;
+  if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return safe;
+  if (t.bn == 128 && stage != 1) return safe;
+  if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
   return c;
 }
 
@@ -348,9 +358,10 @@ int unit_order() {
   return v;
 }
 
-template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB>
+template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
+          int EPI = 4>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB>;
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>;
   static const int evict_first = [] {
     const char* v = getenv("MOE_B200_B_EVICT_FIRST");  // experiments: 1 = evict_first for weights
     return v && strcmp(v, "1") == 0 ? 1 : 0;
@@ -368,15 +379,15 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   MOE_TRY(device_sms(dev, &sms));
   const int grid = max_tiles < sms * CPS ? max_tiles : sms * CPS;
   if (grid <= 0) return MOE_OK;
-  kern<<<grid, kThreads, smem, stream>>>(m.a, m.a1, m.b0, m.b1, args_l);
+  kern<<<grid, 96 + 32 * EPI, smem, stream>>>(m.a, m.a1, m.b0, m.b1, args_l);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }
 
 // CTA-pair kernel: clusters of two CTAs, one pair per two SMs (as many as can be resident).
-template <int MODE, typename OutT, bool I8, int AST, int BST>
+template <int MODE, typename OutT, bool I8, int AST, int BST, int EPI = 4>
 int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST>;
+  auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST, EPI>;
   static const int evict_first = [] {
     const char* v = getenv("MOE_B200_B_EVICT_FIRST");
     return v && strcmp(v, "1") == 0 ? 1 : 0;
@@ -396,7 +407,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
     MOE_TRY(device_sms(dev, &sms));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(96 + 32 * EPI, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
@@ -407,7 +418,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   }
   const int pairs = max_tiles < max_pairs[dev] ? max_tiles : max_pairs[dev];
   if (pairs <= 0) return MOE_OK;
-  kern<<<2 * pairs, kThreads, smem, stream>>>(m.a, m.b0, m.b1, args_l);
+  kern<<<2 * pairs, 96 + 32 * EPI, smem, stream>>>(m.a, m.b0, m.b1, args_l);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }
@@ -458,6 +469,13 @@ int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, i
     case kTP256A4B10:
       if constexpr (kTma) return launch_pair<MODE, OutT, I8, 4, 10>(dev, c, m, args, max_tiles, stream);
       break;
+    case kT256A4B5E8:
+      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+      break;
+    case kT256x2A3B4E8:
+      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+      break;
+
     default:
       break;
   }

@@ -54,7 +54,7 @@ namespace moe {
 constexpr int kBM = 128;       // rows per block = routing block size
 constexpr int kMmaN = 256;     // N of one tcgen05.mma
 constexpr int kKBytes = 128;   // k-block width in bytes (one 128B swizzle atom)
-constexpr int kThreads = 224;  // 7 warps
+constexpr int kThreads = 224;  // 7 warps (4 epilogue warps); kernels with 8 epilogue warps use 352
 constexpr int kABytes = kBM * kKBytes;  // 16 KiB per A block per stage
 constexpr int kTmemCols = 512;
 constexpr int kRingMax = 224 * 1024;
@@ -233,9 +233,11 @@ __device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& f
 }
 
 // ------------------------------------------------------------------ epilogue of one block
+// Columns [c_begin, c_end) of the block's output tile (Stage1: of the BN/2 SiLU*up outputs), in
+// chunks of 32: with 8 epilogue warps two warps share a TMEM lane quadrant, each taking half.
 template <int MODE, typename OutT, bool IS_I8, int BN, int AMODE>
 __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_row, int mb, int nt, int e,
-                                               int row_in_tile) {
+                                               int row_in_tile, int c_begin, int c_end) {
   const int p = mb * kBM + row_in_tile;  // padded row of this thread
   if (MODE == kStage1) {
     OutT* U = reinterpret_cast<OutT*>(args.U);
@@ -247,7 +249,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     }
     float amax = 0.0f;
 #pragma unroll 1
-    for (int c = 0; c < BN / 2; c += 32) {
+    for (int c = c_begin; c < c_end; c += 32) {
       const int col0 = n0 + c;
       if (col0 >= args.N) break;
       uint32_t g[32], u[32];
@@ -311,7 +313,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     OutT* out = reinterpret_cast<OutT*>(args.out);
     const size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
+    for (int c = c_begin; c < c_end; c += 32) {
       const int col0 = n0 + c;
       if (col0 >= args.N) break;
       uint32_t d[32];
@@ -359,8 +361,9 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 //         when args.b_split. Stage2: {K, rows} for KPB = 1, {k-block elements, rows, k-blocks}
 //         otherwise.
 //   tmB1  Stage1 with args.b_split: the up rows ({K, rows}).
-template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB>
-__global__ void __launch_bounds__(kThreads, CPS)
+template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
+          int EPI = 4>
+__global__ void __launch_bounds__(96 + EPI * 32, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
                     const GemmArgs args) {
@@ -371,6 +374,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
   constexpr int kMN = RingT::kMN;
   constexpr int kSlots = RingT::kSlots;
   constexpr int kHalves = BN / kMN;  // MMAs per k-step per block
+  static_assert(EPI == 4 || EPI == 8, "epilogue warps");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring_b = smem;                            // [BST][KPB][BN rows x 128 B]
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
     }
     for (int a = 0; a < kSlots; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty_bar[a], EPI);  // one arrive per epilogue warp
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -640,15 +644,21 @@ __global__ void __launch_bounds__(kThreads, CPS)
       mbar_wait_drain(drain_bar, 0);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    // ---------------------------------------------------------------- epilogue (warps 2..5, 7..10)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row_in_tile = q * 32 + lane;
+    const int eg = warp >= 7 ? 1 : 0;  // column half (8 epilogue warps)
+    constexpr int kCols = MODE == kStage1 ? BN / 2 : BN;
+    constexpr int kSpan = kCols / (EPI / 4);
+    const int c_begin = eg * kSpan, c_end = c_begin + kSpan;
     if (MODE == kStage1 && args.zero_ptr != nullptr) {
       // clear the Stage2 combine target while the first tile's main loop runs
       uint4* z = static_cast<uint4*>(args.zero_ptr);
       const long long n16 = args.zero_bytes / 16;
-      const long long t0 = static_cast<long long>(blockIdx.x) * 128 + (threadIdx.x - 64);
-      for (long long i2 = t0; i2 < n16; i2 += static_cast<long long>(gridDim.x) * 128) z[i2] = make_uint4(0, 0, 0, 0);
+      const int et = eg * 128 + (warp - (eg ? 7 : 2)) * 32 + lane;
+      const long long t0 = static_cast<long long>(blockIdx.x) * (EPI * 32) + et;
+      for (long long i2 = t0; i2 < n16; i2 += static_cast<long long>(gridDim.x) * (EPI * 32))
+        z[i2] = make_uint4(0, 0, 0, 0);
     }
     uint32_t slot_cnt = 0;
     bool ok = true;
@@ -668,7 +678,7 @@ __global__ void __launch_bounds__(kThreads, CPS)
         tc_fence_after();
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * BN);
-        epilogue_block<MODE, OutT, IS_I8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile);
+        epilogue_block<MODE, OutT, IS_I8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile, c_begin, c_end);
         // hand the slot back to the MMA warp
         tc_fence_before();
         __syncwarp();

@@ -16,8 +16,8 @@ from oracle.moe_ref import fused_moe_ref, run_kernel_ref_f32
 
 pytestmark = pytest.mark.gpu
 
-TILES = ["256a4b5", "256x2a3b4", "512a2b3", "256a2b2c2", "256a6b4", "256a6b2k2", "128x2a3b4k2", "128x2a3b8",
-         "256x2a3b2k2", "p256a6b8", "p256a7b7", "p256a4b10"]
+TILES = ["256a4b5", "256x2a3b4", "256a4b5e8", "256x2a3b4e8", "512a2b3", "256a2b2c2", "256a6b4", "256a6b2k2",
+         "128x2a3b4k2", "128x2a3b8", "256x2a3b2k2", "p256a6b8", "p256a7b7", "p256a4b10"]
 
 
 @pytest.fixture
