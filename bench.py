@@ -347,7 +347,7 @@ def bench_ep(args, world, rank, local):
 
     import muxi_race_b200 as m
     from muxi_race_b200 import _lib
-    from muxi_race_b200.ep import ExpertParallelMoE, ExpertPlacement
+    from muxi_race_b200.ep import ExpertParallelMoE, ExpertPlacement, PeerMemoryEP
     from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
 
     dev = torch.device("cuda", local)
@@ -364,18 +364,34 @@ def bench_ep(args, world, rank, local):
     w13, w2 = make_weights(cfg, seed=0, device=dev, experts=mine)
     x = make_hidden(cfg, seed=1 + rank, device=dev, T=T_rank)
     ids, tw = make_routing(cfg, seed=2 + rank, device=dev, T=T_rank)
-    moe = ExpertParallelMoE(w13, w2, placement)
+    p2p = args.ep_mode == "p2p"
+    if p2p:
+        moe = PeerMemoryEP(w13, w2, placement, max_tokens=T_rank, topk=cfg.topk)
+    else:
+        moe = ExpertParallelMoE(w13, w2, placement, chunks=args.ep_chunks)
+    n_chunks = 1 if p2p else args.ep_chunks
 
     for _ in range(args.warmup):
         moe(x, ids, tw)
     torch.cuda.synchronize()
     assert m.device_status() == 0, "device status flagged an error during warm-up"
 
+    # stage-boundary events for every local fused-MoE call (one per chunk) of every timed step
     stream = torch.cuda.current_stream(dev)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
-    for row in evs:
-        for e in row:
-            e.record(stream)
+    evs = [[[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(n_chunks)]
+           for _ in range(args.steps)]
+    for step in evs:
+        for row in step:
+            for e in row:
+                e.record(stream)
+    slot = {"k": 0, "c": 0}
+    if not p2p:
+        local_moe = moe.ops.local_moe
+
+        def profiled_local_moe(*a, **kw):
+            _lib.set_profile_events(evs[slot["k"]][min(slot["c"], n_chunks - 1)])
+            slot["c"] += 1
+            return local_moe(*a, **kw)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(dev) if rank == 0 else None
     torch.cuda.synchronize()
@@ -383,9 +399,15 @@ def bench_ep(args, world, rank, local):
     if clocks:
         clocks.start()
     start.record(stream)
+    if not p2p:
+        moe.ops.local_moe = profiled_local_moe
     for k in range(args.steps):
-        _lib.set_profile_events(evs[k])
+        slot["k"], slot["c"] = k, 0
+        if p2p:
+            _lib.set_profile_events(evs[k][0])
         moe(x, ids, tw)
+    if not p2p:
+        moe.ops.local_moe = local_moe
     _lib.set_profile_events(None)
     end.record(stream)
     torch.cuda.synchronize()
@@ -393,12 +415,12 @@ def bench_ep(args, world, rank, local):
     ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
     rank_ms = gather_over_ranks(start.elapsed_time(end) / args.steps, world)
     # per-step wall on the device: from one step's first stage event to the next step's
-    steps_ms = [evs[k][0].elapsed_time(evs[k + 1][0]) for k in range(args.steps - 1)]
+    steps_ms = [evs[k][0][0].elapsed_time(evs[k + 1][0][0]) for k in range(args.steps - 1)]
     rank_step_max = gather_over_ranks(max(steps_ms) if steps_ms else 0.0, world)
     rank_step_med = gather_over_ranks(statistics.median(steps_ms) if steps_ms else 0.0, world)
 
-    def stage_ms(a, b):
-        return sum(evs[k][a].elapsed_time(evs[k][b]) for k in range(args.steps)) / args.steps
+    def stage_ms(a, b):  # summed over the chunks of a step
+        return sum(row[a].elapsed_time(row[b]) for step in evs for row in step) / args.steps
 
     local_ms = {"align": stage_ms(0, 1), "gather": stage_ms(1, 2), "stage1": stage_ms(2, 3), "stage2": stage_ms(3, 4)}
     local_ms["exchange_and_rest"] = start.elapsed_time(end) / args.steps - sum(local_ms.values())
@@ -407,9 +429,13 @@ def bench_ep(args, world, rank, local):
     tot = torch.tensor([float(T_rank * cfg.topk)], dtype=torch.float64, device=dev)
     dist.all_reduce(tot)
     flops_total = 2.0 * float(tot.item()) * 3 * cfg.H * cfg.I
-    recv_ids = moe.last_recv_ids
-    local_routes = int((recv_ids >= 0).sum().item())
-    local_active = int(torch.unique(recv_ids[recv_ids >= 0]).numel())
+    # this rank's local routes and active experts, from every rank's routing
+    all_ids = [torch.empty_like(ids) for _ in range(world)]
+    dist.all_gather(all_ids, ids)
+    routed = torch.cat(all_ids).flatten().long()
+    mine_mask = placement.expert_rank.to(dev)[routed] == rank
+    local_routes = int(mine_mask.sum().item())
+    local_active = int(torch.unique(routed[mine_mask]).numel())
     s1_flops = 2.0 * local_routes * 2 * cfg.I * cfg.H
     s1_bytes = local_active * 2 * cfg.I * cfg.H * 2 + local_routes * cfg.H * 2 + local_routes * cfg.I * 2
     s1_s = local_ms["stage1"] * 1e-3
@@ -451,7 +477,9 @@ def bench_ep(args, world, rank, local):
     assert m.device_status() == 0, "device status flagged an error during timing"
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
     d2h = out_h.numel() * out_h.element_size()
-    send, recv = moe.last_counts
+    send, recv = moe.last_counts if not p2p else (None, None)
+    if p2p:
+        moe.close()
 
     if rank == 0:
         print(json.dumps({
@@ -464,6 +492,9 @@ def bench_ep(args, world, rank, local):
                                    f"top-{cfg.topk}, {T_rank} tokens per rank, {T_rank * world} in total",
                        "tokens_per_rank": T_rank, "parallelism": f"ep{world}", "experts_per_rank": len(mine),
                        "placement": "balanced (greedy LPT from an 8192-token calibration sample)",
+                       "ep_exchange": ("peer memory: NVLink loads of the token rows and partial outputs "
+                                       "inside the library's kernels, flag barriers; no collectives library")
+                       if p2p else f"NCCL all_to_all_single, {n_chunks} chunk(s)",
                        "l2": "inputs larger than L2 (expert weights streamed per step)"},
             "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
             "rank0_stage_ms": {k: round(v, 4) for k, v in local_ms.items()},
@@ -472,7 +503,10 @@ def bench_ep(args, world, rank, local):
             "roofline": roofline,
             "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * 12,
+            # per chunk: plan 4 (pair keys + 3 alignment), pack 1, local MoE 7 (3 alignment, block
+            # groups, gather, Stage1, Stage2), combine 1
+            # p2p: stage, 2 barriers, route, local MoE 7, combine = 12
+            "gpu_launches": args.steps * (12 if p2p else 13 * n_chunks),
             "clocks": clock_info,
         }), flush=True)
 
@@ -596,6 +630,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "nccl"],
+                    help="expert parallelism: exchange over peer memory in the library's kernels, or NCCL")
+    ap.add_argument("--ep-chunks", type=int, default=1,
+                    help="expert parallelism: token chunks whose exchanges overlap the local MoE of the others")
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
                     help="run_kernel: the reference drop-in on the reference's contest case --case")
     ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))

@@ -234,6 +234,59 @@ MOE_API int moe_ep_pack(const void* hidden_states, const void* topk_ids, int ids
 MOE_API int moe_ep_combine(const void* y, const int32_t* pair_slot, int64_t num_tokens, int64_t hidden,
                            int64_t world, int dtype, void* out, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Expert parallelism over peer memory. No reference counterpart (the reference runs on one
+ * device); the same operator as moe_fused, with its experts sharded over W ranks (one process per
+ * GPU of one node, NVLink peer access), and no collectives library or host synchronisation on
+ * the data path.
+ *
+ * Every rank owns one region of moe_ep_region_bytes(T_max, hidden, topk, W) bytes from
+ * moe_ep_region_alloc (device memory, zeroed), exports it with moe_ep_ipc_get (a 64-byte CUDA IPC
+ * handle) and maps every peer's region with moe_ep_ipc_open. `regions` below is a DEVICE array of
+ * W uint64 addresses: rank q's region as mapped in this process (this rank's own at [rank]).
+ * A forward on every rank, in this order, on one stream:
+ *   moe_ep_p2p_stage    copy this rank's hidden_states [T, H], topk_ids [T, k] (int32/int64) and
+ *                       topk_weights [T, k] (fp32/fp16/bf16) into its region (T <= T_max);
+ *   moe_ep_p2p_barrier  epoch e (increasing by one per barrier, starting at 1);
+ *   moe_ep_p2p_compute  (own_region = this rank's region, as allocated) route every rank's
+ *                       (token, slot) pairs whose expert this rank owns to its
+ *                       local experts (expert_rank / expert_local: [E] int32 device arrays),
+ *                       gather those token rows from the peers, run Stage1 / Stage2 with the
+ *                       local weights w_gate_up [E_local, 2I, H] / w_down [E_local, H, I], and
+ *                       combine each token's local routes into this rank's region;
+ *   moe_ep_p2p_barrier  epoch e + 1;
+ *   moe_ep_p2p_combine  out [T, H] = for each token, the sum over the ranks owning its experts of
+ *                       their partial rows (read from their regions, ascending rank order).
+ * A rank's region must not be freed or staged again before every rank has passed the second
+ * barrier of the forward. Requirements: 1 <= W <= 32, dtype MOE_F16 / MOE_BF16, H % 8 == 0.
+ * Barrier waits are bounded (2 s; status bit 0 on timeout).
+ * ---------------------------------------------------------------------------------------- */
+MOE_API size_t moe_ep_region_bytes(int64_t max_tokens, int64_t hidden, int64_t topk, int64_t world);
+MOE_API int moe_ep_region_alloc(size_t bytes, void** region);
+MOE_API int moe_ep_region_free(void* region);
+MOE_API int moe_ep_ipc_get(const void* region, void* handle_64_bytes);
+MOE_API int moe_ep_ipc_open(const void* handle_64_bytes, void** region);
+MOE_API int moe_ep_ipc_close(void* region);
+
+MOE_API int moe_ep_p2p_stage(void* region, const void* hidden_states, const void* topk_ids, int ids_dtype,
+                             const void* topk_weights, int weights_dtype, int64_t num_tokens, int64_t max_tokens,
+                             int64_t hidden, int64_t topk, int64_t world, int dtype, void* stream);
+
+MOE_API int moe_ep_p2p_barrier(const uint64_t* regions, int rank, int world, uint32_t epoch, void* stream);
+
+MOE_API size_t moe_ep_p2p_workspace_bytes(int64_t max_tokens, int64_t topk, int64_t world, int64_t local_experts,
+                                          int64_t hidden, int64_t intermediate, int dtype);
+
+MOE_API int moe_ep_p2p_compute(const uint64_t* regions, void* own_region, int rank, int world, int64_t max_tokens,
+                               int64_t hidden, int64_t intermediate, int64_t topk, const int32_t* expert_rank,
+                               const int32_t* expert_local, int64_t num_experts, const void* w_gate_up_local,
+                               const void* w_down_local, int64_t local_experts, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+MOE_API int moe_ep_p2p_combine(const uint64_t* regions, int rank, int world, int64_t num_tokens, int64_t max_tokens,
+                               int64_t hidden, int64_t topk, const int32_t* expert_rank, int64_t num_experts,
+                               int dtype, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -34,6 +34,20 @@ SIGNATURES = {
     "moe_device_status": (_int, [_c_void_p, _int, ctypes.POINTER(ctypes.c_uint32)]),
     "moe_set_profile_events": (_int, [ctypes.POINTER(_c_void_p), _int]),
     "moe_set_tile": (_int, [_int, ctypes.c_char_p]),
+    "moe_ep_region_bytes": (_size, [_i64, _i64, _i64, _i64]),
+    "moe_ep_region_alloc": (_int, [_size, ctypes.POINTER(_c_void_p)]),
+    "moe_ep_region_free": (_int, [_c_void_p]),
+    "moe_ep_ipc_get": (_int, [_c_void_p, _c_void_p]),
+    "moe_ep_ipc_open": (_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "moe_ep_ipc_close": (_int, [_c_void_p]),
+    "moe_ep_p2p_stage": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _c_void_p, _int, _i64, _i64, _i64, _i64, _i64,
+                                _int, _c_void_p]),
+    "moe_ep_p2p_barrier": (_int, [_c_void_p, _int, _int, ctypes.c_uint32, _c_void_p]),
+    "moe_ep_p2p_workspace_bytes": (_size, [_i64, _i64, _i64, _i64, _i64, _i64, _int]),
+    "moe_ep_p2p_compute": (_int, [_c_void_p, _c_void_p, _int, _int, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64,
+                                  _c_void_p, _c_void_p, _i64, _int, _c_void_p, _size, _c_void_p]),
+    "moe_ep_p2p_combine": (_int, [_c_void_p, _int, _int, _i64, _i64, _i64, _i64, _c_void_p, _i64, _int, _c_void_p,
+                                  _c_void_p]),
     "moe_run_kernel_workspace_bytes": (_size, [_i64, _i64, _int]),
     "moe_run_kernel": (
         _int,

@@ -1,0 +1,210 @@
+// ep_p2p.cuh — expert parallelism over peer memory: one process per GPU, every rank's "region"
+// mapped into every other rank by CUDA IPC, NVLink loads for the data path and one bounded
+// flag barrier on each side of the local MoE. No collectives library and no host
+// synchronisation in a forward.
+//
+// Region of rank s (layout in EpRegion, identical on every rank):
+//   sig[W]            barrier epochs written by the peers (slot q written by rank q)
+//   tcount            this forward's token count of rank s
+//   x[T_max, H]       rank s's hidden states
+//   ids[T_max, k]     rank s's top-k expert ids (int32)
+//   w[T_max, k]       rank s's top-k weights (fp32)
+//   y[W * T_max, H]   partial outputs rank s computed for every rank's tokens: row q * T_max + t
+//                     = sum over rank s's experts among token (q, t)'s top-k of weight * expert(x)
+// A forward on rank s: stage its inputs in its region -> barrier -> route every rank's (token,
+// slot) pairs whose expert it owns onto its local experts (reading the peers' ids and weights),
+// gather those token rows from the peers' x, run the grouped GEMMs, Stage2 combining into its own
+// y -> barrier -> out[t] = sum over the owners o of token t's experts of y_o[s * T_max + t], read
+// from the owners' regions in ascending rank order (deterministic given the partials).
+// Peer data is read with L2-only loads (ld.global.cg); nothing but the barrier flags is written
+// to peer memory, and no load uses a tensor map or cluster multicast.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace moe {
+
+struct EpRegion {
+  long long sig, tcount, x, ids, w, y, total;  // byte offsets
+};
+
+__host__ __device__ inline long long ep_round256(long long v) { return (v + 255) / 256 * 256; }
+
+__host__ __device__ inline EpRegion ep_region_layout(long long T_max, long long H, long long topk, long long W) {
+  EpRegion L{};
+  L.sig = 0;
+  L.tcount = ep_round256(W * 4);
+  L.x = 1024 > L.tcount + 256 ? 1024 : ep_round256(L.tcount + 4);
+  L.ids = ep_round256(L.x + T_max * H * 2);
+  L.w = ep_round256(L.ids + T_max * topk * 4);
+  L.y = ep_round256(L.w + T_max * topk * 4);
+  L.total = ep_round256(L.y + W * T_max * H * 2);
+  return L;
+}
+
+template <typename T>
+__device__ __forceinline__ const T* ep_at(const uint64_t* regions, int rank, long long off) {
+  return reinterpret_cast<const T*>(regions[rank] + static_cast<uint64_t>(off));
+}
+
+// Copy this rank's inputs into its region: x rows (16-byte vectors), ids as int32, weights as
+// fp32, and the token count.
+template <typename T, typename IdT>
+__global__ void ep_stage_kernel(uint8_t* __restrict__ region, EpRegion L, const T* __restrict__ x,
+                                const IdT* __restrict__ ids, const void* __restrict__ w, int w_dtype, int tokens, int H,
+                                int topk) {
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long nvec = static_cast<long long>(tokens) * H / 8;
+  const uint4* src = reinterpret_cast<const uint4*>(x);
+  uint4* dst = reinterpret_cast<uint4*>(region + L.x);
+  for (long long i = tid; i < nvec; i += nth) dst[i] = src[i];
+  int32_t* rid = reinterpret_cast<int32_t*>(region + L.ids);
+  float* rw = reinterpret_cast<float*>(region + L.w);
+  const long long nk = static_cast<long long>(tokens) * topk;
+  for (long long i = tid; i < nk; i += nth) {
+    const long long e = static_cast<long long>(ids[i]);
+    rid[i] = (e >= 0 && e < 0x7fffffff) ? static_cast<int32_t>(e) : -1;
+    float v;
+    if (w_dtype == 0)
+      v = reinterpret_cast<const float*>(w)[i];
+    else if (w_dtype == 1)
+      v = __half2float(reinterpret_cast<const __half*>(w)[i]);
+    else
+      v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w)[i]);
+    rw[i] = v;
+  }
+  if (tid == 0) *reinterpret_cast<int32_t*>(region + L.tcount) = tokens;
+}
+
+// Barrier over the W ranks: thread q < W stores `epoch` into rank q's slot for this rank
+// (release, system scope), then waits until rank q has stored `epoch` (or later) into this
+// rank's slot q (acquire, system scope). Bounded: after MOE_WAIT_NS the wait gives up and
+// flags the status word. Launched as one block of 32 threads per rank, each on its own GPU.
+__global__ void ep_barrier_kernel(const uint64_t* __restrict__ regions, long long sig_off, int rank, int W,
+                                  uint32_t epoch, uint32_t* status) {
+  const int q = threadIdx.x;
+  if (q < W) {
+    uint32_t* slot = reinterpret_cast<uint32_t*>(regions[q] + static_cast<uint64_t>(sig_off)) + rank;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(slot), "r"(epoch) : "memory");
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(regions[rank] + static_cast<uint64_t>(sig_off)) + q;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (static_cast<int32_t>(v - epoch) >= 0) break;
+      if (globaltimer_ns() - t0 > MOE_WAIT_NS) {
+        if (status) atomicOr(status, kStatusWaitTimeout);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
+// Virtual route r = (s * T_max + t) * k + j covers slot j of token t of rank s. local_ids[r] =
+// this rank's local index of that expert if this rank owns it (and t < rank s's token count),
+// else -1; local_w[r] = its routing weight.
+__global__ void ep_p2p_route_kernel(const uint64_t* __restrict__ regions, EpRegion L, int W, int T_max, int topk,
+                                    const int32_t* __restrict__ expert_rank, const int32_t* __restrict__ expert_local,
+                                    int E, int rank, int32_t* __restrict__ local_ids, float* __restrict__ local_w) {
+  const long long per_rank = static_cast<long long>(T_max) * topk;
+  const long long n = per_rank * W;
+  for (long long r = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; r < n;
+       r += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(r / per_rank);
+    const long long i = r - s * per_rank;  // t * k + j inside rank s
+    const int tokens = __ldcg(ep_at<int32_t>(regions, s, L.tcount));
+    int lid = -1;
+    float wv = 0.0f;
+    if (i / topk < tokens) {
+      const int e = __ldcg(ep_at<int32_t>(regions, s, L.ids) + i);
+      if (e >= 0 && e < E && expert_rank[e] == rank) {
+        lid = expert_local[e];
+        wv = __ldcg(ep_at<float>(regions, s, L.w) + i);
+      }
+    }
+    local_ids[r] = lid;
+    local_w[r] = wv;
+  }
+}
+
+// xs[route_slot[r]] = x row of token (s, t) of route r, read from rank s's region; and zero
+// this rank's y rows of every token with at least one local route (the Stage2 combine target).
+// One warp per work item, 16-byte vectors.
+template <typename T>
+__global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int T_max,
+                                        int topk, int W, const int32_t* __restrict__ route_slot,
+                                        const int32_t* __restrict__ local_ids, int H, T* __restrict__ xs) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const int vecs = H / 8;
+  const long long R = static_cast<long long>(W) * T_max * topk;
+  const long long rows = static_cast<long long>(W) * T_max;
+  uint4* y = reinterpret_cast<uint4*>(regions[rank] + static_cast<uint64_t>(L.y));
+  for (long long item = warp_id; item < R + rows; item += n_warps) {
+    if (item < R) {
+      const int slot = route_slot[item];
+      if (slot < 0) continue;
+      const long long tok = item / topk;  // s * T_max + t
+      const int s = static_cast<int>(tok / T_max);
+      const long long t = tok - static_cast<long long>(s) * T_max;
+      const uint4* src = ep_at<uint4>(regions, s, L.x) + t * vecs;
+      uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<size_t>(slot) * H);
+      for (int v = lane; v < vecs; v += 32) dst[v] = __ldcg(src + v);
+    } else {
+      const long long tok = item - R;
+      bool served = false;
+      for (int j = 0; j < topk; ++j) served |= local_ids[tok * topk + j] >= 0;
+      if (!served) continue;
+      uint4* dst = y + tok * vecs;
+      for (int v = lane; v < vecs; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// out[t] = sum over the distinct owner ranks o of token t's experts (ascending o) of rank o's
+// y[rank * T_max + t], accumulated in fp32. One warp per token, 8 elements per lane step.
+template <typename T>
+__global__ void ep_combine_pull_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int W, int T_max,
+                                       int tokens, int H, int topk, const int32_t* __restrict__ expert_rank, int E,
+                                       T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const int vecs = H / 8;
+  const int32_t* ids = ep_at<int32_t>(regions, rank, L.ids);
+  for (long long t = warp_id; t < tokens; t += n_warps) {
+    uint32_t owners = 0;  // bit o: rank o owns one of the token's experts (W <= 32)
+    for (int j = 0; j < topk; ++j) {
+      const int e = ids[t * topk + j];
+      if (e >= 0 && e < E) {
+        const int o = expert_rank[e];
+        if (o >= 0 && o < W) owners |= 1u << o;
+      }
+    }
+    for (int v = lane; v < vecs; v += 32) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int o = 0; o < W; ++o) {
+        if (!(owners >> o & 1u)) continue;
+        const uint4 p = __ldcg(ep_at<uint4>(regions, o, L.y) + (static_cast<long long>(rank) * T_max + t) * vecs + v);
+        const T* pe = reinterpret_cast<const T*>(&p);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(pe[i]);
+      }
+      uint4 r;
+      T* re = reinterpret_cast<T*>(&r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) re[i] = static_cast<T>(acc[i]);
+      reinterpret_cast<uint4*>(out + t * static_cast<long long>(H))[v] = r;
+    }
+  }
+}
+
+}  // namespace moe

@@ -14,6 +14,7 @@
 
 #include "../../include/moe_b200.h"
 #include "ep_kernels.cuh"
+#include "ep_p2p.cuh"
 #include "gather_quant.cuh"
 #include "moe_gemm.cuh"
 #include "moe_gemm_pair.cuh"
@@ -539,8 +540,7 @@ struct FusedLayout {
   int64_t P_max, nblk_max;
 };
 
-FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8) {
-  const bool lsu = a_path_lsu();
+FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8, bool lsu) {
   FusedLayout L{};
   const int64_t R = T * topk;
   L.P_max = moe_max_padded_rows(R, E, kBM);
@@ -805,13 +805,22 @@ int moe_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, 
 size_t moe_fused_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, false).total;
+  return fused_layout(T, topk, E, H, I, false, a_path_lsu()).total;
 }
+
+// Expert parallelism over peer memory: token rows come from the ranks' regions (route r = (s *
+// T_max + t) * topk + j reads row t of rank s) and `out` is this rank's partial-output block; the
+// fused pipeline is otherwise unchanged.
+struct PeerSource {
+  const uint64_t* regions;
+  EpRegion L;
+  int rank, W, T_max;
+};
 
 static int fused_common(bool int8, const void* x, const void* w13, const float* w13_scale, const void* w2,
                         const float* w2_scale, const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out,
                         int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+                        size_t workspace_bytes, void* stream, const PeerSource* peer = nullptr) {
   t_last_error.clear();
   MOE_TRY(check_common(H, I, E, dtype, int8 ? 16 : 8));
   if (T < 0 || topk < 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be >= 0 and topk >= 1");
@@ -827,7 +836,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (!x || !w13 || !w2 || !ids || !tw || !out) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
   if (int8 && (!w13_scale || !w2_scale)) return fail(MOE_ERR_INVALID_ARG, "null weight scales");
   if (!aligned16(x) || !aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "hidden_states/out must be 16-byte aligned");
-  const FusedLayout L = fused_layout(T, topk, E, H, I, int8);
+  if (peer && int8) return fail(MOE_ERR_UNSUPPORTED, "the int8 route has no peer-memory expert-parallel mode");
+  const bool lsu = a_path_lsu() && !peer;
+  const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu);
   if (!workspace || workspace_bytes < L.total) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", L.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
 
@@ -851,10 +862,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   void* U = ws + L.u;
   int32_t* groups = reinterpret_cast<int32_t*>(ws + L.groups);
   int32_t* ngroups = groups + L.nblk_max;
-  const bool lsu = a_path_lsu();
   const int elt = int8 ? 1 : 2;
-  // expected blocks per expert: routes per expert / 128, plus half a block of padding
-  const double bpe = static_cast<double>(R) / static_cast<double>(E) / kBM + 0.5;
+  // expected blocks per expert: routes per expert / 128, plus half a block of padding (peer mode:
+  // about 1 / W of the virtual routes land on this rank)
+  const double bpe = static_cast<double>(R) / (peer ? peer->W : 1) / static_cast<double>(E) / kBM + 0.5;
   const TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe), tc2 = usable_cfg(2, I, elt, lsu, bpe);
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
@@ -886,6 +897,16 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_CUDA(cudaGetLastError());
       MOE_CUDA(cudaMemsetAsync(amax, 0, sizeof(float) * (size_t)L.P_max, s));
     }
+  } else if (peer) {  // token rows from the ranks' regions; zero the served partial rows
+    if (dtype == MOE_F16)
+      gather_rows_peer_kernel<__half><<<gblocks, 256, 0, s>>>(peer->regions, peer->L, peer->rank, peer->T_max,
+                                                              (int)topk, peer->W, slot, static_cast<const int32_t*>(ids),
+                                                              (int)H, static_cast<__half*>(xs));
+    else
+      gather_rows_peer_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
+          peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs));
+    MOE_CUDA(cudaGetLastError());
   } else if (dtype == MOE_F16) {
     if (int8)
       gather_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
@@ -1043,7 +1064,7 @@ int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols,
 size_t moe_fused_int8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, true).total;
+  return fused_layout(T, topk, E, H, I, true, a_path_lsu()).total;
 }
 
 int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, const void* w2_q, const float* w2_scale,
@@ -1146,6 +1167,167 @@ int moe_ep_combine(const void* y, const int32_t* pair_slot, int64_t T, int64_t H
   else
     ep_combine_kernel<__nv_bfloat16><<<sms * 8, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(y), pair_slot, (int)T,
                                                              (int)H, (int)W, static_cast<__nv_bfloat16*>(out));
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+// ---------------------------------------------------------------------------- EP over peer memory
+static int ep_p2p_check(int64_t T_max, int64_t H, int64_t topk, int64_t W) {
+  if (T_max < 1 || H < 8 || H % 8 != 0 || topk < 1 || W < 1 || W > 32)
+    return fail(MOE_ERR_INVALID_ARG, "need max_tokens >= 1, hidden a multiple of 8, topk >= 1, 1 <= world <= 32");
+  if (W * T_max * topk > (int64_t(1) << 31) - 1 || W * T_max > (int64_t(1) << 30))
+    return fail(MOE_ERR_INVALID_ARG, "world * max_tokens * topk exceeds 32-bit indexing");
+  return MOE_OK;
+}
+
+size_t moe_ep_region_bytes(int64_t T_max, int64_t H, int64_t topk, int64_t W) {
+  if (T_max < 1 || H < 8 || topk < 1 || W < 1 || W > 32) return 0;
+  return static_cast<size_t>(ep_region_layout(T_max, H, topk, W).total);
+}
+
+int moe_ep_region_alloc(size_t bytes, void** region) {
+  t_last_error.clear();
+  if (!region || bytes == 0) return fail(MOE_ERR_INVALID_ARG, "null region pointer or zero size");
+  *region = nullptr;
+  MOE_CUDA(cudaMalloc(region, bytes));
+  MOE_CUDA(cudaMemset(*region, 0, bytes));
+  return MOE_OK;
+}
+
+int moe_ep_region_free(void* region) {
+  t_last_error.clear();
+  if (region) MOE_CUDA(cudaFree(region));
+  return MOE_OK;
+}
+
+int moe_ep_ipc_get(const void* region, void* handle) {
+  t_last_error.clear();
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  if (!region || !handle) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  MOE_CUDA(cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), const_cast<void*>(region)));
+  return MOE_OK;
+}
+
+int moe_ep_ipc_open(const void* handle, void** region) {
+  t_last_error.clear();
+  if (!region || !handle) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  MOE_CUDA(cudaIpcOpenMemHandle(region, h, cudaIpcMemLazyEnablePeerAccess));
+  return MOE_OK;
+}
+
+int moe_ep_ipc_close(void* region) {
+  t_last_error.clear();
+  if (region) MOE_CUDA(cudaIpcCloseMemHandle(region));
+  return MOE_OK;
+}
+
+int moe_ep_p2p_stage(void* region, const void* x, const void* ids, int ids_dtype, const void* tw, int w_dtype, int64_t T,
+                     int64_t T_max, int64_t H, int64_t topk, int64_t W, int dtype, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(ep_p2p_check(T_max, H, topk, W));
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (ids_dtype != MOE_I32 && ids_dtype != MOE_I64) return fail(MOE_ERR_INVALID_ARG, "topk_ids must be int32 or int64");
+  if (w_dtype != MOE_F32 && w_dtype != MOE_F16 && w_dtype != MOE_BF16)
+    return fail(MOE_ERR_INVALID_ARG, "topk_weights must be fp32, fp16 or bf16");
+  if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
+  if (!region || (T > 0 && (!x || !ids || !tw))) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (T > 0 && !aligned16(x)) return fail(MOE_ERR_ALIGNMENT, "hidden_states must be 16-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  const EpRegion L = ep_region_layout(T_max, H, topk, W);
+  const int wd = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* rg = static_cast<uint8_t*>(region);
+  // one element type suffices for the row copy (16-byte vectors)
+  if (ids_dtype == MOE_I32)
+    ep_stage_kernel<__half, int32_t><<<sms * 4, 256, 0, s>>>(rg, L, static_cast<const __half*>(x),
+                                                            static_cast<const int32_t*>(ids), tw, wd, (int)T, (int)H,
+                                                            (int)topk);
+  else
+    ep_stage_kernel<__half, int64_t><<<sms * 4, 256, 0, s>>>(rg, L, static_cast<const __half*>(x),
+                                                            static_cast<const int64_t*>(ids), tw, wd, (int)T, (int)H,
+                                                            (int)topk);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+int moe_ep_p2p_barrier(const uint64_t* regions, int rank, int W, uint32_t epoch, void* stream) {
+  t_last_error.clear();
+  if (!regions || W < 1 || W > 32 || rank < 0 || rank >= W) return fail(MOE_ERR_INVALID_ARG, "bad regions/rank/world");
+  int dev;
+  MOE_TRY(current_device(&dev));
+  uint32_t* status;
+  MOE_TRY(device_status_ptr(dev, &status));
+  ep_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(regions, 0, rank, W, epoch, status);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+static size_t ep_p2p_extra_bytes(int64_t T_max, int64_t topk, int64_t W) {
+  return 2 * round_up(sizeof(int32_t) * static_cast<size_t>(W * T_max * topk), 256);
+}
+
+size_t moe_ep_p2p_workspace_bytes(int64_t T_max, int64_t topk, int64_t W, int64_t E_local, int64_t H, int64_t I,
+                                  int dtype) {
+  (void)dtype;
+  if (T_max < 1 || topk < 1 || W < 1 || W > 32 || E_local < 1 || H < 1 || I < 1) return 0;
+  return fused_layout(W * T_max, topk, E_local, H, I, false, false).total + ep_p2p_extra_bytes(T_max, topk, W);
+}
+
+int moe_ep_p2p_compute(const uint64_t* regions, void* own_region, int rank, int W, int64_t T_max, int64_t H, int64_t I,
+                       int64_t topk,
+                       const int32_t* expert_rank, const int32_t* expert_local, int64_t E, const void* w13,
+                       const void* w2, int64_t E_local, int dtype, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  t_last_error.clear();
+  MOE_TRY(ep_p2p_check(T_max, H, topk, W));
+  if (!regions || !own_region || rank < 0 || rank >= W || !expert_rank || !expert_local || E < 1 || E_local < 1)
+    return fail(MOE_ERR_INVALID_ARG, "bad regions/rank/expert tables");
+  const size_t need = moe_ep_p2p_workspace_bytes(T_max, topk, W, E_local, H, I, dtype);
+  if (!workspace || workspace_bytes < need) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", need);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  const EpRegion L = ep_region_layout(T_max, H, topk, W);
+  uint8_t* extra = static_cast<uint8_t*>(workspace) + (need - ep_p2p_extra_bytes(T_max, topk, W));
+  int32_t* local_ids = reinterpret_cast<int32_t*>(extra);
+  float* local_w = reinterpret_cast<float*>(extra + ep_p2p_extra_bytes(T_max, topk, W) / 2);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ep_p2p_route_kernel<<<sms * 4, 256, 0, s>>>(regions, L, W, (int)T_max, (int)topk, expert_rank, expert_local, (int)E,
+                                              rank, local_ids, local_w);
+  MOE_CUDA(cudaGetLastError());
+  PeerSource peer{regions, L, rank, W, (int)T_max};
+  void* y = static_cast<uint8_t*>(own_region) + L.y;
+  return fused_common(false, own_region, w13, nullptr, w2, nullptr, local_ids, MOE_I32,
+                      local_w, MOE_F32, y, W * T_max, H, I, E_local, topk, dtype, workspace,
+                      need - ep_p2p_extra_bytes(T_max, topk, W), stream, &peer);
+}
+
+int moe_ep_p2p_combine(const uint64_t* regions, int rank, int W, int64_t T, int64_t T_max, int64_t H, int64_t topk,
+                       const int32_t* expert_rank, int64_t E, int dtype, void* out, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(ep_p2p_check(T_max, H, topk, W));
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
+  if (T == 0) return MOE_OK;
+  if (!regions || rank < 0 || rank >= W || !expert_rank || !out) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (!aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "out must be 16-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  const EpRegion L = ep_region_layout(T_max, H, topk, W);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MOE_F16)
+    ep_combine_pull_kernel<__half><<<sms * 8, 256, 0, s>>>(regions, L, rank, W, (int)T_max, (int)T, (int)H, (int)topk,
+                                                           expert_rank, (int)E, static_cast<__half*>(out));
+  else
+    ep_combine_pull_kernel<__nv_bfloat16><<<sms * 8, 256, 0, s>>>(regions, L, rank, W, (int)T_max, (int)T, (int)H,
+                                                                  (int)topk, expert_rank, (int)E,
+                                                                  static_cast<__nv_bfloat16*>(out));
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }

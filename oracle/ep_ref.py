@@ -71,5 +71,9 @@ class ReferenceOps:
     def local_moe(self, x, ids, w, w13, w2):
         return fused_moe_ref(x, w13, w2, ids, w).to(x.dtype)
 
-    def combine(self, y_back, plan, T, H, dtype):
-        return combine_ref(y_back, plan.pair_slot, T, self.world, dtype)
+    def combine(self, y_back, plan, T, H, dtype, out=None):
+        res = combine_ref(y_back, plan.pair_slot, T, self.world, dtype)
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res

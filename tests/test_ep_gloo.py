@@ -43,7 +43,7 @@ def _placement(kind):
     return ExpertPlacement.balanced(loads, WORLD)
 
 
-def _worker(rank, port, out_dir, kind, fault):
+def _worker(rank, port, out_dir, kind, fault, chunks=1, cut=T_PER_RANK):
     import datetime
 
     import torch.distributed as dist
@@ -68,8 +68,9 @@ def _worker(rank, port, out_dir, kind, fault):
                 return p
 
             ops.plan = bad_plan
-        moe = ExpertParallelMoE(w13[mine].contiguous(), w2[mine].contiguous(), placement, ops=ops)
-        sl = slice(rank * T_PER_RANK, (rank + 1) * T_PER_RANK)
+        moe = ExpertParallelMoE(w13[mine].contiguous(), w2[mine].contiguous(), placement, ops=ops, chunks=chunks,
+                                min_chunk_tokens=8)
+        sl = slice(0, cut) if rank == 0 else slice(cut, WORLD * T_PER_RANK)
         if fault == "rank_raises" and rank == 1:
             raise RuntimeError("injected failure on rank 1 before the exchange")
         out = moe(x[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous())
@@ -84,10 +85,11 @@ def _worker(rank, port, out_dir, kind, fault):
         json.dump(result, f)
 
 
-def _run(tmp_path, kind="contiguous", fault=None):
+def _run(tmp_path, kind="contiguous", fault=None, chunks=1, cut=T_PER_RANK):
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, port, str(tmp_path), kind, fault)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, str(tmp_path), kind, fault, chunks, cut))
+             for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:
@@ -98,11 +100,14 @@ def _run(tmp_path, kind="contiguous", fault=None):
     return [json.load(open(tmp_path / f"rank{r}.json")) for r in range(WORLD)]
 
 
-@pytest.mark.parametrize("kind", ["contiguous", "balanced"])
-def test_ep_matches_single_process_oracle(tmp_path, kind):
+@pytest.mark.parametrize("kind,chunks,cut", [("contiguous", 1, T_PER_RANK), ("balanced", 1, T_PER_RANK),
+                                              ("balanced", 3, 30)])
+def test_ep_matches_single_process_oracle(tmp_path, kind, chunks, cut):
+    """chunks=3 with 30 / 18 tokens per rank: rank 0 runs three chunks, rank 1 two (plus one round of
+    empty sends), so the chunked exchange must line up across ranks with different chunk counts."""
     from oracle.moe_ref import fused_moe_ref
 
-    res = _run(tmp_path, kind)
+    res = _run(tmp_path, kind, chunks=chunks, cut=cut)
     for r in res:
         assert "error" not in r, r.get("trace")
     x, w13, w2, ids, w = _global_problem()

@@ -14,7 +14,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from muxi_race_b200.ep import CudaOps, ExpertParallelMoE, ExpertPlacement
+from muxi_race_b200.ep import CudaOps, ExpertParallelMoE, ExpertPlacement, PeerMemoryEP
 from oracle.ep_ref import combine_ref, pack_ref, plan_ref
 
 pytestmark = pytest.mark.gpu
@@ -58,7 +58,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew):
+def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="nccl"):
     import torch.distributed as dist
 
     from muxi_race_b200.workloads import MoeConfig, make_hidden, make_routing, make_weights
@@ -77,17 +77,29 @@ def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew):
         loads = torch.bincount(ids.flatten().long(), minlength=E).float().cpu().tolist()
         placement = ExpertPlacement.balanced(loads, world)
         mine = placement.local_experts(rank)
-        moe = ExpertParallelMoE(w13[mine].contiguous(), w2[mine].contiguous(), placement)
         sl = slice(rank * T_per_rank, (rank + 1) * T_per_rank)
+        if mode == "p2p":
+            moe = PeerMemoryEP(w13[mine].contiguous(), w2[mine].contiguous(), placement, max_tokens=T_per_rank, topk=k)
+        else:
+            moe = ExpertParallelMoE(w13[mine].contiguous(), w2[mine].contiguous(), placement)
         out = moe(x[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous())
         out2 = moe(x[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous())
         ref = fused_moe_ref(x[sl], w13, w2, ids[sl], w[sl])
+        # a forward with a different token count on every rank (rank r drops its last 13 * r + 1)
+        cut = slice(rank * T_per_rank, (rank + 1) * T_per_rank - 13 * rank - 1)
+        out3 = moe(x[cut].contiguous(), ids[cut].contiguous(), w[cut].contiguous())
+        ref3 = fused_moe_ref(x[cut], w13, w2, ids[cut], w[cut])
         torch.cuda.synchronize()
         err = (out.float() - ref).abs()
-        res["bad"] = int((err > 1e-2 + 1e-2 * ref.abs()).sum())
-        res["max_err"] = float(err.max())
+        err3 = (out3.float() - ref3).abs()
+        res["bad"] = int((err > 1e-2 + 1e-2 * ref.abs()).sum()) + int((err3 > 1e-2 + 1e-2 * ref3.abs()).sum())
+        res["max_err"] = max(float(err.max()), float(err3.max()))
         res["repeat_max_diff"] = float((out2.float() - out.float()).abs().max())
-        res["counts"] = moe.last_counts
+        res["counts"] = moe.last_counts if mode != "p2p" else None
+        from muxi_race_b200 import device_status
+        res["status"] = device_status()
+        if mode == "p2p":
+            moe.close()
         dist.barrier()
         dist.destroy_process_group()
     except Exception as exc:
@@ -97,15 +109,18 @@ def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew):
         json.dump(res, f)
 
 
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("skew", [0.0, 1.1])
-def test_ep_multi_gpu_matches_oracle(cuda_device, tmp_path, skew):
+def test_ep_multi_gpu_matches_oracle(cuda_device, tmp_path, skew, mode):
+    """NCCL all-to-all mode and peer-memory mode against the single-process oracle, including a
+    forward where every rank has a different token count."""
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("expert parallelism needs at least 2 GPUs")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    args = (world, port, str(tmp_path), 256, 64, 1024, 512, 8, skew)
+    args = (world, port, str(tmp_path), 256, 64, 1024, 512, 8, skew, mode)
     procs = [ctx.Process(target=_ep_worker, args=(r,) + args) for r in range(world)]
     for p in procs:
         p.start()
@@ -119,7 +134,27 @@ def test_ep_multi_gpu_matches_oracle(cuda_device, tmp_path, skew):
         assert "error" not in r, r.get("trace")
         assert r["bad"] == 0, r
         assert r["repeat_max_diff"] < 2e-2, r
+        assert r["status"] == 0, r
+    if mode == "p2p":
+        return
     # what rank a sends to rank b, rank b receives from rank a
     for a in range(world):
         for b in range(world):
             assert res[a]["counts"][0][b] == res[b]["counts"][1][a]
+
+
+def test_ep_p2p_single_rank_matches_oracle(cuda_device, tmp_path):
+    """The peer-memory path with one rank (its own region only): routing, gather, grouped GEMMs,
+    partial rows and the pull-combine against the oracle on one GPU."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    p = ctx.Process(target=_ep_worker, args=(0, 1, port, str(tmp_path), 300, 32, 1024, 512, 8, 1.1, "p2p"))
+    p.start()
+    p.join(timeout=600)
+    if p.is_alive():
+        p.kill()
+        pytest.fail("the single-rank peer-memory run did not finish")
+    r = json.load(open(tmp_path / "rank0.json"))
+    assert "error" not in r, r.get("trace")
+    assert r["bad"] == 0 and r["status"] == 0, r
+    assert r["repeat_max_diff"] < 2e-2, r
