@@ -18,7 +18,8 @@ cpu_baseline = the oracle (a port of the reference's PyTorch operator) on the ho
          bounded sample of experts, rank 0 at N=1 only.
 With --gpus N > 1 the step is the expert-parallel fused MoE (muxi_race_b200.ep): the 256 experts
 are sharded E/N per GPU (load-balanced placement from a calibration routing sample) and tokens are
-dispatched and combined with NCCL all-to-all. Default: weak scaling, 4096 tokens per rank (N = 1 is
+dispatched and combined over NVLink peer memory by the library's kernels (--ep-mode p2p, default) or
+with NCCL all-to-all (--ep-mode nccl). Default: weak scaling, 4096 tokens per rank (N = 1 is
 exactly cfg3, N = 8 is the 32768-token cfg5 size); --config cfg5: strong scaling, 32768 tokens in
 total with the Zipf-skewed routing. value = all ranks' algorithmic FLOPs / the slowest rank's time.
 --impl reference times the reference's CPU operator (the oracle port) instead.
@@ -315,7 +316,8 @@ def bench_ours(args, world, rank, local):
             "workload": f"{cfg.name}: fused MoE T={cfg.T} H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
             "tokens_per_rank": cfg.T, "routed_rows_per_rank": routes, "active_experts": active,
             "parallelism": "replicas" if world > 1 else "single",
-            "l2": "inputs larger than L2 (22.5 GB of expert weights streamed per step)",
+            "l2": f"inputs larger than L2 ({active * 3 * cfg.H * cfg.I * (1 if cfg.int8 else 2) / 1e9:.1f} GB of "
+                  "expert weights streamed per step)",
         },
         "ms_per_call": round(ms, 4),
         "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12, 2),
