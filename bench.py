@@ -18,8 +18,8 @@ cpu_baseline = the oracle (a port of the reference's PyTorch operator) on the ho
          bounded sample of experts, rank 0 at N=1 only.
 With --gpus N > 1 the step is the expert-parallel fused MoE (muxi_race_b200.ep): the 256 experts
 are sharded E/N per GPU (load-balanced placement from a calibration routing sample) and tokens are
-dispatched and combined over NVLink peer memory by the library's kernels (--ep-mode p2p, default) or
-with NCCL all-to-all (--ep-mode nccl). Default: weak scaling, 4096 tokens per rank (N = 1 is
+dispatched and combined with NCCL all-to-all (--ep-mode nccl, default) or over NVLink peer memory by
+the library's kernels (--ep-mode p2p). Default: weak scaling, 4096 tokens per rank (N = 1 is
 exactly cfg3, N = 8 is the 32768-token cfg5 size); --config cfg5: strong scaling, 32768 tokens in
 total with the Zipf-skewed routing. value = all ranks' algorithmic FLOPs / the slowest rank's time.
 --impl reference times the reference's CPU operator (the oracle port) instead.
@@ -217,7 +217,8 @@ def bench_ours(args, world, rank, local):
     for _ in range(args.warmup):
         fn(x, ids, tw, out)
     torch.cuda.synchronize()
-    assert m.device_status() == 0, "device status flagged an error during warm-up"
+    st = m.device_status()
+    assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after warm-up"
 
     # ---- device-resident timing, with stage-boundary events on the launch stream
     stream = torch.cuda.current_stream(dev)
@@ -265,6 +266,8 @@ def bench_ours(args, world, rank, local):
         fn(x_d, ids_d, tw_d, out)
         out_h.copy_(out, non_blocking=True)
 
+    torch.cuda.synchronize()
+    barrier(world)  # the ranks enter the end-to-end phase together
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()
@@ -280,7 +283,8 @@ def bench_ours(args, world, rank, local):
     clock_info = clocks.stop()  # sampled across both timed regions
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
     d2h = out_h.numel() * out_h.element_size()
-    assert m.device_status() == 0, "device status flagged an error during timing"
+    st = m.device_status()
+    assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after timing"
 
     # ---- roofline of the dominant kernel (Stage1): algorithmic bytes per launch / launch time
     elt = 1 if cfg.int8 else 2
@@ -376,7 +380,8 @@ def bench_ep(args, world, rank, local):
     for _ in range(args.warmup):
         moe(x, ids, tw)
     torch.cuda.synchronize()
-    assert m.device_status() == 0, "device status flagged an error during warm-up"
+    st = m.device_status()
+    assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after warm-up"
 
     # stage-boundary events for every local fused-MoE call (one per chunk) of every timed step
     stream = torch.cuda.current_stream(dev)
@@ -463,6 +468,8 @@ def bench_ep(args, world, rank, local):
         tw_d.copy_(tw_h, non_blocking=True)
         out_h.copy_(moe(x_d, ids_d, tw_d), non_blocking=True)
 
+    torch.cuda.synchronize()
+    barrier(world)  # the ranks enter the end-to-end phase together
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()
@@ -476,7 +483,8 @@ def bench_ep(args, world, rank, local):
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
     clock_info = clocks.stop() if clocks else None  # sampled across both timed regions
-    assert m.device_status() == 0, "device status flagged an error during timing"
+    st = m.device_status()
+    assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after timing"
     h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
     d2h = out_h.numel() * out_h.element_size()
     send, recv = moe.last_counts if not p2p else (None, None)
@@ -632,8 +640,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "nccl"],
-                    help="expert parallelism: exchange over peer memory in the library's kernels, or NCCL")
+    ap.add_argument("--ep-mode", default="nccl", choices=["p2p", "nccl"],
+                    help="expert parallelism: NCCL all-to-all exchange, or over peer memory in the library's kernels")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallelism: token chunks whose exchanges overlap the local MoE of the others")
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],

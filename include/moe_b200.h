@@ -259,7 +259,8 @@ MOE_API int moe_ep_combine(const void* y, const int32_t* pair_slot, int64_t num_
  *                       their partial rows (read from their regions, ascending rank order).
  * A rank's region must not be freed or staged again before every rank has passed the second
  * barrier of the forward. Requirements: 1 <= W <= 32, dtype MOE_F16 / MOE_BF16, H % 8 == 0.
- * Barrier waits are bounded (2 s; status bit 0 on timeout).
+ * Barrier waits are bounded (60 s, far above any legitimate skew between the ranks' host threads;
+ * status bit 0 on timeout).
  * ---------------------------------------------------------------------------------------- */
 MOE_API size_t moe_ep_region_bytes(int64_t max_tokens, int64_t hidden, int64_t topk, int64_t world);
 MOE_API int moe_ep_region_alloc(size_t bytes, void** region);

@@ -82,8 +82,13 @@ __global__ void ep_stage_kernel(uint8_t* __restrict__ region, EpRegion L, const 
 
 // Barrier over the W ranks: thread q < W stores `epoch` into rank q's slot for this rank
 // (release, system scope), then waits until rank q has stored `epoch` (or later) into this
-// rank's slot q (acquire, system scope). Bounded: after MOE_WAIT_NS the wait gives up and
-// flags the status word. Launched as one block of 32 threads per rank, each on its own GPU.
+// rank's slot q (acquire, system scope). Bounded: after kEpBarrierWaitNs the wait gives up and
+// flags the status word. The bound is far above the pipeline waits' because the ranks' host
+// threads enqueue their forwards independently (pinning host memory or other host work can put
+// one rank seconds behind another). Launched as one block of 32 threads per rank, each on its
+// own GPU.
+constexpr uint64_t kEpBarrierWaitNs = 60ull * 1000000000ull;
+
 __global__ void ep_barrier_kernel(const uint64_t* __restrict__ regions, long long sig_off, int rank, int W,
                                   uint32_t epoch, uint32_t* status) {
   const int q = threadIdx.x;
@@ -97,7 +102,7 @@ __global__ void ep_barrier_kernel(const uint64_t* __restrict__ regions, long lon
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
       if (static_cast<int32_t>(v - epoch) >= 0) break;
-      if (globaltimer_ns() - t0 > MOE_WAIT_NS) {
+      if (globaltimer_ns() - t0 > kEpBarrierWaitNs) {
         if (status) atomicOr(status, kStatusWaitTimeout);
         break;
       }
@@ -157,7 +162,17 @@ __global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, Ep
       const long long t = tok - static_cast<long long>(s) * T_max;
       const uint4* src = ep_at<uint4>(regions, s, L.x) + t * vecs;
       uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<size_t>(slot) * H);
-      for (int v = lane; v < vecs; v += 32) dst[v] = __ldcg(src + v);
+      // eight 16-byte loads in flight per lane: peer reads cross NVLink with microseconds of latency
+      constexpr int U = 8;
+      for (int v0 = lane; v0 < vecs; v0 += 32 * U) {
+        uint4 tmp[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + u * 32 < vecs) tmp[u] = __ldcg(src + v0 + u * 32);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + u * 32 < vecs) dst[v0 + u * 32] = tmp[u];
+      }
     } else {
       const long long tok = item - R;
       bool served = false;
@@ -189,14 +204,26 @@ __global__ void ep_combine_pull_kernel(const uint64_t* __restrict__ regions, EpR
         if (o >= 0 && o < W) owners |= 1u << o;
       }
     }
+    int ow[32];  // owner ranks in ascending order
+    int n_ow = 0;
+    for (int o = 0; o < W; ++o)
+      if (owners >> o & 1u) ow[n_ow++] = o;
+    const long long row = (static_cast<long long>(rank) * T_max + t) * vecs;
     for (int v = lane; v < vecs; v += 32) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int o = 0; o < W; ++o) {
-        if (!(owners >> o & 1u)) continue;
-        const uint4 p = __ldcg(ep_at<uint4>(regions, o, L.y) + (static_cast<long long>(rank) * T_max + t) * vecs + v);
-        const T* pe = reinterpret_cast<const T*>(&p);
+      // all owners' vectors requested before any is summed (up to 8 NVLink loads in flight)
+      for (int o0 = 0; o0 < n_ow; o0 += 8) {
+        uint4 p[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(pe[i]);
+        for (int u = 0; u < 8; ++u)
+          if (o0 + u < n_ow) p[u] = __ldcg(ep_at<uint4>(regions, ow[o0 + u], L.y) + row + v);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (o0 + u >= n_ow) break;
+          const T* pe = reinterpret_cast<const T*>(&p[u]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(pe[i]);
+        }
       }
       uint4 r;
       T* re = reinterpret_cast<T*>(&r);
