@@ -19,12 +19,14 @@
 // read the same weight tile at different times rarely meet in L2: at ~7 TB/s the 126 MB L2 turns
 // over in ~18 us). A two-block group's A rows are contiguous and arrive as one 256-row box.
 //
-// TMA operations per byte: measured on B200, one CTA completes about one TMA box per ~300-350 ns
-// almost whatever its size (16 KiB boxes: ~48 GB/s per SM from L2; 64 KiB boxes: ~160 GB/s), so
-// the kernel moves few, large boxes: the gate and up rows of a Stage1 weight tile come as one
-// box of a 3-D/4-D tensor map (the gate/up offset is a tensor dimension), and a weight box may
-// span KPB consecutive k-blocks (a k-block dimension of stride 128 bytes), which lands in shared
-// memory exactly as KPB consecutive 128B-swizzled k-block tiles.
+// TMA operations per byte: in a streaming microbenchmark on B200 one CTA completes about one TMA
+// box per ~300-350 ns almost whatever its size (16 KiB boxes: ~48 GB/s per SM from L2; 64 KiB
+// boxes: ~160 GB/s), so the kernel can move fewer, larger boxes: the gate and up rows of a Stage1
+// weight tile come as one box of a 3-D/4-D tensor map (the gate/up offset is a tensor dimension),
+// and a weight box may span KPB consecutive k-blocks (a k-block dimension of stride 128 bytes),
+// which lands in shared memory exactly as KPB consecutive 128B-swizzled k-block tiles. (In the
+// full GEMM neither measured faster on cfg3, where the MMA side sets the pace; KPB > 1 stays an
+// option.)
 //
 // CTAs per SM (CPS): with CPS = 2 each CTA takes half the shared memory and half of TMEM, and the
 // two CTAs' epilogues and main loops overlap each other.

@@ -2,9 +2,9 @@
 // spans the tensor cores, shared memory and TMEM of two SMs.
 //
 // Why: the single-CTA kernel's work unit is 128 rows x 256 columns per SM, and every k-block
-// brings 16 KiB of token rows plus 32 KiB of weight rows into that SM. Measured on B200, the
-// grouped GEMM runs at the rate the SMs can take bytes in from L2 (about 10-11 TB/s over the
-// GPU), so bytes per output decide its speed. A CTA pair computes a 256 x 256 unit (two 128-row
+// brings 16 KiB of token rows plus 32 KiB of weight rows into that SM (and the MMAs read them back
+// out of shared memory). Measured on B200, the grouped GEMM's speed tracks the bytes each SM moves
+// per output more than the TMA box count. A CTA pair computes a 256 x 256 unit (two 128-row
 // blocks of one expert) with each SM loading its own 128 token rows and HALF of the 256 weight
 // rows: 32 KiB per SM per k-block for the same 128 x 256 outputs per SM, a third less intake,
 // and each expert's weight tile crosses L2 -> SM once for both blocks. Each SM keeps its 128 x 256
