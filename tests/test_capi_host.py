@@ -90,3 +90,32 @@ def test_set_tile_host():
         _lib.set_tile(2, "256a4b5x")
     with pytest.raises(_lib.MoeError):
         _lib.set_tile(-1, "auto")
+
+
+def test_peer_memory_ep_host_checks():
+    """Peer-memory expert parallelism: region and workspace sizes, and argument checks that fail
+    before any CUDA call."""
+    lib = _lib.lib()
+    T, H, k, W = 4096, 7168, 8, 8
+    region = lib.moe_ep_region_bytes(T, H, k, W)
+    # flags + count, x [T, H], ids and weights [T, k], partials [W * T, H], each 256-byte aligned
+    assert region >= T * H * 2 + 2 * T * k * 4 + W * T * H * 2
+    assert region % 256 == 0 and region < T * H * 2 + 2 * T * k * 4 + W * T * H * 2 + 8192
+    assert lib.moe_ep_region_bytes(T, H, k, 33) == 0 and lib.moe_ep_region_bytes(0, H, k, W) == 0
+    ws = lib.moe_ep_p2p_workspace_bytes(T, k, W, 32, H, 2048, _lib.MOE_F16)
+    # the local pipeline over W * T virtual tokens plus the local ids and weights of every route
+    assert ws >= lib.moe_fused_workspace_bytes(W * T, k, 32, H, 2048, _lib.MOE_F16) + 2 * 4 * W * T * k
+    assert lib.moe_ep_p2p_workspace_bytes(T, k, 0, 32, H, 2048, _lib.MOE_F16) == 0
+    # more tokens than the region holds, a world above 32, a rank outside the world
+    rc = lib.moe_ep_p2p_stage(None, None, None, _lib.MOE_I32, None, _lib.MOE_F32, T + 1, T, H, k, W, _lib.MOE_F16,
+                              None)
+    assert rc == -1 and b"max_tokens" in lib.moe_last_error()
+    rc = lib.moe_ep_p2p_stage(None, None, None, _lib.MOE_I32, None, _lib.MOE_F32, 1, T, H, k, 33, _lib.MOE_F16, None)
+    assert rc == -1 and b"world" in lib.moe_last_error()
+    assert lib.moe_ep_p2p_barrier(None, 0, W, 1, None) == -1
+    rc = lib.moe_ep_p2p_combine(None, 8, W, 4, T, H, k, None, 256, _lib.MOE_F16, None, None)
+    assert rc == -1
+    rc = lib.moe_ep_p2p_compute(None, None, 0, W, T, H, 2048, k, None, None, 256, None, None, 32, _lib.MOE_F16, None,
+                                0, None)
+    assert rc == -1 and b"regions" in lib.moe_last_error()
+    assert lib.moe_ep_region_alloc(0, None) == -1
