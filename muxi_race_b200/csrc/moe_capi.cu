@@ -18,6 +18,7 @@
 #include "gather_quant.cuh"
 #include "moe_gemm.cuh"
 #include "moe_gemm_pair.cuh"
+#include "moe_gemm_tn.cuh"
 #include "route_align.cuh"
 
 namespace moe {
@@ -123,6 +124,7 @@ struct TileInfo {
   int bn, gmax, ast, bst, cps, kpb;
   int pair;  // 1: CTA-pair kernel (cta_group::2), 256-row units, each CTA loads half the weights
   int epi;   // epilogue warps (4, or 8: two per TMEM lane quadrant, each half of the columns)
+  int tn;    // 1: operand-swapped kernel (weights as M, an expert's tokens as N; fused path only)
 };
 
 // Tiled map over a tensor of `rank` dimensions (dims[0] innermost, in elements; strides of dims
@@ -270,6 +272,7 @@ enum TileCfg {
   kTP256A4B10,
   kT256A4B5E8,
   kT256x2A3B4E8,
+  kTTN,
   kNumTileCfg
 };
 constexpr TileInfo kTiles[kNumTileCfg] = {
@@ -280,7 +283,7 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
     {"128x2a3b8", 128, 2, 3, 8, 1, 1, 0, 4},   {"256x2a3b2k2", 256, 2, 3, 2, 1, 2, 0, 4},
     {"p256a6b8", 256, 2, 6, 8, 1, 1, 1, 4},    {"p256a7b7", 256, 2, 7, 7, 1, 1, 1, 4},
     {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
-    {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8},
+    {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8}, {"tn", 256, 1, 6, 4, 1, 1, 0, 4, 1},
 };
 static_assert(kNumTileCfg * 36 <= 64 * 16, "smem attribute bits");
 
@@ -346,6 +349,7 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return safe;
   if (t.bn == 128 && stage != 1) return safe;
   if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
+  if (t.tn && (lsu || elt != 2 || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
 
@@ -422,6 +426,55 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   kern<<<2 * pairs, 96 + 32 * EPI, smem, stream>>>(m.a, m.b0, m.b1, args_l);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
+}
+
+// Tensor maps of the operand-swapped kernel: the weights and the token rows in boxes of 128 /
+// 64 / 32 / 16 rows.
+struct TnMaps {
+  CUtensorMap w, x128, x64, x32, x16;
+};
+
+int make_tn_x_maps(TnMaps* m, const void* rows_base, int64_t rows, int64_t K, const char* what) {
+  MOE_TRY(make_tmap(&m->x128, rows_base, 2, rows, K, 128, what));
+  MOE_TRY(make_tmap(&m->x64, rows_base, 2, rows, K, 64, what));
+  MOE_TRY(make_tmap(&m->x32, rows_base, 2, rows, K, 32, what));
+  MOE_TRY(make_tmap(&m->x16, rows_base, 2, rows, K, 16, what));
+  return MOE_OK;
+}
+
+// Stage1 weights of the fused path: 5-D map {k-block elements, 8 rows, gate/up, 8-row groups,
+// k-blocks} over w_gate_up [E, 2I, H] (gate rows at e*2I + f, up rows I further), box
+// {64, 8, 2, 8, 1}: 64 gate and 64 up rows interleaved by 8-row atoms.
+int make_tn_w13_map(CUtensorMap* map, const void* w13, int64_t E, int64_t H, int64_t I) {
+  if (I % 8 != 0 || (H * 2) % kKBytes != 0) return fail(MOE_ERR_UNSUPPORTED, "operand-swapped Stage1 needs I a multiple of 8 and H a multiple of 64");
+  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(kKBytes / 2), 8, 2, static_cast<cuuint64_t>((2 * E * I - I) / 8),
+                              static_cast<cuuint64_t>(H * 2 / kKBytes)};
+  const cuuint64_t strides[4] = {static_cast<cuuint64_t>(H * 2), static_cast<cuuint64_t>(I * H * 2),
+                                 static_cast<cuuint64_t>(8 * H * 2), static_cast<cuuint64_t>(kKBytes)};
+  const cuuint32_t box[5] = {static_cast<cuuint32_t>(kKBytes / 2), 8, 2, 8, 1};
+  return encode_map(map, w13, 2, 5, dims, strides, box, "w_gate_up (operand-swapped)");
+}
+
+template <int MODE, typename OutT>
+int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t stream) {
+  constexpr int AST = 6, BST = 4;
+  auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST>;
+  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2) * kNumTileCfg * 3 + tcfg * 3 + 2;
+  constexpr int smem = TnRing<AST, BST>::kSmemBytes;
+  MOE_TRY(raise_smem(dev, bit, kern, smem));
+  int sms = 0;
+  MOE_TRY(device_sms(dev, &sms));
+  const int grid = max_units < sms ? max_units : sms;
+  if (grid <= 0) return MOE_OK;
+  kern<<<grid, kThreads, smem, stream>>>(m.w, m.x128, m.x64, m.x32, m.x16, args);
+  MOE_CUDA(cudaGetLastError());
+  return MOE_OK;
+}
+
+template <int MODE>
+int launch_tn_rt(int dtype, int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t s) {
+  return dtype == MOE_F16 ? launch_tn<MODE, __half>(dev, tcfg, m, args, max_units, s)
+                          : launch_tn<MODE, __nv_bfloat16>(dev, tcfg, m, args, max_units, s);
 }
 
 // One grouped GEMM stage with the chosen tile configuration.
@@ -536,7 +589,7 @@ int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t b
 
 // Workspace carving for the token-major paths.
 struct FusedLayout {
-  size_t counts, gs, go, gpo, meta, gidx, groups, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
+  size_t counts, gs, go, gpo, meta, gidx, groups, tn, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
   int64_t P_max, nblk_max;
 };
 
@@ -558,6 +611,7 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.meta = take(sizeof(int) * 4);
   L.gidx = take(sizeof(int) * (size_t)L.nblk_max);
   L.groups = take(sizeof(int) * (size_t)(L.nblk_max + 1));  // block groups + their count
+  L.tn = take(sizeof(int) * (size_t)(2 * L.nblk_max + 1));   // operand-swapped kernel: entries + count
   L.sorted = take(sizeof(int) * (size_t)L.P_max);
   L.slot = take(sizeof(int) * (size_t)R);
   // token rows: stacked per expert (TMA A path) or read in place (LSU gather; int8 quantised
@@ -677,7 +731,9 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   int32_t* ngroups = groups + nblk;
   const bool lsu = a_path_lsu();
   const double bpe = static_cast<double>(nblk) / static_cast<double>(E);  // blocks per expert
-  const TileCfg tc1 = usable_cfg(1, H, 2, lsu, bpe), tc2 = usable_cfg(2, I, 2, lsu, bpe);
+  TileCfg tc1 = usable_cfg(1, H, 2, lsu, bpe), tc2 = usable_cfg(2, I, 2, lsu, bpe);
+  if (kTiles[tc1].tn) tc1 = kT256A4B5;  // the operand-swapped kernel runs on the fused path only
+  if (kTiles[tc2].tn) tc2 = kT256x2A3B4;
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
 
@@ -877,6 +933,12 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
   }
+  int32_t* tn_entries = reinterpret_cast<int32_t*>(ws + L.tn);
+  int32_t* tn_count = tn_entries + 2 * L.nblk_max;
+  if (t1.tn || t2.tn) {  // (expert, token chunk) entries of the operand-swapped kernel
+    build_tn_entries_kernel<<<1, 1024, 0, s>>>(gs, (int)E, (int)L.nblk_max, tn_entries, tn_count);
+    MOE_CUDA(cudaGetLastError());
+  }
   prof_record(1, s);
 
   // 2. activations: the TMA A path stacks the gathered token rows (int8: quantised per token)
@@ -1008,9 +1070,52 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
-    MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
+    // the operand-swapped kernel (tile "tn"): weights as the MMA's M side, tokens as N
+    TnArgs tn{};
+    tn.n_entries_dev = tn_count;
+    tn.entries = tn_entries;
+    tn.E = (int)E;
+    tn.group_sizes = gs;
+    tn.group_offsets = go;
+    tn.group_padded_offsets = gpo;
+    tn.R = (int)R;
+    tn.sorted_route_ids = sorted;
+    tn.topk = (int)topk;
+    tn.nblk = (int)L.nblk_max;
+    tn.status = status;
+    if (t1.tn) {
+      TnMaps tm{};
+      MOE_TRY(make_tn_w13_map(&tm.w, w13, E, H, I));
+      MOE_TRY(make_tn_x_maps(&tm, xs, L.P_max, H, "gathered hidden_states"));
+      TnArgs t = tn;
+      t.K = (int)H;
+      t.N = (int)I;
+      t.n_tiles = (int)((I + 63) / 64);
+      t.w_group_per_expert = 2 * I / 8;
+      t.U = U;
+      t.ldu = (int)I;
+      MOE_TRY(launch_tn_rt<kStage1>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s));
+    } else {
+      MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
+    }
     prof_record(3, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
+    if (t2.tn) {
+      TnMaps tm{};
+      MOE_TRY(make_tmap(&tm.w, w2, 2, E * H, I, kBM, "w_down"));
+      MOE_TRY(make_tn_x_maps(&tm, U, L.P_max, I, "intermediate"));
+      TnArgs t = tn;
+      t.K = (int)I;
+      t.N = (int)H;
+      t.n_tiles = (int)((H + kBM - 1) / kBM);
+      t.b_rows_per_expert = (int)H;
+      t.out = out;
+      t.ldo = (int)H;
+      t.routed = tw;
+      t.routed_dtype = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
+      MOE_TRY(launch_tn_rt<kStage2Comb>(dtype, dev, tc2, tm, t, (int)L.nblk_max * t.n_tiles, s));
+    } else {
+      MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
+    }
     prof_record(4, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
