@@ -154,34 +154,53 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_sample(cfg, ids_cpu, w_cpu, x_cpu, budget_s: float, seed: int = 0):
+_CPU_WEIGHTS: dict = {}
+
+
+def cpu_sample(cfg, ids_cpu, w_cpu, x_cpu, budget_s: float, seed: int = 0, max_weight_bytes: float = 1.5e9):
     """Oracle (port of the reference's PyTorch operator) on a subset of experts, on the host cores.
 
     Returns (flops, seconds, n_experts, rows). Weights of the sampled experts are generated on the
-    CPU with the workload's distribution (the values do not change the arithmetic cost).
+    CPU with the workload's distribution (the values do not change the arithmetic cost); at most
+    max_weight_bytes of them, so host memory stays bounded, and the subset is run repeatedly until
+    about budget_s seconds of work have been timed.
     """
     from oracle.moe_ref import fused_moe_ref
 
     E, H, I, k = cfg.E, cfg.H, cfg.I, cfg.topk
-    g = torch.Generator().manual_seed(seed)
     flat = ids_cpu.reshape(-1).long()
+    elt = 1 if cfg.int8 else 2
+    n_mem = int(max(1, min(E, max_weight_bytes // (3 * H * I * elt))))
 
-    def run(n):
+    def make(n):
         sel = torch.arange(n)
         remap = torch.full((E,), -1, dtype=torch.long)
         remap[sel] = torch.arange(n)
         ids_r = remap[flat].reshape(ids_cpu.shape)
-        w13 = (torch.randn((n, 2 * I, H), generator=g) * H ** -0.5).to(cfg.dtype)
-        w2 = (torch.randn((n, H, I), generator=g) * I ** -0.5).to(cfg.dtype)
-        rows = int((ids_r >= 0).sum())
+        key = (cfg.name, n)
+        if key not in _CPU_WEIGHTS:  # generated once per process: the values do not change the cost
+            g = torch.Generator().manual_seed(seed)
+            if len(_CPU_WEIGHTS) >= 2:  # the one-expert estimate and the sampled subset
+                _CPU_WEIGHTS.pop(next(iter(_CPU_WEIGHTS)))
+            _CPU_WEIGHTS[key] = ((torch.randn((n, 2 * I, H), generator=g) * H ** -0.5).to(cfg.dtype),
+                                 (torch.randn((n, H, I), generator=g) * I ** -0.5).to(cfg.dtype))
+        w13, w2 = _CPU_WEIGHTS[key]
+        return ids_r, w13, w2, int((ids_r >= 0).sum())
+
+    ids_r, w13, w2, rows = make(1)  # estimate (also warms the BLAS threads)
+    t0 = time.perf_counter()
+    fused_moe_ref(x_cpu, w13, w2, ids_r, w_cpu)
+    t1 = time.perf_counter() - t0
+    n = int(max(1, min(n_mem, budget_s / max(t1, 1e-3))))
+    ids_r, w13, w2, rows = make(n)
+    flops = dt = 0.0
+    while True:
         t0 = time.perf_counter()
         fused_moe_ref(x_cpu, w13, w2, ids_r, w_cpu)
-        dt = time.perf_counter() - t0
-        return 2.0 * rows * 3 * H * I, dt, rows
-
-    f1, t1, _ = run(1)  # estimate (also warms the BLAS threads)
-    n = int(max(1, min(E, budget_s / max(t1, 1e-3))))
-    flops, dt, rows = run(n)
+        dt += time.perf_counter() - t0
+        flops += 2.0 * rows * 3 * H * I
+        if dt >= 0.5 * budget_s or dt + dt / max(flops, 1.0) * 2.0 * rows * 3 * H * I > budget_s:
+            break
     return flops, dt, n, rows
 
 
