@@ -542,8 +542,9 @@ def bench_ep(args, world, rank, local):
 
 # ----------------------------------------------------------------------------- contest cases
 # The reference's own benchmark shapes (初审材料/源代码/benchmark/remote_bench.py:21-29, cases 1-3) and
-# its published C500 times for them: v755 on the judge (xpuoj_data/oj_submission_record_v755_8033.json,
-# README.md:62-66) and the judge's PyTorch baseline T_b (OJ_最终提交_SPJ报告.md:11,22,33).
+# its published C500 times for them: v755 on the contest's online judge
+# (xpuoj_data/oj_submission_record_v755_8033.json, README.md:62-66) and that online judge's PyTorch
+# baseline T_b (OJ_最终提交_SPJ报告.md:11,22,33).
 CONTEST = {
     1: dict(experts=16, hidden=2048, intermediate=8192, valid=2272, high_experts=8, low_size=124,
             c500_ms=2.544, c500_torch_ms=11.251),
@@ -606,8 +607,9 @@ def bench_run_kernel(args):
                                f"valid rows={c['valid']} padded rows={P}", "dtype": "fp16"},
         "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
         "roofline_ms": round(max(flops / (peaks['bf16_tflops'] * 1e12), (wbytes + 2 * P * H * 2) / (peaks["hbm_gbs"] * 1e9)) * 1e3, 4),
-        "reference_c500": {"ms": c["c500_ms"], "judge_torch_ms": c["c500_torch_ms"],
-                           "note": "published MetaX C500 times of the reference's final operator and the judge's "
+        "reference_c500": {"ms": c["c500_ms"], "contest_torch_ms": c["c500_torch_ms"],
+                           "note": "published MetaX C500 times of the reference's final operator and the contest "
+                                   "online judge's "
                                    "PyTorch baseline on the same shapes (different hardware)"},
     }), flush=True)
 

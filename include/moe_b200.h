@@ -1,7 +1,8 @@
 /*
  * moe_b200.h — C ABI of the B200 (sm_100a) fused Mixture-of-Experts operator.
  *
- * Conventions (the judge's CUDA C ABI for this operator, xpuoj_data/evaluation_guide.md:79-97):
+ * Conventions (the contest online judge's CUDA C ABI for this operator,
+ * xpuoj_data/evaluation_guide.md:79-97):
  *   - every tensor is a device pointer (`void*`) to contiguous, row-major memory on the current
  *     CUDA device; integers are int64_t; `stream` is a cudaStream_t (NULL = legacy default);
  *   - calls are stream-ordered and asynchronous: no entry point synchronises the device or the
@@ -85,7 +86,7 @@ MOE_API int moe_set_tile(int stage, const char* name);
  * group_sizes, group_offsets, group_padded_offsets, group_idx_for_bx, out)
  * (初审材料/源代码/submission.py:2098-2184; problem statement xpuoj_data/problem1_contest5.json,
  * interface section), with the shape scalars the Python entry point reads from tensor shapes
- * (:2110-2115) passed explicitly, as the judge's C ABI does for `int` arguments.
+ * (:2110-2115) passed explicitly, as the contest online judge's C ABI does for `int` arguments.
  *
  *   stacked_expert_tokens [P, H]  dtype   (expert-grouped, padded to 128 rows per expert)
  *   gate_w, up_w          [E, I, H] dtype
@@ -110,9 +111,9 @@ MOE_API int moe_run_kernel(const void* stacked_expert_tokens, const void* gate_w
 
 /* moe_run_kernel for callers that cannot allocate device memory. This entry point has no
  * counterpart in the reference. Some callers have no way to hand the operator a scratch buffer:
- * a judge that binds `run_kernel` through the C ABI passes only the operator's own tensors and
- * integers (xpuoj_data/evaluation_guide.md:79-97), and calling cudaMalloc inside a timed or
- * captured loop is not an option. Here the Stage1 intermediate lives in a buffer of
+ * the contest online judge, which binds `run_kernel` through the C ABI, passes only the operator's
+ * own tensors and integers (xpuoj_data/evaluation_guide.md:79-97), and calling cudaMalloc inside a
+ * timed or captured loop is not an option. Here the Stage1 intermediate lives in a buffer of
  * MOE_NOALLOC_WORKSPACE_BYTES that the library itself holds in static device memory: every GPU
  * that loads the library keeps those 64 MiB until the process exits. The call allocates nothing.
  *   - Same arguments and results as moe_run_kernel, without workspace / workspace_bytes.

@@ -32,7 +32,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import cases  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) < 2:
+    sys.exit("usage: python tests/golden/make_golden.py <reference checkout>")
+REF = sys.argv[1]
 BENCH = os.path.join(REF, "初审材料", "源代码", "benchmark")
 
 

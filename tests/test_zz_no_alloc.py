@@ -1,7 +1,7 @@
 """GPU: moe_run_kernel_noalloc, the reference drop-in for callers that cannot allocate.
 
-A caller such as a judge that binds ``run_kernel`` through the C ABI passes only the operator's own
-tensors, so it cannot hand the operator a scratch buffer. ``moe_run_kernel_noalloc`` keeps the
+A caller such as the contest's online judge, which binds ``run_kernel`` through the C ABI, passes
+only the operator's own tensors, so it cannot hand the operator a scratch buffer. ``moe_run_kernel_noalloc`` keeps the
 Stage1 intermediate in the library's static device buffer instead. This test calls it through
 the C ABI twice in a row (different inputs, so the second call runs over the first call's leftover
 buffer contents) and checks each output against the existing ``moe_run_kernel`` entry point with
