@@ -77,3 +77,52 @@ class ReferenceOps:
             out.copy_(res)
             return out
         return res
+
+
+# ----------------------------------------------------------------------------- peer-memory mode
+def p2p_local_routes_ref(all_ids, expert_rank, expert_local, rank, T_max):
+    """Virtual routes of the peer-memory mode for one rank: route r = (s * T_max + t) * k + j covers
+    slot j of token t of rank s; local id = this rank's local index of that expert, -1 if another
+    rank owns it or t is beyond rank s's token count (all_ids: one [T_s, k] tensor per rank)."""
+    W = len(all_ids)
+    k = all_ids[0].shape[1]
+    local = torch.full((W * T_max * k,), -1, dtype=torch.int64)
+    for s, ids in enumerate(all_ids):
+        T_s = ids.shape[0]
+        flat = ids.long().reshape(-1)
+        own = expert_rank.long()[flat] == rank
+        lid = torch.where(own, expert_local.long()[flat], torch.full_like(flat, -1))
+        local[s * T_max * k: s * T_max * k + T_s * k] = lid
+    return local
+
+
+def p2p_partials_ref(all_x, all_ids, all_w, expert_rank, expert_local, rank, T_max, w13_local, w2_local):
+    """Rank `rank`'s partial block y [W * T_max, H] (fp32): row s * T_max + t = sum over this rank's
+    experts among token (s, t)'s top-k of weight * expert(x); rows without a local route are 0."""
+    W = len(all_x)
+    k = all_ids[0].shape[1]
+    H = all_x[0].shape[1]
+    local = p2p_local_routes_ref(all_ids, expert_rank, expert_local, rank, T_max).view(W, T_max, k)
+    y = torch.zeros((W * T_max, H), dtype=torch.float32)
+    for s in range(W):
+        T_s = all_x[s].shape[0]
+        if T_s == 0:
+            continue
+        ids = local[s, :T_s]
+        w = torch.where(ids >= 0, all_w[s].float(), torch.zeros_like(all_w[s].float()))
+        ids_c = ids.clamp(min=0)  # masked routes carry weight 0
+        y[s * T_max: s * T_max + T_s] = fused_moe_ref(all_x[s], w13_local, w2_local, ids_c, w)
+    return y
+
+
+def p2p_combine_ref(partials, all_ids, expert_rank, rank, T_max, dtype):
+    """out[t] of rank `rank` = sum, over the distinct owner ranks o of token t's experts in ascending
+    order, of partials[o][rank * T_max + t] (fp32, then cast)."""
+    ids = all_ids[rank].long()
+    T = ids.shape[0]
+    out = torch.zeros((T, partials[0].shape[1]), dtype=torch.float32)
+    owners = expert_rank.long()[ids]  # [T, k]
+    for o in range(len(partials)):
+        m = (owners == o).any(dim=1)
+        out[m] += partials[o][rank * T_max: rank * T_max + T][m].float()
+    return out.to(dtype)
