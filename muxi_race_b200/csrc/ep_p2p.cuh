@@ -184,6 +184,106 @@ __global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, Ep
   }
 }
 
+// Bulk-copy variant of gather_rows_peer_kernel (selected with MOE_B200_EP_GATHER=bulk): lane 0
+// of each warp moves whole token rows with the bulk-copy engine, peer row -> shared memory
+// (cp.async.bulk with an mbarrier) -> xs (cp.async.bulk store), two rows in flight per warp. Then
+// all threads zero the served partial rows as in gather_rows_peer_kernel. Dynamic shared memory:
+// kEpBulkWarps * 2 rows of H * 2 bytes, plus the mbarriers.
+constexpr int kEpBulkWarps = 4;
+__device__ __forceinline__ void bulk_load_row(uint32_t dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_smem),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_store_row(void* dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src_smem), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_reads() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+template <typename T>
+__global__ void __launch_bounds__(kEpBulkWarps * 32)
+    gather_rows_peer_bulk_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int T_max, int topk,
+                                 int W, const int32_t* __restrict__ route_slot, const int32_t* __restrict__ local_ids,
+                                 int H, T* __restrict__ xs, uint32_t* status) {
+  extern __shared__ __align__(128) uint8_t ep_smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row_bytes = static_cast<uint32_t>(H) * 2u;
+  uint8_t* buf = ep_smem + static_cast<size_t>(warp) * 2 * row_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ep_smem + static_cast<size_t>(kEpBulkWarps) * 2 * row_bytes) + 2 * warp;
+  const long long R = static_cast<long long>(W) * T_max * topk;
+  const long long gw = static_cast<long long>(blockIdx.x) * kEpBulkWarps + warp;
+  const long long nw = static_cast<long long>(gridDim.x) * kEpBulkWarps;
+  if (lane == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_mbar_init();
+    auto next_valid = [&](long long r) {
+      while (r < R && route_slot[r] < 0) r += nw;
+      return r;
+    };
+    auto src_of = [&](long long r) {
+      const long long tok = r / topk;  // s * T_max + t
+      const int s = static_cast<int>(tok / T_max);
+      const long long t = tok - static_cast<long long>(s) * T_max;
+      return reinterpret_cast<const uint8_t*>(regions[s] + static_cast<uint64_t>(L.x)) + t * row_bytes;
+    };
+    uint32_t phase[2] = {0u, 0u};
+    long long cur = next_valid(gw);
+    int sb = 0;
+    if (cur < R) {
+      mbar_arrive_expect_tx(&bars[0], row_bytes);
+      bulk_load_row(smem_u32(buf), src_of(cur), row_bytes, &bars[0]);
+    }
+    bool ok = true;
+    while (cur < R && ok) {
+      const long long nxt = next_valid(cur + nw);
+      const int nb = sb ^ 1;
+      if (nxt < R) {
+        bulk_wait_reads();  // the store that last used buffer nb has read it
+        mbar_arrive_expect_tx(&bars[nb], row_bytes);
+        bulk_load_row(smem_u32(buf + nb * row_bytes), src_of(nxt), row_bytes, &bars[nb]);
+      }
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&bars[sb], phase[sb])) {
+        if (globaltimer_ns() - t0 > MOE_WAIT_NS) {
+          if (status) atomicOr(status, kStatusWaitTimeout);
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
+      phase[sb] ^= 1u;
+      const int slot = route_slot[cur];
+      bulk_store_row(xs + static_cast<size_t>(slot) * H, smem_u32(buf + sb * row_bytes), row_bytes);
+      cur = nxt;
+      sb = nb;
+    }
+    // every load issued has landed (bounded) and every store has completed before the CTA exits
+    for (int b = 0; b < 2; ++b) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!ok && !mbar_try_wait(&bars[b], phase[b]) && globaltimer_ns() - t0 < MOE_WAIT_NS) {
+      }
+    }
+    bulk_wait_all();
+  }
+  __syncwarp();
+  // zero this rank's partial rows of every token with at least one local route
+  const int vecs = H / 8;
+  const long long rows = static_cast<long long>(W) * T_max;
+  uint4* y = reinterpret_cast<uint4*>(regions[rank] + static_cast<uint64_t>(L.y));
+  for (long long tok = gw; tok < rows; tok += nw) {
+    bool served = false;
+    for (int j = 0; j < topk; ++j) served |= local_ids[tok * topk + j] >= 0;
+    if (!served) continue;
+    uint4* dst = y + tok * vecs;
+    for (int v = lane; v < vecs; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
 // out[t] = sum over the distinct owner ranks o of token t's experts (ascending o) of rank o's
 // y[rank * T_max + t], accumulated in fp32. One warp per token, 8 elements per lane step.
 template <typename T>

@@ -352,6 +352,16 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   if (t.tn && (lsu || elt != 2 || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
+// Peer-memory EP gather: MOE_B200_EP_GATHER=bulk selects gather_rows_peer_bulk_kernel (bulk
+// copies through shared memory) instead of the per-lane 16-byte load loop.
+constexpr size_t kEpBulkMaxSmem = 220 * 1024;
+static bool ep_gather_bulk() {
+  static const bool v = [] {
+    const char* e = getenv("MOE_B200_EP_GATHER");
+    return e && strcmp(e, "bulk") == 0;
+  }();
+  return v;
+}
 
 // Unit order (see tile_unit): MOE_B200_UNIT_ORDER = expert (default: an expert's groups side by
 // side per column tile) | group (group-major).
@@ -959,6 +969,24 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_CUDA(cudaGetLastError());
       MOE_CUDA(cudaMemsetAsync(amax, 0, sizeof(float) * (size_t)L.P_max, s));
     }
+  } else if (peer && ep_gather_bulk() &&
+             (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps <= kEpBulkMaxSmem) {
+    // bulk-copy gather: whole rows through shared memory, one CTA of 4 warps per SM
+    const size_t smem = (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps;
+    if (dtype == MOE_F16) {
+      MOE_CUDA(cudaFuncSetAttribute(gather_rows_peer_bulk_kernel<__half>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      gather_rows_peer_bulk_kernel<__half><<<sms, kEpBulkWarps * 32, smem, s>>>(
+          peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__half*>(xs), status);
+    } else {
+      MOE_CUDA(cudaFuncSetAttribute(gather_rows_peer_bulk_kernel<__nv_bfloat16>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      gather_rows_peer_bulk_kernel<__nv_bfloat16><<<sms, kEpBulkWarps * 32, smem, s>>>(
+          peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs), status);
+    }
+    MOE_CUDA(cudaGetLastError());
   } else if (peer) {  // token rows from the ranks' regions; zero the served partial rows
     if (dtype == MOE_F16)
       gather_rows_peer_kernel<__half><<<gblocks, 256, 0, s>>>(peer->regions, peer->L, peer->rank, peer->T_max,
