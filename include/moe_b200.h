@@ -180,6 +180,30 @@ MOE_API int moe_fused(const void* hidden_states, const void* w_gate_up, const vo
               void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * Router: softmax top-k of router logits, the step that produces topk_ids / topk_weights for the
+ * fused MoE (no reference counterpart: the reference receives its routing pre-built; the
+ * synthetic workloads route by softmax -> top-k -> renormalise, as tests/golden/cases.py:118-129
+ * does with torch).
+ *
+ * moe_router_topk: logits [T, E] logits_dtype (MOE_F32 / MOE_F16 / MOE_BF16) ->
+ *   topk_ids [T, topk] int32 in descending logit order (equal logits: lower expert id first;
+ *   the order of fp32 values, +0 above -0), topk_weights [T, topk] fp32 =
+ *   softmax(logits)[ids], divided by their sum when renormalize != 0.
+ *   Requirements: 1 <= topk <= min(E, 32), 1 <= E <= 1024; logits finite.
+ * moe_fused_router: moe_router_topk followed by moe_fused on its output, with the router kernel
+ *   also building the alignment's expert histogram (one pass fewer). topk_ids / topk_weights are
+ *   caller buffers and hold the routing afterwards. Workspace: moe_fused_workspace_bytes.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API int moe_router_topk(const void* logits, int logits_dtype, int64_t num_tokens, int64_t num_experts,
+                            int64_t topk, int renormalize, int32_t* topk_ids, float* topk_weights, void* stream);
+
+MOE_API int moe_fused_router(const void* hidden_states, const void* w_gate_up, const void* w_down,
+                             const void* logits, int logits_dtype, int renormalize, int32_t* topk_ids,
+                             float* topk_weights, void* out, int64_t num_tokens, int64_t hidden,
+                             int64_t intermediate, int64_t num_experts, int64_t topk, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * W8A8 int8 route. Semantics of the reference's int8 experiment
  * (xpuoj_data/submission_v322_int8_v2.py:164-205 weight quantisation, :207-232 activation
  * quantisation, :234-454 int8 GEMMs with int32 accumulation and dequantisation), with one scale

@@ -20,6 +20,7 @@
 #include "moe_gemm_pair.cuh"
 #include "moe_gemm_tn.cuh"
 #include "route_align.cuh"
+#include "router_topk.cuh"
 
 namespace moe {
 
@@ -567,14 +568,15 @@ int align_chunk(int64_t R) {
 }
 int64_t align_chunks(int64_t R) { return R <= 0 ? 0 : (R + align_chunk(R) - 1) / align_chunk(R); }
 
+// counted: `counts` already holds the per-chunk histogram (built by the router kernel).
 int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, int32_t* gs, int32_t* go,
                  int32_t* gpo, int32_t* gidx, int32_t* sorted, int32_t* route_slot, int32_t* meta, int* counts,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, bool counted = false) {
   const int chunk = align_chunk(R);
   const int n_chunks = static_cast<int>(align_chunks(R));
   const int grid = (n_chunks + kAlignWarps - 1) / kAlignWarps;
   const size_t smem = sizeof(int) * kAlignWarps * E;
-  if (n_chunks > 0) {
+  if (n_chunks > 0 && !counted) {
     if (ids_dtype == MOE_I32)
       align_count_kernel<int32_t><<<grid, kAlignWarps * 32, smem, stream>>>(
           static_cast<const int32_t*>(ids), (int)R, (int)E, chunk, n_chunks, counts);
@@ -645,6 +647,64 @@ int check_common(int64_t H, int64_t I, int64_t E, int dtype, int mult) {
                 (long long)I, mult);
   if (H > (1 << 30) || I > (1 << 30)) return fail(MOE_ERR_INVALID_ARG, "hidden/intermediate too large");
   return MOE_OK;
+}
+
+// ------------------------------------------------------------------ router
+template <typename LogitT>
+int launch_router_t(const LogitT* logits, int64_t T, int64_t E, int64_t topk, int renorm, int32_t* ids, float* w,
+                    int* counts, int chunk, int n_chunks, int sms, cudaStream_t s) {
+  const int64_t want = (T + kRouterWarps - 1) / kRouterWarps;
+  const int grid = static_cast<int>(want < (int64_t)sms * 16 ? want : (int64_t)sms * 16);
+  const int threads = kRouterWarps * 32;
+#define MOE_ROUTER_CASE(V)                                                                                      \
+  if (E <= 32 * (V)) {                                                                                          \
+    router_topk_kernel<LogitT, V><<<grid, threads, 0, s>>>(logits, (int)T, (int)E, (int)topk, renorm, ids, w, \
+                                                          counts, chunk, n_chunks);                           \
+    MOE_CUDA(cudaGetLastError());                                                                               \
+    return MOE_OK;                                                                                              \
+  }
+  MOE_ROUTER_CASE(1)
+  MOE_ROUTER_CASE(2)
+  MOE_ROUTER_CASE(4)
+  MOE_ROUTER_CASE(8)
+  MOE_ROUTER_CASE(16)
+  MOE_ROUTER_CASE(32)
+#undef MOE_ROUTER_CASE
+  return fail(MOE_ERR_INVALID_ARG, "num_experts must be <= %d", 32 * 32);
+}
+
+int check_router(const void* logits, int logits_dtype, int64_t T, int64_t E, int64_t topk, const int32_t* ids,
+                        const float* w) {
+  if (logits_dtype != MOE_F32 && logits_dtype != MOE_F16 && logits_dtype != MOE_BF16)
+    return fail(MOE_ERR_INVALID_ARG, "router logits must be fp32, fp16 or bf16");
+  if (E < 1 || E > kAlignMaxExperts) return fail(MOE_ERR_INVALID_ARG, "num_experts must be in [1, %d]", kAlignMaxExperts);
+  if (topk < 1 || topk > kRouterMaxTopk || topk > E)
+    return fail(MOE_ERR_INVALID_ARG, "topk must be in [1, min(num_experts, %d)]", kRouterMaxTopk);
+  if (T < 0 || T * topk > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "bad token count");
+  if (T > 0 && (!logits || !ids || !w)) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  return MOE_OK;
+}
+
+// Runs the router on `s`; with `counts` (zeroed here) it also builds the alignment histogram for
+// R = T * topk routes.
+int launch_router(const void* logits, int logits_dtype, int64_t T, int64_t E, int64_t topk, int renorm,
+                         int32_t* ids, float* w, int* counts, cudaStream_t s) {
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  const int64_t R = T * topk;
+  const int chunk = align_chunk(R);
+  const int n_chunks = static_cast<int>(align_chunks(R));
+  if (counts) MOE_CUDA(cudaMemsetAsync(counts, 0, sizeof(int) * (size_t)n_chunks * (size_t)E, s));
+  renorm = renorm ? 1 : 0;
+  if (logits_dtype == MOE_F32)
+    return launch_router_t(static_cast<const float*>(logits), T, E, topk, renorm, ids, w, counts, chunk, n_chunks, sms,
+                           s);
+  if (logits_dtype == MOE_F16)
+    return launch_router_t(static_cast<const __half*>(logits), T, E, topk, renorm, ids, w, counts, chunk, n_chunks,
+                           sms, s);
+  return launch_router_t(static_cast<const __nv_bfloat16*>(logits), T, E, topk, renorm, ids, w, counts, chunk,
+                         n_chunks, sms, s);
 }
 
 }  // namespace
@@ -850,6 +910,15 @@ size_t moe_align_workspace_bytes(int64_t R, int64_t E) {
   return round_up(sizeof(int) * static_cast<size_t>(align_chunks(R)) * static_cast<size_t>(E > 0 ? E : 0), 256);
 }
 
+int moe_router_topk(const void* logits, int logits_dtype, int64_t T, int64_t E, int64_t topk, int renormalize,
+                    int32_t* ids, float* w, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(check_router(logits, logits_dtype, T, E, topk, ids, w));
+  if (T == 0) return MOE_OK;
+  return launch_router(logits, logits_dtype, T, E, topk, renormalize, ids, w, nullptr,
+                       static_cast<cudaStream_t>(stream));
+}
+
 int moe_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, int32_t* gs, int32_t* go,
               int32_t* gpo, int32_t* gidx, int32_t* sorted, int32_t* route_slot, int32_t* meta, void* workspace,
               size_t workspace_bytes, void* stream) {
@@ -883,10 +952,18 @@ struct PeerSource {
   int rank, W, T_max;
 };
 
+// Routing from router logits: the router kernel writes `ids` / `tw` (the fused call's topk_ids /
+// topk_weights) and the alignment histogram.
+struct RouterSource {
+  const void* logits;
+  int logits_dtype, renormalize;
+};
+
 static int fused_common(bool int8, const void* x, const void* w13, const float* w13_scale, const void* w2,
                         const float* w2_scale, const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out,
                         int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype, void* workspace,
-                        size_t workspace_bytes, void* stream, const PeerSource* peer = nullptr) {
+                        size_t workspace_bytes, void* stream, const PeerSource* peer = nullptr,
+                        const RouterSource* router = nullptr) {
   t_last_error.clear();
   MOE_TRY(check_common(H, I, E, dtype, int8 ? 16 : 8));
   if (T < 0 || topk < 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be >= 0 and topk >= 1");
@@ -938,7 +1015,11 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
 
   // 1. routing metadata
   prof_record(0, s);
-  MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s));
+  if (router)
+    MOE_TRY(launch_router(router->logits, router->logits_dtype, T, E, topk, router->renormalize,
+                          static_cast<int32_t*>(const_cast<void*>(ids)), static_cast<float*>(const_cast<void*>(tw)),
+                          counts, s));
+  MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s, router != nullptr));
   if (gmax1 > 1 || gmax2 > 1) {
     build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups);
     MOE_CUDA(cudaGetLastError());
@@ -1170,6 +1251,16 @@ int moe_fused(const void* x, const void* w13, const void* w2, const void* ids, i
               void* workspace, size_t workspace_bytes, void* stream) {
   return fused_common(false, x, w13, nullptr, w2, nullptr, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk, dtype,
                       workspace, workspace_bytes, stream);
+}
+
+int moe_fused_router(const void* x, const void* w13, const void* w2, const void* logits, int logits_dtype,
+                     int renormalize, int32_t* ids, float* tw, void* out, int64_t T, int64_t H, int64_t I, int64_t E,
+                     int64_t topk, int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(check_router(logits, logits_dtype, T, E, topk, ids, tw));
+  const RouterSource rs{logits, logits_dtype, renormalize ? 1 : 0};
+  return fused_common(false, x, w13, nullptr, w2, nullptr, ids, MOE_I32, tw, MOE_F32, out, T, H, I, E, topk, dtype,
+                      workspace, workspace_bytes, stream, nullptr, &rs);
 }
 
 int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale, void* stream) {

@@ -157,6 +157,82 @@ def fused_moe(
     return out
 
 
+# ----------------------------------------------------------------------------- router
+_LOGIT_DTYPES = {torch.float32: _lib.MOE_F32, torch.float16: _lib.MOE_F16, torch.bfloat16: _lib.MOE_BF16}
+
+
+def _check_logits(gating_output: torch.Tensor, T: int, topk: int) -> int:
+    _check(gating_output.dim() == 2 and gating_output.shape[0] == T, "gating_output must be [T, E]")
+    _check(gating_output.is_cuda and gating_output.is_contiguous(), "gating_output must be a contiguous CUDA tensor")
+    _check(gating_output.dtype in _LOGIT_DTYPES, "gating_output must be fp32, fp16 or bf16")
+    E = int(gating_output.shape[1])
+    _check(1 <= topk <= min(E, 32), "topk must be in [1, min(E, 32)]")
+    return E
+
+
+def fused_topk(
+    hidden_states: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Softmax top-k routing in one kernel: (topk_weights [T, k] fp32, topk_ids [T, k] int32).
+
+    topk_weights = softmax(gating_output)[topk_ids], renormalised to sum 1 per token when
+    ``renormalize``; ids in descending logit order, equal logits by ascending expert id.
+    ``hidden_states`` only fixes T (the argument order of the usual fused-MoE router helper).
+    """
+    T = int(hidden_states.shape[0])
+    E = _check_logits(gating_output, T, topk)
+    dev = gating_output.device
+    ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    if T:
+        _lib.call("moe_router_topk", gating_output.data_ptr(), _LOGIT_DTYPES[gating_output.dtype], T, E, topk,
+                  int(bool(renormalize)), ids.data_ptr(), w.data_ptr(), _stream(dev))
+    return w, ids
+
+
+def fused_moe_router(
+    hidden_states: torch.Tensor,
+    w_gate_up: torch.Tensor,
+    w_down: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool = True,
+    out: Optional[torch.Tensor] = None,
+    return_routing: bool = False,
+):
+    """``fused_moe`` with the routing computed from router logits on the device.
+
+    Same result as ``fused_moe(hidden_states, w_gate_up, w_down, ids, weights)`` with
+    ``weights, ids = fused_topk(hidden_states, gating_output, topk, renormalize)``; the router
+    kernel also builds the alignment's expert histogram. Returns ``out`` or, with
+    ``return_routing``, ``(out, topk_weights, topk_ids)``.
+    """
+    T = int(hidden_states.shape[0])
+    E = _check_logits(gating_output, T, topk)
+    dev = hidden_states.device
+    ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    T, H, I, E2, k = _check_fused(hidden_states, w_gate_up, w_down, ids, w, False)
+    _check(E2 == E, f"gating_output has {E} experts, the weights {E2}")
+    _check(gating_output.device == dev, "gating_output must be on the device of hidden_states")
+    if out is None:
+        out = torch.empty((T, H), dtype=hidden_states.dtype, device=dev)
+    _check(tuple(out.shape) == (T, H) and out.dtype == hidden_states.dtype and out.is_contiguous(), "bad out")
+    if T:
+        dt = _DTYPES[hidden_states.dtype]
+        nbytes = _lib.lib().moe_fused_workspace_bytes(T, k, E, H, I, dt)
+        ws = _workspace(("fused", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+        _lib.call(
+            "moe_fused_router", hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(),
+            gating_output.data_ptr(), _LOGIT_DTYPES[gating_output.dtype], int(bool(renormalize)), ids.data_ptr(),
+            w.data_ptr(), out.data_ptr(), T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
+        )
+    return (out, w, ids) if return_routing else out
+
+
 # ----------------------------------------------------------------------------- W8A8 int8
 def quantize_rows_int8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row symmetric int8: q = round_half_away(w * 127 / amax_row), scale = amax_row / 127.

@@ -60,6 +60,24 @@ def test_invalid_arguments_fail_before_any_launch():
                   None, 0, None)
 
 
+def test_router_argument_checks():
+    """moe_router_topk / moe_fused_router refuse bad arguments before touching a device pointer;
+    no tokens is a no-op."""
+    lib = _lib.lib()
+    cases = [((_lib.MOE_F32, 8, 256, 33), b"topk"), ((_lib.MOE_F32, 8, 4, 5), b"topk"),
+             ((_lib.MOE_F32, 8, 2000, 8), b"num_experts"), ((_lib.MOE_I8, 8, 256, 8), b"fp32, fp16 or bf16"),
+             ((_lib.MOE_F16, -1, 256, 8), b"token count")]
+    for (dt, T, E, k), msg in cases:
+        rc = lib.moe_router_topk(None, dt, T, E, k, 1, None, None, None)
+        assert rc == -1 and msg in lib.moe_last_error(), (dt, T, E, k, lib.moe_last_error())
+        rc = lib.moe_fused_router(None, None, None, None, dt, 1, None, None, None, T, 128, 128, E, k, _lib.MOE_F16,
+                                  None, 0, None)
+        assert rc == -1 and msg in lib.moe_last_error(), (dt, T, E, k, lib.moe_last_error())
+    assert lib.moe_router_topk(None, _lib.MOE_F32, 0, 256, 8, 1, None, None, None) == 0
+    rc = lib.moe_router_topk(None, _lib.MOE_F32, 4, 256, 8, 1, None, None, None)
+    assert rc == -1 and b"null" in lib.moe_last_error()
+
+
 def test_python_entry_points_reject_cpu_tensors():
     from muxi_race_b200 import fused_moe, run_kernel
 
