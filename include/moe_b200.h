@@ -180,6 +180,23 @@ MOE_API int moe_fused(const void* hidden_states, const void* w_gate_up, const vo
               void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * moe_fused_ordered: moe_fused with a deterministic top-k combine (no reference counterpart: the
+ * reference writes the padded per-route rows and leaves the combine to its caller). Stage2 runs
+ * in the reference's padded-store form (submission.py:317-357) into a workspace buffer, then
+ * out[t] = sum over j = 0 .. topk-1 of those rows, accumulated in fp32 in route order and
+ * rounded once: bitwise the same result on every run. Arguments as moe_fused; workspace:
+ * moe_fused_ordered_workspace_bytes (moe_fused's plus P_max * H * 2 + T * topk * 4 bytes).
+ * ---------------------------------------------------------------------------------------- */
+MOE_API size_t moe_fused_ordered_workspace_bytes(int64_t num_tokens, int64_t topk, int64_t num_experts,
+                                                 int64_t hidden, int64_t intermediate, int dtype);
+
+MOE_API int moe_fused_ordered(const void* hidden_states, const void* w_gate_up, const void* w_down,
+                              const void* topk_ids, int ids_dtype, const void* topk_weights, int weights_dtype,
+                              void* out, int64_t num_tokens, int64_t hidden, int64_t intermediate,
+                              int64_t num_experts, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Router: softmax top-k of router logits, the step that produces topk_ids / topk_weights for the
  * fused MoE (no reference counterpart: the reference receives its routing pre-built; the
  * synthetic workloads route by softmax -> top-k -> renormalise, as tests/golden/cases.py:118-129

@@ -16,7 +16,7 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_NAME = "libmoe_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 SOURCES = ["moe_capi.cu"]
-HEADERS = ["moe_gemm.cuh", "moe_gemm_pair.cuh", "moe_gemm_tn.cuh", "ep_p2p.cuh", "route_align.cuh", "router_topk.cuh", "gather_quant.cuh", "ep_kernels.cuh", "sm100_ptx.cuh"]
+HEADERS = ["moe_gemm.cuh", "moe_gemm_pair.cuh", "moe_gemm_tn.cuh", "ep_p2p.cuh", "route_align.cuh", "router_topk.cuh", "ordered_combine.cuh", "gather_quant.cuh", "ep_kernels.cuh", "sm100_ptx.cuh"]
 GENCODE = "arch=compute_100a,code=sm_100a"
 
 

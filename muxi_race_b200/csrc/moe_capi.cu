@@ -19,6 +19,7 @@
 #include "moe_gemm.cuh"
 #include "moe_gemm_pair.cuh"
 #include "moe_gemm_tn.cuh"
+#include "ordered_combine.cuh"
 #include "route_align.cuh"
 #include "router_topk.cuh"
 
@@ -601,11 +602,13 @@ int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t b
 
 // Workspace carving for the token-major paths.
 struct FusedLayout {
-  size_t counts, gs, go, gpo, meta, gidx, groups, tn, sorted, slot, xs, xscale, u, uq, uscale, amax, total;
+  size_t counts, gs, go, gpo, meta, gidx, groups, tn, sorted, slot, xs, xscale, u, uq, uscale, amax, y, raw, total;
   int64_t P_max, nblk_max;
 };
 
-FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8, bool lsu) {
+// ordered: the padded Stage2 rows y [P_max, H] and raw-order weights [R] of the ordered combine.
+FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, bool int8, bool lsu,
+                         bool ordered = false) {
   FusedLayout L{};
   const int64_t R = T * topk;
   L.P_max = moe_max_padded_rows(R, E, kBM);
@@ -635,6 +638,8 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.uq = take(int8 ? (size_t)L.P_max * I : 0);
   L.uscale = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
   L.amax = take(int8 ? sizeof(float) * (size_t)L.P_max : 0);
+  L.y = take(ordered ? 2 * (size_t)L.P_max * H : 0);
+  L.raw = take(ordered ? sizeof(float) * (size_t)R : 0);
   L.total = off;
   return L;
 }
@@ -963,7 +968,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
                         const float* w2_scale, const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out,
                         int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype, void* workspace,
                         size_t workspace_bytes, void* stream, const PeerSource* peer = nullptr,
-                        const RouterSource* router = nullptr) {
+                        const RouterSource* router = nullptr, bool ordered = false) {
   t_last_error.clear();
   MOE_TRY(check_common(H, I, E, dtype, int8 ? 16 : 8));
   if (T < 0 || topk < 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be >= 0 and topk >= 1");
@@ -981,7 +986,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (!aligned16(x) || !aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "hidden_states/out must be 16-byte aligned");
   if (peer && int8) return fail(MOE_ERR_UNSUPPORTED, "the int8 route has no peer-memory expert-parallel mode");
   const bool lsu = a_path_lsu() && !peer;
-  const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu);
+  if (ordered && (int8 || peer)) return fail(MOE_ERR_UNSUPPORTED, "the ordered combine is for the fp16/bf16 route");
+  const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu, ordered);
   if (!workspace || workspace_bytes < L.total) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", L.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
 
@@ -1086,7 +1092,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     else
       gather_rows_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
                                                          (int)H, static_cast<__half*>(xs), static_cast<__half*>(out),
-                                                         (int)T, nullptr, 0);
+                                                         ordered ? 0 : (int)T, nullptr, 0);
     MOE_CUDA(cudaGetLastError());
   } else {
     if (int8)
@@ -1096,7 +1102,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     else
       gather_rows_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<__nv_bfloat16*>(xs),
-          static_cast<__nv_bfloat16*>(out), (int)T, nullptr, 0);
+          static_cast<__nv_bfloat16*>(out), ordered ? 0 : (int)T, nullptr, 0);
     MOE_CUDA(cudaGetLastError());
   }
   prof_record(2, s);
@@ -1119,6 +1125,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (lsu) {  // the LSU path does not use the A tensor maps
     m1.a = m1.a1 = m1.b0;
     m2.a = m2.a1 = m2.b0;
+    if (ordered) MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
   } else {
     MOE_TRY(make_a_maps(&m1, xs, elt, L.P_max, H, t1.pair ? 1 : gmax1, "gathered hidden_states"));
     MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
@@ -1149,8 +1156,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a1.sorted_route_ids = sorted;
   a1.R = (int)R;
   a1.topk = (int)topk;
-  a1.zero_ptr = lsu ? out : nullptr;
-  a1.zero_bytes = lsu ? T * H * 2 : 0;
+  a1.zero_ptr = lsu && !ordered ? out : nullptr;
+  a1.zero_bytes = lsu && !ordered ? T * H * 2 : 0;
 
   GemmArgs a2{};
   a2.K = (int)I;
@@ -1208,7 +1215,32 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
     }
     prof_record(3, s);
-    if (t2.tn) {
+    if (ordered) {
+      // padded-store Stage2 into y (weights in raw order), then the in-order per-token sum
+      if (t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no ordered combine");
+      float* raw = reinterpret_cast<float*>(ws + L.raw);
+      void* y = ws + L.y;
+      raw_weights_kernel<<<sms * 2, 256, 0, s>>>(tw, a2.routed_dtype, sorted, gidx, go, gpo, meta, (int)R, L.P_max,
+                                                 kBM, raw);
+      MOE_CUDA(cudaGetLastError());
+      GemmArgs a = a2;
+      a.out = y;
+      a.group_sizes = gs;
+      a.group_offsets = go;
+      a.routed = raw;
+      a.routed_dtype = 0;
+      MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, false, tc2, dev, m2, a, max_tiles2, s)));
+      const int64_t want = (T + 7) / 8;
+      const int cblocks = static_cast<int>(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+      if (dtype == MOE_F16)
+        combine_ordered_kernel<__half><<<cblocks, 256, 0, s>>>(static_cast<const __half*>(y), slot, (int)T,
+                                                               (int)topk, (int)H, static_cast<__half*>(out));
+      else
+        combine_ordered_kernel<__nv_bfloat16><<<cblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(y), slot,
+                                                                      (int)T, (int)topk, (int)H,
+                                                                      static_cast<__nv_bfloat16*>(out));
+      MOE_CUDA(cudaGetLastError());
+    } else if (t2.tn) {
       TnMaps tm{};
       MOE_TRY(make_tmap(&tm.w, w2, 2, E * H, I, kBM, "w_down"));
       MOE_TRY(make_tn_x_maps(&tm, U, L.P_max, I, "intermediate"));
@@ -1251,6 +1283,19 @@ int moe_fused(const void* x, const void* w13, const void* w2, const void* ids, i
               void* workspace, size_t workspace_bytes, void* stream) {
   return fused_common(false, x, w13, nullptr, w2, nullptr, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk, dtype,
                       workspace, workspace_bytes, stream);
+}
+
+size_t moe_fused_ordered_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
+  (void)dtype;
+  if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+  return fused_layout(T, topk, E, H, I, false, a_path_lsu(), true).total;
+}
+
+int moe_fused_ordered(const void* x, const void* w13, const void* w2, const void* ids, int ids_dtype, const void* tw,
+                      int w_dtype, void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  return fused_common(false, x, w13, nullptr, w2, nullptr, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk, dtype,
+                      workspace, workspace_bytes, stream, nullptr, nullptr, true);
 }
 
 int moe_fused_router(const void* x, const void* w13, const void* w2, const void* logits, int logits_dtype,

@@ -133,11 +133,14 @@ def fused_moe(
     topk_ids: torch.Tensor,
     topk_weights: torch.Tensor,
     out: Optional[torch.Tensor] = None,
+    deterministic: bool = False,
 ) -> torch.Tensor:
     """out[t] = sum_j topk_weights[t,j] * W_down[e] (silu(W_gate[e] x_t) * W_up[e] x_t), e = topk_ids[t,j].
 
     hidden_states [T, H] fp16/bf16; w_gate_up [E, 2I, H] (gate rows first, then up rows);
     w_down [E, H, I]; topk_ids [T, k] int32/int64; topk_weights [T, k] fp32/fp16/bf16.
+    ``deterministic``: sum each token's k rows in route order in fp32 (``moe_fused_ordered``),
+    so repeated calls give identical bits; the default adds them with atomics in Stage2.
     """
     T, H, I, E, k = _check_fused(hidden_states, w_gate_up, w_down, topk_ids, topk_weights, False)
     if out is None:
@@ -147,10 +150,11 @@ def fused_moe(
         return out
     dev = hidden_states.device
     dt = _DTYPES[hidden_states.dtype]
-    nbytes = _lib.lib().moe_fused_workspace_bytes(T, k, E, H, I, dt)
+    fn = "moe_fused_ordered" if deterministic else "moe_fused"
+    nbytes = getattr(_lib.lib(), fn + "_workspace_bytes")(T, k, E, H, I, dt)
     ws = _workspace(("fused", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
     _lib.call(
-        "moe_fused", hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), topk_ids.data_ptr(),
+        fn, hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), topk_ids.data_ptr(),
         _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(), _W_DTYPES[topk_weights.dtype], out.data_ptr(),
         T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
     )

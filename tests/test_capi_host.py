@@ -55,9 +55,15 @@ def test_invalid_arguments_fail_before_any_launch():
     assert rc == -1 and b"num_blocks_m" in lib.moe_last_error()
     rc = lib.moe_align(None, _lib.MOE_I32, 10, 2000, 128, *([None] * 7), None, 0, None)
     assert rc == -1 and b"num_experts" in lib.moe_last_error()
-    with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
-        _lib.call("moe_fused", *([None] * 4), _lib.MOE_I8, None, _lib.MOE_F32, None, 4, 128, 128, 8, 2, _lib.MOE_F16,
-                  None, 0, None)
+    for fn in ("moe_fused", "moe_fused_ordered"):
+        with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
+            _lib.call(fn, *([None] * 4), _lib.MOE_I8, None, _lib.MOE_F32, None, 4, 128, 128, 8, 2, _lib.MOE_F16,
+                      None, 0, None)
+    # the ordered combine's workspace adds the padded Stage2 rows and the raw-order weights
+    T, k, E, H, I = 4096, 8, 256, 7168, 2048
+    extra = lib.moe_fused_ordered_workspace_bytes(T, k, E, H, I, _lib.MOE_F16) - lib.moe_fused_workspace_bytes(
+        T, k, E, H, I, _lib.MOE_F16)
+    assert extra >= lib.moe_max_padded_rows(T * k, E, 128) * H * 2 + T * k * 4
 
 
 def test_router_argument_checks():
