@@ -246,6 +246,27 @@ MOE_API int moe_fused_int8(const void* hidden_states, const void* w13_q, const f
                    void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * W8A8 fp8 (e4m3) route: the int8 route's scheme with e4m3 values (no reference counterpart; the
+ * reference probed fp8 MMA code generation only, xpuoj_data/probe_v209_fp8_mma.py:1).
+ * moe_quantize_rows_fp8: scale[r] = amax_r / 448, q[r, :] = e4m3(w[r, :] * (448 / amax_r)),
+ *   rounded to nearest even and saturated to +-448; q holds the e4m3 bytes.
+ * moe_fused_fp8: as moe_fused_int8 with fp8 weights and per-token fp8 activations; tcgen05
+ *   kind::f8f6f4 with fp32 accumulation. Runs on the TMA A path only.
+ * Requirements: H % 16 == 0, I % 16 == 0, 1 <= E <= 1024.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API int moe_quantize_rows_fp8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale,
+                                  void* stream);
+
+MOE_API size_t moe_fused_fp8_workspace_bytes(int64_t num_tokens, int64_t topk, int64_t num_experts, int64_t hidden,
+                                             int64_t intermediate, int dtype);
+
+MOE_API int moe_fused_fp8(const void* hidden_states, const void* w13_q, const float* w13_scale, const void* w2_q,
+                          const float* w2_scale, const void* topk_ids, int ids_dtype, const void* topk_weights,
+                          int weights_dtype, void* out, int64_t num_tokens, int64_t hidden, int64_t intermediate,
+                          int64_t num_experts, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Expert-parallel building blocks (no reference counterpart: the reference runs on one GPU;
  * these wrap the NCCL all-to-all exchange that muxi_race_b200/ep.py issues through
  * torch.distributed). Experts are owned by ranks: expert_rank [E], expert_local [E] int32.

@@ -4,6 +4,7 @@ Entry points:
   run_kernel(...)      drop-in for the contest operator's ``run_kernel`` (10 tensors, padded layout)
   fused_moe(...)       token-major fused MoE (routing alignment + both GEMM stages + top-k combine)
   fused_moe_int8(...)  W8A8 variant; weights from quantize_rows_int8()
+  fused_moe_fp8(...)   fp8 (e4m3) variant; weights from quantize_rows_fp8()
   moe_align(...)       device-side routing metadata
   fused_topk(...)      softmax top-k routing of router logits; fused_moe_router(...) routes + runs
   ep.ExpertParallelMoE expert-parallel fused MoE over torch.distributed (NCCL all-to-all)
@@ -11,11 +12,12 @@ Entry points:
 All compute runs in hand-written CUDA kernels of ``libmoe_b200.so`` (C ABI in
 ``include/moe_b200.h``); there is no CPU or library fallback.
 """
-from .fused import (Alignment, clear_workspace_cache, device_status, fused_moe, fused_moe_int8, fused_moe_router,
-                    fused_topk, max_padded_rows, moe_align, quantize_rows_int8)
+from .fused import (Alignment, clear_workspace_cache, device_status, fused_moe, fused_moe_fp8, fused_moe_int8,
+                    fused_moe_router, fused_topk, max_padded_rows, moe_align, quantize_rows_fp8, quantize_rows_int8)
 from .submission import run_kernel
 
 __all__ = [
-    "Alignment", "clear_workspace_cache", "device_status", "fused_moe", "fused_moe_int8", "fused_moe_router",
-    "fused_topk", "max_padded_rows", "moe_align", "quantize_rows_int8", "run_kernel",
+    "Alignment", "clear_workspace_cache", "device_status", "fused_moe", "fused_moe_fp8", "fused_moe_int8",
+    "fused_moe_router", "fused_topk", "max_padded_rows", "moe_align", "quantize_rows_fp8", "quantize_rows_int8",
+    "run_kernel",
 ]

@@ -78,6 +78,12 @@ SIGNATURES = {
     ),
     "moe_quantize_rows_int8": (_int, [_c_void_p, _int, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
     "moe_fused_int8_workspace_bytes": (_size, [_i64] * 5 + [_int]),
+    "moe_quantize_rows_fp8": (_int, [_c_void_p, _int, _i64, _i64, _c_void_p, _c_void_p, _c_void_p]),
+    "moe_fused_fp8_workspace_bytes": (_size, [_i64] * 5 + [_int]),
+    "moe_fused_fp8": (
+        _int,
+        [_c_void_p] * 6 + [_int, _c_void_p, _int, _c_void_p] + [_i64] * 5 + [_int, _c_void_p, _size, _c_void_p],
+    ),
     "moe_ep_plan_workspace_bytes": (_size, [_i64, _i64]),
     "moe_ep_plan": (_int, [_c_void_p, _int, _i64, _i64, _c_void_p, _i64, _i64] + [_c_void_p] * 5 + [_c_void_p, _size, _c_void_p]),
     "moe_ep_pack": (

@@ -375,7 +375,7 @@ int unit_order() {
   return v;
 }
 
-template <int MODE, typename OutT, bool I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
+template <int MODE, typename OutT, int I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
           int EPI = 4>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>;
@@ -402,7 +402,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
 }
 
 // CTA-pair kernel: clusters of two CTAs, one pair per two SMs (as many as can be resident).
-template <int MODE, typename OutT, bool I8, int AST, int BST, int EPI = 4>
+template <int MODE, typename OutT, int I8, int AST, int BST, int EPI = 4>
 int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST, EPI>;
   static const int evict_first = [] {
@@ -490,66 +490,88 @@ int launch_tn_rt(int dtype, int dev, int tcfg, const TnMaps& m, const TnArgs& ar
 }
 
 // One grouped GEMM stage with the chosen tile configuration.
-template <int MODE, typename OutT, bool I8, int AMODE>
+// I8: operand kind (kQ16, kQI8, kQF8); the fp8 kind is built for the default tiles and the TMA A
+// path only.
+template <int MODE, typename OutT, int I8, int AMODE>
 int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   constexpr bool kTma = AMODE == kATma;
   constexpr bool kS1 = MODE == kStage1;
-  switch (c) {
-    case kT256A4B5:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-    case kT256x2A3B4:  // the LSU A path's row table does not fit next to this ring: 2-deep A there
-      if constexpr (kTma)
-        return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-      else
-        return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-    case kT512A2B3:
-      return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-    case kT256A2B2C2:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2, 1>(dev, c, m, args, max_tiles, stream);
-    case kT256A6B4:
-      return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-    case kT256A6B2K2:
-      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 6, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT128x2A3B4K2:
-      if constexpr (kTma && kS1)
-        return launch_gemm<MODE, OutT, I8, 128, 2, 3, 4, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT128x2A4B3K2:
-      if constexpr (kTma && kS1)
-        return launch_gemm<MODE, OutT, I8, 128, 2, 4, 3, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT128x2A3B8:
-      if constexpr (kTma && kS1)
-        return launch_gemm<MODE, OutT, I8, 128, 2, 3, 8, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT256x2A3B2K2:
-      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kTP256A6B8:
-      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 6, 8>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kTP256A7B7:
-      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 7, 7>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kTP256A4B10:
-      if constexpr (kTma) return launch_pair<MODE, OutT, I8, 4, 10>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT256A4B5E8:
-      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
-      break;
-    case kT256x2A3B4E8:
-      if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
-      break;
+  if constexpr (I8 == kQF8) {
+    if constexpr (kTma) {
+      switch (c) {
+        case kT256A4B5:
+          return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+        case kT256x2A3B4:
+          return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+        case kT256A4B5E8:
+          return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        case kT256x2A3B4E8:
+          return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        case kTP256A6B8:
+          return launch_pair<MODE, OutT, I8, 6, 8>(dev, c, m, args, max_tiles, stream);
+        default:
+          break;
+      }
+    }
+    return fail(MOE_ERR_UNSUPPORTED, "tile configuration %s is not built for fp8 operands", kTiles[c].name);
+  } else {
+    switch (c) {
+      case kT256A4B5:
+        return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+      case kT256x2A3B4:  // the LSU A path's row table does not fit next to this ring: 2-deep A there
+        if constexpr (kTma)
+          return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+        else
+          return launch_gemm<MODE, OutT, I8, 256, 2, 2, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+      case kT512A2B3:
+        return launch_gemm<MODE, OutT, I8, 512, 1, 2, 3, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+      case kT256A2B2C2:
+        return launch_gemm<MODE, OutT, I8, 256, 1, 2, 2, AMODE, 2, 1>(dev, c, m, args, max_tiles, stream);
+      case kT256A6B4:
+        return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+      case kT256A6B2K2:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 6, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT128x2A3B4K2:
+        if constexpr (kTma && kS1)
+          return launch_gemm<MODE, OutT, I8, 128, 2, 3, 4, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT128x2A4B3K2:
+        if constexpr (kTma && kS1)
+          return launch_gemm<MODE, OutT, I8, 128, 2, 4, 3, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT128x2A3B8:
+        if constexpr (kTma && kS1)
+          return launch_gemm<MODE, OutT, I8, 128, 2, 3, 8, AMODE, 1, 1>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256x2A3B2K2:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 2, AMODE, 1, 2>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kTP256A6B8:
+        if constexpr (kTma) return launch_pair<MODE, OutT, I8, 6, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kTP256A7B7:
+        if constexpr (kTma) return launch_pair<MODE, OutT, I8, 7, 7>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kTP256A4B10:
+        if constexpr (kTma) return launch_pair<MODE, OutT, I8, 4, 10>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A4B5E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 4, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256x2A3B4E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
 
-    default:
-      break;
+      default:
+        break;
+    }
   }
   return fail(MOE_ERR_UNSUPPORTED, "tile configuration %s is not available for this stage", kTiles[c].name);
 }
 
 // Stage dispatch over the runtime element type and A path.
-template <int MODE, bool I8, int AMODE_LSU>
+template <int MODE, int I8, int AMODE_LSU>
 int launch_stage_rt(int dtype, bool lsu, TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles,
                     cudaStream_t stream) {
   if (dtype == MOE_F16)
@@ -968,7 +990,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
                         const float* w2_scale, const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out,
                         int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype, void* workspace,
                         size_t workspace_bytes, void* stream, const PeerSource* peer = nullptr,
-                        const RouterSource* router = nullptr, bool ordered = false) {
+                        const RouterSource* router = nullptr, bool ordered = false, bool fp8 = false) {
   t_last_error.clear();
   MOE_TRY(check_common(H, I, E, dtype, int8 ? 16 : 8));
   if (T < 0 || topk < 1) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be >= 0 and topk >= 1");
@@ -987,6 +1009,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (peer && int8) return fail(MOE_ERR_UNSUPPORTED, "the int8 route has no peer-memory expert-parallel mode");
   const bool lsu = a_path_lsu() && !peer;
   if (ordered && (int8 || peer)) return fail(MOE_ERR_UNSUPPORTED, "the ordered combine is for the fp16/bf16 route");
+  if (fp8 && !int8) return fail(MOE_ERR_INVALID_ARG, "fp8 is an 8-bit route");
+  if (fp8 && lsu) return fail(MOE_ERR_UNSUPPORTED, "the fp8 route runs on the TMA A path (MOE_B200_A_PATH=tma)");
   const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu, ordered);
   if (!workspace || workspace_bytes < L.total) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", L.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
@@ -1085,7 +1109,11 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
           static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs));
     MOE_CUDA(cudaGetLastError());
   } else if (dtype == MOE_F16) {
-    if (int8)
+    if (fp8)
+      gather_rows_q8_kernel<__half, kQF8><<<gblocks, 256, 0, s>>>(
+          static_cast<const __half*>(x), slot, (int)R, (int)topk, (int)H, static_cast<int8_t*>(xs), xscale,
+          static_cast<__half*>(out), (int)T, amax, (int)L.P_max);
+    else if (int8)
       gather_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), slot, (int)R, (int)topk,
                                                             (int)H, static_cast<int8_t*>(xs), xscale,
                                                             static_cast<__half*>(out), (int)T, amax, (int)L.P_max);
@@ -1095,7 +1123,11 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
                                                          ordered ? 0 : (int)T, nullptr, 0);
     MOE_CUDA(cudaGetLastError());
   } else {
-    if (int8)
+    if (fp8)
+      gather_rows_q8_kernel<__nv_bfloat16, kQF8><<<gblocks, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<int8_t*>(xs), xscale,
+          static_cast<__nv_bfloat16*>(out), (int)T, amax, (int)L.P_max);
+    else if (int8)
       gather_rows_q8_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
           static_cast<const __nv_bfloat16*>(x), slot, (int)R, (int)topk, (int)H, static_cast<int8_t*>(xs), xscale,
           static_cast<__nv_bfloat16*>(out), (int)T, amax, (int)L.P_max);
@@ -1258,6 +1290,22 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
     }
     prof_record(4, s);
+  } else if (fp8) {
+    // as the int8 route below, with e4m3 operands and fp32 accumulation (TMA A path only)
+    MOE_TRY((launch_stage_rt<kStage1, kQF8, kATma>(dtype, false, tc1, dev, m1, a1, max_tiles1, s)));
+    prof_record(3, s);
+    if (dtype == MOE_F16)
+      quantize_rows_q8_kernel<__half, kQF8><<<sms * 4, 256, 0, s>>>(
+          static_cast<const __half*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
+          reinterpret_cast<float*>(ws + L.uscale));
+    else
+      quantize_rows_q8_kernel<__nv_bfloat16, kQF8><<<sms * 4, 256, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
+          reinterpret_cast<float*>(ws + L.uscale));
+    MOE_CUDA(cudaGetLastError());
+    prof_record(4, s);
+    MOE_TRY((launch_stage_rt<kStage2Comb, kQF8, kATma>(dtype, false, tc2, dev, m2, a2, max_tiles2, s)));
+    prof_record(5, s);
   } else {
     // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
     MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
@@ -1308,7 +1356,8 @@ int moe_fused_router(const void* x, const void* w13, const void* w2, const void*
                       workspace, workspace_bytes, stream, nullptr, &rs);
 }
 
-int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale, void* stream) {
+static int quantize_rows(bool fp8, const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale,
+                         void* stream) {
   t_last_error.clear();
   if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
   if (rows < 0 || cols <= 0 || cols % 16 != 0) return fail(MOE_ERR_INVALID_ARG, "cols must be a positive multiple of 16");
@@ -1319,7 +1368,13 @@ int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols,
   MOE_TRY(current_device(&dev));
   MOE_TRY(device_sms(dev, &sms));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == MOE_F16)
+  if (fp8 && dtype == MOE_F16)
+    quantize_rows_q8_kernel<__half, kQF8><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(w), rows, (int)cols,
+                                                                  nullptr, nullptr, static_cast<int8_t*>(q), scale);
+  else if (fp8)
+    quantize_rows_q8_kernel<__nv_bfloat16, kQF8><<<sms * 4, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(w), rows, (int)cols, nullptr, nullptr, static_cast<int8_t*>(q), scale);
+  else if (dtype == MOE_F16)
     quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(w), rows, (int)cols, nullptr,
                                                             nullptr, static_cast<int8_t*>(q), scale);
   else
@@ -1328,6 +1383,14 @@ int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols,
                                                                    static_cast<int8_t*>(q), scale);
   MOE_CUDA(cudaGetLastError());
   return MOE_OK;
+}
+
+int moe_quantize_rows_int8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale, void* stream) {
+  return quantize_rows(false, w, dtype, rows, cols, q, scale, stream);
+}
+
+int moe_quantize_rows_fp8(const void* w, int dtype, int64_t rows, int64_t cols, void* q, float* scale, void* stream) {
+  return quantize_rows(true, w, dtype, rows, cols, q, scale, stream);
 }
 
 size_t moe_fused_int8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
@@ -1342,6 +1405,20 @@ int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, con
                    void* stream) {
   return fused_common(true, x, w13_q, w13_scale, w2_q, w2_scale, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
                       dtype, workspace, workspace_bytes, stream);
+}
+
+size_t moe_fused_fp8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
+  (void)dtype;
+  if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+  return fused_layout(T, topk, E, H, I, true, false).total;
+}
+
+int moe_fused_fp8(const void* x, const void* w13_q, const float* w13_scale, const void* w2_q, const float* w2_scale,
+                  const void* ids, int ids_dtype, const void* tw, int w_dtype, void* out, int64_t T, int64_t H,
+                  int64_t I, int64_t E, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
+                  void* stream) {
+  return fused_common(true, x, w13_q, w13_scale, w2_q, w2_scale, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
+                      dtype, workspace, workspace_bytes, stream, nullptr, nullptr, false, true);
 }
 
 // ---------------------------------------------------------------------------- expert parallel

@@ -43,8 +43,9 @@
 //               padded stacked layout (reference Stage2, SUB/submission.py:317-357, 933-947);
 //   kStage2Comb out[token(p), :] += D * topk_weight(p) via vector red.add into the token-major
 //               output (the top-k combine fused into the down GEMM's epilogue).
-// Integer variants (IS_I8) dequantise the int32 accumulator with per-row (token) and per-column
-// (weight output row) scales before the same epilogue.
+// 8-bit variants (Q8 = kQI8: int8 with int32 accumulation; kQF8: fp8 e4m3 with fp32
+// accumulation) dequantise the accumulator with per-row (token) and per-column (weight output
+// row) scales before the same epilogue.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -195,6 +196,13 @@ __device__ __forceinline__ float load_weight(const void* w, int dtype, int i) {
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(w)[i]);
 }
 
+// Accumulator word -> fp32: int32 for the int8 kind, fp32 otherwise.
+template <int Q8>
+__device__ __forceinline__ float acc_f32(uint32_t d) {
+  if constexpr (Q8 == kQI8) return static_cast<float>(static_cast<int>(d));
+  return __uint_as_float(d);
+}
+
 // silu(g) * u = g / (1 + e^-g) * u; the exponential is CUDA's __expf.
 __device__ __forceinline__ float silu_mul(float g, float u) { return g * __frcp_rn(1.0f + __expf(-g)) * u; }
 
@@ -237,7 +245,7 @@ __device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& f
 // ------------------------------------------------------------------ epilogue of one block
 // Columns [c_begin, c_end) of the block's output tile (Stage1: of the BN/2 SiLU*up outputs), in
 // chunks of 32: with 8 epilogue warps two warps share a TMEM lane quadrant, each taking half.
-template <int MODE, typename OutT, bool IS_I8, int BN, int AMODE>
+template <int MODE, typename OutT, int Q8, int BN, int AMODE>
 __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_row, int mb, int nt, int e,
                                                int row_in_tile, int c_begin, int c_end) {
   const int p = mb * kBM + row_in_tile;  // padded row of this thread
@@ -245,7 +253,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     OutT* U = reinterpret_cast<OutT*>(args.U);
     const int n0 = nt * (BN / 2);
     float sa = 1.0f;
-    if (IS_I8) {
+    if (Q8) {
       const long long src = a_source_row<AMODE>(args, p);
       sa = src >= 0 ? args.a_scale[src] : 0.0f;
     }
@@ -263,13 +271,13 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         float g0, g1, u0, u1;
-        if (IS_I8) {
+        if (Q8) {
           const int cc = min(col0 + j, args.N - 2);
           const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
-          g0 = static_cast<float>(static_cast<int>(g[j])) * sa * args.b0_scale[wrow + cc];
-          g1 = static_cast<float>(static_cast<int>(g[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
-          u0 = static_cast<float>(static_cast<int>(u[j])) * sa * args.b1_scale[wrow + args.b1_row_offset + cc];
-          u1 = static_cast<float>(static_cast<int>(u[j + 1])) * sa * args.b1_scale[wrow + args.b1_row_offset + cc + 1];
+          g0 = acc_f32<Q8>(g[j]) * sa * args.b0_scale[wrow + cc];
+          g1 = acc_f32<Q8>(g[j + 1]) * sa * args.b0_scale[wrow + cc + 1];
+          u0 = acc_f32<Q8>(u[j]) * sa * args.b1_scale[wrow + args.b1_row_offset + cc];
+          u1 = acc_f32<Q8>(u[j + 1]) * sa * args.b1_scale[wrow + args.b1_row_offset + cc + 1];
         } else {
           g0 = __uint_as_float(g[j]);
           g1 = __uint_as_float(g[j + 1]);
@@ -277,7 +285,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
           u1 = __uint_as_float(u[j + 1]);
         }
         const float h0 = silu_mul(g0, u0), h1 = silu_mul(g1, u1);
-        if (IS_I8 && col0 + j < args.N) amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
+        if (Q8 && col0 + j < args.N) amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
         packed[j / 2] = Elt<OutT>::pack2(h0, h1);
       }
       OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
@@ -288,7 +296,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
               make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
       }
     }
-    if (IS_I8 && args.row_amax) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
+    if (Q8 && args.row_amax) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
   } else {
     const int n0 = nt * BN;
     float scale = 0.0f;
@@ -311,7 +319,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       }
     }
     float sa = 1.0f;
-    if (IS_I8) sa = args.a_scale[p];
+    if (Q8) sa = args.a_scale[p];
     OutT* out = reinterpret_cast<OutT*>(args.out);
     const size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
 #pragma unroll 1
@@ -325,11 +333,11 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         float d0, d1;
-        if (IS_I8) {
+        if (Q8) {
           const int cc = min(col0 + j, args.N - 2);
           const size_t wrow = static_cast<size_t>(e) * args.b_rows_per_expert;
-          d0 = static_cast<float>(static_cast<int>(d[j])) * sa * args.b0_scale[wrow + cc];
-          d1 = static_cast<float>(static_cast<int>(d[j + 1])) * sa * args.b0_scale[wrow + cc + 1];
+          d0 = acc_f32<Q8>(d[j]) * sa * args.b0_scale[wrow + cc];
+          d1 = acc_f32<Q8>(d[j + 1]) * sa * args.b0_scale[wrow + cc + 1];
         } else {
           d0 = __uint_as_float(d[j]);
           d1 = __uint_as_float(d[j + 1]);
@@ -363,7 +371,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 //         when args.b_split. Stage2: {K, rows} for KPB = 1, {k-block elements, rows, k-blocks}
 //         otherwise.
 //   tmB1  Stage1 with args.b_split: the up rows ({K, rows}).
-template <int MODE, typename OutT, bool IS_I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
+template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
           int EPI = 4>
 __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
@@ -434,8 +442,8 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
 
   const int ngroups = args.ngroups >= 0 ? args.ngroups : *args.ngroups_dev;
   const int num_tiles = ngroups * args.n_tiles;
-  const int num_kb = (args.K * (IS_I8 ? 1 : 2) + kKBytes - 1) / kKBytes;
-  constexpr int kKElems = IS_I8 ? kKBytes : kKBytes / 2;
+  const int num_kb = (args.K * (Q8 ? 1 : 2) + kKBytes - 1) / kKBytes;
+  constexpr int kKElems = Q8 ? kKBytes : kKBytes / 2;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- B producer (weights)
@@ -501,7 +509,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     // the group re-reads these rows.
     if (AMODE != kATma || lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
-      const long long a_k_bytes = static_cast<long long>(args.K) * (IS_I8 ? 1 : 2);
+      const long long a_k_bytes = static_cast<long long>(args.K) * (Q8 ? 1 : 2);
       int st = 0;
       uint32_t ph = 0;
       bool ok = true;
@@ -571,7 +579,9 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = IS_I8 ? idesc_i8(kBM, kMN) : idesc_f16(Elt<OutT>::kBF16, kBM, kMN);
+      const uint32_t idesc = Q8 == kQF8 ? idesc_f8(kBM, kMN)
+                             : Q8   ? idesc_i8(kBM, kMN)
+                                    : idesc_f16(Elt<OutT>::kBF16, kBM, kMN);
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
       uint32_t slot_cnt = 0;  // accumulator slots handed out so far (slot = cnt % kSlots)
@@ -616,7 +626,9 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
               for (int h = 0; h < kHalves; ++h) {
                 const uint64_t bd = smem_desc_sw128(b_addr + h * (kMN * kKBytes) + k * 32);
                 const uint32_t d = d_tmem[j] + static_cast<uint32_t>(h * kMN);
-                if (IS_I8)
+                if (Q8 == kQF8)
+                  mma_f8(d, ad, bd, idesc, (kb | k) != 0);
+                else if (Q8)
                   mma_i8(d, ad, bd, idesc, (kb | k) != 0);
                 else
                   mma_f16(d, ad, bd, idesc, (kb | k) != 0);
@@ -680,7 +692,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
         tc_fence_after();
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * BN);
-        epilogue_block<MODE, OutT, IS_I8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile, c_begin, c_end);
+        epilogue_block<MODE, OutT, Q8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile, c_begin, c_end);
         // hand the slot back to the MMA warp
         tc_fence_before();
         __syncwarp();

@@ -41,7 +41,7 @@ template <int AST, int BST> struct PairRing {
 // Tensor maps: tmA token rows (box 128 rows); tmB0 weight rows (box 128 rows): Stage1 gate rows
 // (and up rows at +args.b1_row_offset when tmB1 is the same tensor), Stage2 down rows; tmB1
 // Stage1 up rows. Work units = (block group of <= 2 blocks, 256-column tile), from args.groups.
-template <int MODE, typename OutT, bool IS_I8, int AST, int BST, int EPI = 4>
+template <int MODE, typename OutT, int Q8, int AST, int BST, int EPI = 4>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
     moe_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                          const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
@@ -109,8 +109,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
 
   const int ngroups = args.ngroups >= 0 ? args.ngroups : *args.ngroups_dev;
   const int num_tiles = ngroups * args.n_tiles;
-  const int num_kb = (args.K * (IS_I8 ? 1 : 2) + kKBytes - 1) / kKBytes;
-  constexpr int kKElems = IS_I8 ? kKBytes : kKBytes / 2;
+  const int num_kb = (args.K * (Q8 ? 1 : 2) + kKBytes - 1) / kKBytes;
+  constexpr int kKElems = Q8 ? kKBytes : kKBytes / 2;
 
   if (warp == 0 || warp == 6) {
     // ---------------------------------------------------------------- producers
@@ -176,7 +176,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader)
     if (leader && lane == 0) {
-      const uint32_t idesc = IS_I8 ? idesc_i8(2 * kBM, kN) : idesc_f16(Elt<OutT>::kBF16, 2 * kBM, kN);
+      const uint32_t idesc = Q8 == kQF8 ? idesc_f8(2 * kBM, kN)
+                             : Q8   ? idesc_i8(2 * kBM, kN)
+                                    : idesc_f16(Elt<OutT>::kBF16, 2 * kBM, kN);
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
       uint32_t slot_cnt = 0;
@@ -203,7 +205,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
           for (int k = 0; k < kKBytes / 32; ++k) {
             const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
             const uint64_t bd = smem_desc_sw128(b_addr + k * 32);
-            if (IS_I8)
+            if (Q8 == kQF8)
+              mma_f8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else if (Q8)
               mma_i8_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
             else
               mma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
@@ -250,7 +254,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
       tc_fence_after();
       if (leader || nb == 2) {
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * kN);
-        epilogue_block<MODE, OutT, IS_I8, kN, kATma>(args, t_row, fb + static_cast<int>(rank), nt, e, row_in_tile,
+        epilogue_block<MODE, OutT, Q8, kN, kATma>(args, t_row, fb + static_cast<int>(rank), nt, e, row_in_tile,
                                                      eg * kSpan, eg * kSpan + kSpan);
       }
       tc_fence_before();

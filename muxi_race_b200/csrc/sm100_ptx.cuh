@@ -196,6 +196,16 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, fp8 inputs (both e4m3), fp32 accumulate.
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // 32 lanes x 32 consecutive 32-bit columns: thread i of the warp receives row (lane_base + i).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -330,6 +340,15 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand stored with the 128-byte swizzle
 // that a TMA SWIZZLE_128B box produces: rows of 128 B, 8-row atoms of 1024 B (SBO), the
@@ -347,7 +366,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
 
 // Instruction descriptor, dense, K-major A and B.
 //   c_format [4,6): 1 = F32, 2 = S32;  a/b format [7,10)/[10,13): F16 0, BF16 1 (kind::f16),
-//   signed int8 1 (kind::i8);  N>>3 at [17,23);  M>>4 at [24,29).
+//   signed int8 1 (kind::i8), E4M3 0 (kind::f8f6f4);  N>>3 at [17,23);  M>>4 at [24,29).
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N) {
   return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
@@ -356,5 +375,12 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
 }
+__host__ __device__ constexpr uint32_t idesc_f8(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+// Operand kinds of the grouped GEMMs (template argument Q): 16-bit, int8, fp8 e4m3. The two 8-bit
+// kinds share the data layout (128 elements per 128-byte k-block, K = 32 per MMA) and the
+// per-row / per-column scale epilogue; they differ in the MMA kind and the accumulator type.
+enum QKind : int { kQ16 = 0, kQI8 = 1, kQF8 = 2 };
 
 }  // namespace moe

@@ -102,7 +102,7 @@ def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) 
 
 
 # ----------------------------------------------------------------------------- fused fp16/bf16
-def _check_fused(hidden_states, w13, w2, topk_ids, topk_weights, int8: bool):
+def _check_fused(hidden_states, w13, w2, topk_ids, topk_weights, int8, q_dtype=torch.int8):
     _check(hidden_states.dim() == 2, "hidden_states must be [T, H]")
     T, H = hidden_states.shape
     _check(w13.dim() == 3 and w2.dim() == 3, "w_gate_up must be [E, 2I, H] and w_down [E, H, I]")
@@ -117,7 +117,7 @@ def _check_fused(hidden_states, w13, w2, topk_ids, topk_weights, int8: bool):
                "all tensors must be contiguous CUDA tensors on one device")
     _check(hidden_states.dtype in _DTYPES, f"unsupported activation dtype {hidden_states.dtype}")
     if int8:
-        _check(w13.dtype == torch.int8 and w2.dtype == torch.int8, "int8 weights expected")
+        _check(w13.dtype == q_dtype and w2.dtype == q_dtype, f"{q_dtype} weights expected")
     else:
         _check(w13.dtype == hidden_states.dtype and w2.dtype == hidden_states.dtype,
                "weights must have the activation dtype")
@@ -281,6 +281,57 @@ def fused_moe_int8(
     ws = _workspace(("fused_i8", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
     _lib.call(
         "moe_fused_int8", hidden_states.data_ptr(), w13_q.data_ptr(), w13_scale.data_ptr(), w2_q.data_ptr(),
+        w2_scale.data_ptr(), topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(),
+        _W_DTYPES[topk_weights.dtype], out.data_ptr(), T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
+    )
+    return out
+
+
+# ----------------------------------------------------------------------------- W8A8 fp8 (e4m3)
+def quantize_rows_fp8(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row e4m3: scale = amax_row / 448, q = e4m3(w * (448 / amax_row)) (nearest even, saturated).
+
+    ``w`` [..., K] fp16/bf16. Returns (q torch.float8_e4m3fn of w's shape, scale fp32 of shape
+    w.shape[:-1]).
+    """
+    _check(w.is_cuda and w.is_contiguous() and w.dtype in _DTYPES, "w must be a contiguous fp16/bf16 CUDA tensor")
+    K = w.shape[-1]
+    rows = w.numel() // K if K else 0
+    q = torch.empty(w.shape, dtype=torch.float8_e4m3fn, device=w.device)
+    scale = torch.empty(w.shape[:-1], dtype=torch.float32, device=w.device)
+    _lib.call("moe_quantize_rows_fp8", w.data_ptr(), _DTYPES[w.dtype], rows, K, q.data_ptr(), scale.data_ptr(),
+              _stream(w.device))
+    return q, scale
+
+
+def fused_moe_fp8(
+    hidden_states: torch.Tensor,
+    w13_q: torch.Tensor,
+    w13_scale: torch.Tensor,
+    w2_q: torch.Tensor,
+    w2_scale: torch.Tensor,
+    topk_ids: torch.Tensor,
+    topk_weights: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """fp8 ``fused_moe``: e4m3 weights with per-output-row scales (from :func:`quantize_rows_fp8`),
+    activations quantised to e4m3 per token on the device, fp32 accumulation, output in the
+    activation dtype."""
+    T, H, I, E, k = _check_fused(hidden_states, w13_q, w2_q, topk_ids, topk_weights, True, torch.float8_e4m3fn)
+    _check(w13_scale.dtype == torch.float32 and w13_scale.numel() == E * 2 * I and w13_scale.is_contiguous(),
+           "w13_scale must be fp32 [E, 2I]")
+    _check(w2_scale.dtype == torch.float32 and w2_scale.numel() == E * H and w2_scale.is_contiguous(),
+           "w2_scale must be fp32 [E, H]")
+    if out is None:
+        out = torch.empty((T, H), dtype=hidden_states.dtype, device=hidden_states.device)
+    if T == 0:
+        return out
+    dev = hidden_states.device
+    dt = _DTYPES[hidden_states.dtype]
+    nbytes = _lib.lib().moe_fused_fp8_workspace_bytes(T, k, E, H, I, dt)
+    ws = _workspace(("fused_f8", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    _lib.call(
+        "moe_fused_fp8", hidden_states.data_ptr(), w13_q.data_ptr(), w13_scale.data_ptr(), w2_q.data_ptr(),
         w2_scale.data_ptr(), topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(),
         _W_DTYPES[topk_weights.dtype], out.data_ptr(), T, H, I, E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev),
     )

@@ -25,6 +25,10 @@ What it restates (the reference is William7743/muxi_race):
 * ``fused_moe_int8_ref`` — the W8A8 route with the quantisation scheme of the reference's int8
   experiment (``xpuoj_data/submission_v322_int8_v2.py:186-203``: amax/127 scale, round half away
   from zero, clamp to +-127), per output row for weights and per row for activations.
+* ``fused_moe_fp8_ref`` — the same route with e4m3 values (scale amax/448, nearest-even
+  rounding, saturation), the fp8 weights path of the scope's "next" rows; the reference only
+  probed fp8 MMA code generation (``xpuoj_data/probe_v209_fp8_mma.py``), so this one is pinned by
+  its own CPU tests, not by reference outputs.
 
 Parity is pinned by ``tests/golden/`` (outputs of the reference's own PyTorch code, extracted
 from the problem statement and run by ``tests/golden/make_golden.py``).
@@ -176,18 +180,33 @@ def quantize_rows_ref(w: torch.Tensor):
     return q, amax / torch.full_like(amax, 127.0)
 
 
+def quantize_rows_fp8_ref(w: torch.Tensor):
+    """e4m3 per row: scale = amax / 448, q = e4m3(w * (448 / amax)), nearest even, saturated to +-448.
+
+    The int8 scheme above with the e4m3 range (no reference counterpart beyond the reference's fp8
+    MMA probe, xpuoj_data/probe_v209_fp8_mma.py:1). torch's float32 -> float8_e4m3fn cast rounds to
+    nearest even but turns values past the top binade into NaN, so the products are clamped to
+    +-448 first (what a saturating conversion gives)."""
+    wf = w.to(torch.float32)
+    amax = wf.abs().amax(dim=-1)
+    inv = torch.where(amax > 0, torch.full_like(amax, 448.0) / amax, torch.zeros_like(amax))
+    v = (wf * inv.unsqueeze(-1)).clamp(-448.0, 448.0)
+    return v.to(torch.float8_e4m3fn), amax / torch.full_like(amax, 448.0)
+
+
 def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights,
-                       out_dtype=torch.float16) -> torch.Tensor:
+                       out_dtype=torch.float16, quantize=quantize_rows_ref) -> torch.Tensor:
     """Exact model of the W8A8 route: per-token int8 x, per-row int8 weights, exact integer GEMMs
     (float64 accumulation of int8 products is exact here), dequant, silu*up rounded to the output
     dtype, per-row requantisation of the intermediate, int8 down GEMM, dequant, route weight,
-    per-token sum. Returns fp32 [T, H]."""
+    per-token sum. Returns fp32 [T, H]. With ``quantize=quantize_rows_fp8_ref`` and e4m3 weights
+    it is the fp8 route (products of e4m3 values are exact in float64 too)."""
     T, H = hidden_states.shape
     E = w13_q.shape[0]
     I = w13_q.shape[1] // 2
     k = topk_ids.shape[1]
     dev = hidden_states.device
-    xq, xs = quantize_rows_ref(hidden_states)
+    xq, xs = quantize(hidden_states)
     ids = topk_ids.reshape(-1).to(torch.int64)
     w = topk_weights.reshape(-1).to(torch.float32)
     out = torch.zeros((T, H), dtype=torch.float32, device=dev)
@@ -203,8 +222,15 @@ def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids
         deq = acc.to(torch.float32) * xs[tok].unsqueeze(1) * w13s[e].unsqueeze(0)
         g, u = deq[:, :I], deq[:, I:]
         h = (g * torch.reciprocal(1.0 + torch.exp(-g)) * u).to(out_dtype)
-        hq, hs = quantize_rows_ref(h)
+        hq, hs = quantize(h)
         acc2 = hq.to(torch.float64) @ w2_q[e].to(torch.float64).T
         y = acc2.to(torch.float32) * hs.unsqueeze(1) * w2s[e].unsqueeze(0)
         out.index_add_(0, tok, y * w[routes].unsqueeze(1))
     return out
+
+
+def fused_moe_fp8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights,
+                      out_dtype=torch.float16) -> torch.Tensor:
+    """Exact model of the fp8 (e4m3) route; see ``fused_moe_int8_ref``."""
+    return fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids, topk_weights, out_dtype,
+                              quantize=quantize_rows_fp8_ref)
