@@ -210,31 +210,40 @@ def bench_ours(args, world, rank, local):
         return bench_ep(args, world, rank, local)
     import muxi_race_b200 as m
     from muxi_race_b200 import _lib
-    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_router_logits, make_routing, make_weights
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = CONFIGS[args.config]
     peaks, peak_kind = load_peaks()
+    variant = args.variant
+    q8 = cfg.int8 or variant == "fp8"
 
     w13, w2 = make_weights(cfg, seed=0, device=dev)
     x = make_hidden(cfg, seed=1 + rank, device=dev)
     ids, tw = make_routing(cfg, seed=2 + rank, device=dev)
-    if cfg.int8:
-        w13q, w13s = m.quantize_rows_int8(w13)
-        w2q, w2s = m.quantize_rows_int8(w2)
+    # inputs of one call after x: (topk_ids, topk_weights), or the router logits for "router"
+    ins = [make_router_logits(cfg, seed=2 + rank, device=dev)] if variant == "router" else [ids, tw]
+    if q8:
+        quant = m.quantize_rows_fp8 if variant == "fp8" else m.quantize_rows_int8
+        fused_q = m.fused_moe_fp8 if variant == "fp8" else m.fused_moe_int8
+        w13q, w13s = quant(w13)
+        w2q, w2s = quant(w2)
         del w13, w2
-        fn = lambda xx, ii, ww, oo: m.fused_moe_int8(xx, w13q, w13s, w2q, w2s, ii, ww, out=oo)  # noqa: E731
+        fn = lambda xx, ii, ww, oo: fused_q(xx, w13q, w13s, w2q, w2s, ii, ww, out=oo)  # noqa: E731
+    elif variant == "router":
+        fn = lambda xx, lg, oo: m.fused_moe_router(xx, w13, w2, lg, cfg.topk, out=oo)  # noqa: E731
     else:
-        fn = lambda xx, ii, ww, oo: m.fused_moe(xx, w13, w2, ii, ww, out=oo)  # noqa: E731
+        det = variant == "ordered"
+        fn = lambda xx, ii, ww, oo: m.fused_moe(xx, w13, w2, ii, ww, out=oo, deterministic=det)  # noqa: E731
     out = torch.empty((cfg.T, cfg.H), dtype=cfg.dtype, device=dev)
     routes = cfg.T * cfg.topk
     active = int(torch.unique(ids).numel())
     flops = cfg.flops()
-    n_ev = 6 if cfg.int8 else 5
+    n_ev = 6 if q8 else 5
 
     for _ in range(args.warmup):
-        fn(x, ids, tw, out)
+        fn(x, *ins, out)
     torch.cuda.synchronize()
     st = m.device_status()
     assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after warm-up"
@@ -253,7 +262,7 @@ def bench_ours(args, world, rank, local):
     start.record(stream)
     for k in range(args.steps):
         _lib.set_profile_events(evs[k])
-        fn(x, ids, tw, out)
+        fn(x, *ins, out)
     _lib.set_profile_events(None)
     end.record(stream)
     torch.cuda.synchronize()
@@ -265,24 +274,21 @@ def bench_ours(args, world, rank, local):
         return sum(evs[k][a].elapsed_time(evs[k][b]) for k in range(args.steps)) / args.steps
 
     stages = {"align": stage_ms(0, 1), "gather": stage_ms(1, 2), "stage1": stage_ms(2, 3)}
-    if cfg.int8:
+    if q8:
         stages["requant"] = stage_ms(3, 4)
         stages["stage2"] = stage_ms(4, 5)
     else:
         stages["stage2"] = stage_ms(3, 4)
 
     # ---- end to end through the public API with host buffers
-    x_h = x.cpu().pin_memory()
-    ids_h = ids.cpu().pin_memory()
-    tw_h = tw.cpu().pin_memory()
+    hosts = [t.cpu().pin_memory() for t in [x] + ins]
+    devs = [torch.empty_like(t) for t in [x] + ins]
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    x_d, ids_d, tw_d = torch.empty_like(x), torch.empty_like(ids), torch.empty_like(tw)
 
     def e2e_step():
-        x_d.copy_(x_h, non_blocking=True)
-        ids_d.copy_(ids_h, non_blocking=True)
-        tw_d.copy_(tw_h, non_blocking=True)
-        fn(x_d, ids_d, tw_d, out)
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        fn(*devs, out)
         out_h.copy_(out, non_blocking=True)
 
     torch.cuda.synchronize()
@@ -300,13 +306,13 @@ def bench_ours(args, world, rank, local):
     barrier(world)
     e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
     clock_info = clocks.stop()  # sampled across both timed regions
-    h2d = x_h.numel() * x_h.element_size() + ids_h.numel() * ids_h.element_size() + tw_h.numel() * tw_h.element_size()
+    h2d = sum(h.numel() * h.element_size() for h in hosts)
     d2h = out_h.numel() * out_h.element_size()
     st = m.device_status()
     assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after timing"
 
     # ---- roofline of the dominant kernel (Stage1): algorithmic bytes per launch / launch time
-    elt = 1 if cfg.int8 else 2
+    elt = 1 if q8 else 2
     s1_bytes = active * 2 * cfg.I * cfg.H * elt + routes * cfg.H * elt + routes * cfg.I * 2
     s1_gbs = s1_bytes / (stages["stage1"] * 1e-3) / 1e9
     traffic = None
@@ -333,14 +339,15 @@ def bench_ours(args, world, rank, local):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "int8" if cfg.int8 else ("fp16" if cfg.dtype == torch.float16 else "bf16"),
+        "dtype": "fp8" if variant == "fp8" else "int8" if cfg.int8 else ("fp16" if cfg.dtype == torch.float16 else "bf16"),
         "data": "synthetic (seeded; weights N(0,1/fan_in), hidden N(0,1), softmax-top-k of N(0,1) logits)",
         "config": {
             "workload": f"{cfg.name}: fused MoE T={cfg.T} H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
             "tokens_per_rank": cfg.T, "routed_rows_per_rank": routes, "active_experts": active,
             "parallelism": "replicas" if world > 1 else "single",
-            "l2": f"inputs larger than L2 ({active * 3 * cfg.H * cfg.I * (1 if cfg.int8 else 2) / 1e9:.1f} GB of "
+            "l2": f"inputs larger than L2 ({active * 3 * cfg.H * cfg.I * elt / 1e9:.1f} GB of "
                   "expert weights streamed per step)",
+            **({} if variant == "default" else {"variant": variant}),
         },
         "ms_per_call": round(ms, 4),
         "tflops_per_gpu": round(flops / (ms * 1e-3) / 1e12, 2),
@@ -352,7 +359,9 @@ def bench_ours(args, world, rank, local):
         "roofline": roofline,
         "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps * (7 if cfg.int8 else 6),
+        # per call: alignment (count or router, scan, scatter), block groups, gather, Stage1, Stage2;
+        # 8-bit routes add the intermediate requantisation, the ordered combine its two kernels
+        "gpu_launches": args.steps * (8 if q8 else 9 if variant == "ordered" else 7),
         "clocks": clock_info,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -668,6 +677,9 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
                     help="run_kernel: the reference drop-in on the reference's contest case --case")
     ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))
+    ap.add_argument("--variant", default="default", choices=["default", "ordered", "router", "fp8"],
+                    help="single-GPU fused call: ordered (deterministic) combine, routing from router logits "
+                         "on the device, or the fp8 route")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.path == "run_kernel":

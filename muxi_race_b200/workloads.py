@@ -90,12 +90,19 @@ def zipf_bias(E: int, s: float, seed: int = ZIPF_SEED, device="cpu") -> torch.Te
     return pmf.log().to(torch.float32).to(device)
 
 
-def make_routing(cfg: MoeConfig, seed: int = 2, device="cuda", T: int | None = None, id_dtype=torch.int32):
-    """topk_ids [T, k] (id_dtype) and topk_weights [T, k] fp32 from softmax-top-k of N(0,1) logits."""
+def make_router_logits(cfg: MoeConfig, seed: int = 2, device="cuda", T: int | None = None) -> torch.Tensor:
+    """Router logits [T, E] fp32: N(0,1), plus the log-Zipf popularity bias when cfg.zipf_s > 0."""
     T = cfg.T if T is None else T
     logits = torch.randn((T, cfg.E), generator=_gen(device, seed), device=device)
     if cfg.zipf_s > 0:
         logits = logits + zipf_bias(cfg.E, cfg.zipf_s, device=device)
+    return logits
+
+
+def make_routing(cfg: MoeConfig, seed: int = 2, device="cuda", T: int | None = None, id_dtype=torch.int32):
+    """topk_ids [T, k] (id_dtype) and topk_weights [T, k] fp32 from softmax-top-k of the logits of
+    make_router_logits (same seed: same routing)."""
+    logits = make_router_logits(cfg, seed, device, T)
     probs = torch.softmax(logits, dim=-1)
     vals, ids = torch.topk(probs, cfg.topk, dim=-1)
     weights = vals / vals.sum(dim=-1, keepdim=True)
