@@ -39,7 +39,8 @@ typedef enum {
   MOE_F32 = 2,
   MOE_I32 = 3,
   MOE_I64 = 4,
-  MOE_I8 = 5
+  MOE_I8 = 5,
+  MOE_F8E4M3 = 6
 } moe_dtype_t;
 
 typedef enum {
@@ -265,6 +266,40 @@ MOE_API int moe_fused_fp8(const void* hidden_states, const void* w13_q, const fl
                           int weights_dtype, void* out, int64_t num_tokens, int64_t hidden, int64_t intermediate,
                           int64_t num_experts, int64_t topk, int dtype, void* workspace, size_t workspace_bytes,
                           void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Packed weights: one buffer holding an expert set in the layout the fused kernels read (no
+ * reference counterpart: the reference takes gate_w, up_w [E, I, H] and down_w [E, H, I] as
+ * separate tensors on every call, 初审材料/源代码/submission.py:2098-2109). Sections, each
+ * starting on a 256-byte boundary, in this order:
+ *   w13       [E, 2I, H] kind   expert e's gate rows (0..I-1) then its up rows (I..2I-1): one
+ *                               TMA stream and one [gate | up] accumulator per tile
+ *   w13_scale [E * 2I] fp32     8-bit kinds only: per-row scales
+ *   w2        [E, H, I] kind
+ *   w2_scale  [E * H] fp32      8-bit kinds only
+ * kind = MOE_F16 / MOE_BF16 (the activation dtype, weights copied), MOE_I8 or MOE_F8E4M3
+ * (quantised per row as moe_quantize_rows_int8 / _fp8 do). The layout depends only on (E, H, I,
+ * kind), so a packed buffer can be written to a file and mapped back.
+ * moe_packed_weights_layout: byte offsets of the four sections (absent scales: offset of the
+ *   next section, size 0) and the total size; returns MOE_ERR_INVALID_ARG for a bad kind/shape.
+ * moe_pack_weights: fills `packed` from the reference layout (gate_w, up_w, down_w in `dtype`).
+ * moe_fused_packed: moe_fused / moe_fused_int8 / moe_fused_fp8 on the packed weights;
+ *   workspace: moe_fused_packed_workspace_bytes.
+ * ---------------------------------------------------------------------------------------- */
+MOE_API int moe_packed_weights_layout(int64_t num_experts, int64_t hidden, int64_t intermediate, int kind,
+                                      size_t offsets_out[4], size_t* total_bytes_out);
+
+MOE_API int moe_pack_weights(const void* gate_w, const void* up_w, const void* down_w, int dtype,
+                             int64_t num_experts, int64_t hidden, int64_t intermediate, int kind, void* packed,
+                             size_t packed_bytes, void* stream);
+
+MOE_API size_t moe_fused_packed_workspace_bytes(int64_t num_tokens, int64_t topk, int64_t num_experts,
+                                                int64_t hidden, int64_t intermediate, int kind, int dtype);
+
+MOE_API int moe_fused_packed(const void* hidden_states, const void* packed, int kind, const void* topk_ids,
+                             int ids_dtype, const void* topk_weights, int weights_dtype, void* out,
+                             int64_t num_tokens, int64_t hidden, int64_t intermediate, int64_t num_experts,
+                             int64_t topk, int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
  * Expert-parallel building blocks (no reference counterpart: the reference runs on one GPU;

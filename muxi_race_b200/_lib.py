@@ -12,7 +12,7 @@ import threading
 from .build import LIB_PATH
 
 # enums mirrored from include/moe_b200.h
-MOE_F16, MOE_BF16, MOE_F32, MOE_I32, MOE_I64, MOE_I8 = range(6)
+MOE_F16, MOE_BF16, MOE_F32, MOE_I32, MOE_I64, MOE_I8, MOE_F8E4M3 = range(7)
 MOE_OK = 0
 STATUS_NAMES = {
     -1: "MOE_ERR_INVALID_ARG",
@@ -83,6 +83,14 @@ SIGNATURES = {
     "moe_fused_fp8": (
         _int,
         [_c_void_p] * 6 + [_int, _c_void_p, _int, _c_void_p] + [_i64] * 5 + [_int, _c_void_p, _size, _c_void_p],
+    ),
+    "moe_packed_weights_layout": (_int, [_i64, _i64, _i64, _int, ctypes.POINTER(_size), ctypes.POINTER(_size)]),
+    "moe_pack_weights": (_int, [_c_void_p] * 3 + [_int, _i64, _i64, _i64, _int, _c_void_p, _size, _c_void_p]),
+    "moe_fused_packed_workspace_bytes": (_size, [_i64] * 5 + [_int, _int]),
+    "moe_fused_packed": (
+        _int,
+        [_c_void_p, _c_void_p, _int, _c_void_p, _int, _c_void_p, _int, _c_void_p] + [_i64] * 5
+        + [_int, _c_void_p, _size, _c_void_p],
     ),
     "moe_ep_plan_workspace_bytes": (_size, [_i64, _i64]),
     "moe_ep_plan": (_int, [_c_void_p, _int, _i64, _i64, _c_void_p, _i64, _i64] + [_c_void_p] * 5 + [_c_void_p, _size, _c_void_p]),

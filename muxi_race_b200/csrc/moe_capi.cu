@@ -1421,6 +1421,102 @@ int moe_fused_fp8(const void* x, const void* w13_q, const float* w13_scale, cons
                       dtype, workspace, workspace_bytes, stream, nullptr, nullptr, false, true);
 }
 
+// ---------------------------------------------------------------------------- packed weights
+// One buffer per expert set: w13 [E, 2I, H], w13 scales, w2 [E, H, I], w2 scales, each section
+// 256-byte aligned (include/moe_b200.h gives the contract).
+static bool packed_q8(int kind) { return kind == MOE_I8 || kind == MOE_F8E4M3; }
+
+int moe_packed_weights_layout(int64_t E, int64_t H, int64_t I, int kind, size_t offsets[4], size_t* total_bytes) {
+  t_last_error.clear();
+  if (kind != MOE_F16 && kind != MOE_BF16 && !packed_q8(kind))
+    return fail(MOE_ERR_INVALID_ARG, "kind must be MOE_F16, MOE_BF16, MOE_I8 or MOE_F8E4M3");
+  if (E < 1 || E > kAlignMaxExperts || H < 1 || I < 1 || H > (1 << 30) || I > (1 << 30))
+    return fail(MOE_ERR_INVALID_ARG, "bad packed weight shape");
+  const bool q = packed_q8(kind);
+  const size_t elt = q ? 1 : 2;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t r = o;
+    o = round_up(o + bytes, 256);
+    return r;
+  };
+  size_t off[4];
+  off[0] = take(static_cast<size_t>(E) * 2 * I * H * elt);
+  off[1] = take(q ? sizeof(float) * E * 2 * I : 0);
+  off[2] = take(static_cast<size_t>(E) * H * I * elt);
+  off[3] = take(q ? sizeof(float) * E * H : 0);
+  if (offsets)
+    for (int i = 0; i < 4; ++i) offsets[i] = off[i];
+  if (total_bytes) *total_bytes = o;
+  return MOE_OK;
+}
+
+int moe_pack_weights(const void* gate_w, const void* up_w, const void* down_w, int dtype, int64_t E, int64_t H,
+                     int64_t I, int kind, void* packed, size_t packed_bytes, void* stream) {
+  size_t off[4], total;
+  MOE_TRY(moe_packed_weights_layout(E, H, I, kind, off, &total));
+  const bool q = packed_q8(kind);
+  MOE_TRY(check_common(H, I, E, dtype, q ? 16 : 8));
+  if (!q && kind != dtype) return fail(MOE_ERR_INVALID_ARG, "16-bit packing keeps the weights' dtype");
+  if (!gate_w || !up_w || !down_w || !packed) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  if (packed_bytes < total) return fail(MOE_ERR_INVALID_ARG, "packed must hold %zu bytes", total);
+  if (!aligned16(gate_w) || !aligned16(up_w) || !aligned16(down_w) || reinterpret_cast<uintptr_t>(packed) % 256 != 0)
+    return fail(MOE_ERR_ALIGNMENT, "weights must be 16-byte and packed 256-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* P = static_cast<uint8_t*>(packed);
+  const uint8_t* g = static_cast<const uint8_t*>(gate_w);
+  const uint8_t* u = static_cast<const uint8_t*>(up_w);
+  const size_t half_bytes = static_cast<size_t>(I) * H * 2;  // one expert's gate (or up) rows, 16-bit
+  if (!q) {
+    for (int64_t e = 0; e < E; ++e) {
+      MOE_CUDA(cudaMemcpyAsync(P + off[0] + 2 * e * half_bytes, g + e * half_bytes, half_bytes,
+                               cudaMemcpyDeviceToDevice, s));
+      MOE_CUDA(cudaMemcpyAsync(P + off[0] + (2 * e + 1) * half_bytes, u + e * half_bytes, half_bytes,
+                               cudaMemcpyDeviceToDevice, s));
+    }
+    MOE_CUDA(cudaMemcpyAsync(P + off[2], down_w, static_cast<size_t>(E) * H * I * 2, cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+  }
+  // per-row quantisation straight into the packed rows: expert e's gate rows land at rows
+  // e * 2I .. e * 2I + I - 1 of w13, its up rows right after
+  const bool fp8 = kind == MOE_F8E4M3;
+  float* s13 = reinterpret_cast<float*>(P + off[1]);
+  for (int64_t e = 0; e < E; ++e) {
+    MOE_TRY(quantize_rows(fp8, g + e * half_bytes, dtype, I, H, P + off[0] + static_cast<size_t>(2 * e) * I * H,
+                          s13 + 2 * e * I, stream));
+    MOE_TRY(quantize_rows(fp8, u + e * half_bytes, dtype, I, H, P + off[0] + static_cast<size_t>(2 * e + 1) * I * H,
+                          s13 + (2 * e + 1) * I, stream));
+  }
+  return quantize_rows(fp8, down_w, dtype, E * H, I, P + off[2], reinterpret_cast<float*>(P + off[3]), stream);
+}
+
+size_t moe_fused_packed_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int kind,
+                                        int dtype) {
+  if (kind == MOE_I8) return moe_fused_int8_workspace_bytes(T, topk, E, H, I, dtype);
+  if (kind == MOE_F8E4M3) return moe_fused_fp8_workspace_bytes(T, topk, E, H, I, dtype);
+  return moe_fused_workspace_bytes(T, topk, E, H, I, dtype);
+}
+
+int moe_fused_packed(const void* x, const void* packed, int kind, const void* ids, int ids_dtype, const void* tw,
+                     int w_dtype, void* out, int64_t T, int64_t H, int64_t I, int64_t E, int64_t topk, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  size_t off[4], total;
+  MOE_TRY(moe_packed_weights_layout(E, H, I, kind, off, &total));
+  if (!packed) return fail(MOE_ERR_INVALID_ARG, "null packed weights");
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const float* s13 = reinterpret_cast<const float*>(P + off[1]);
+  const float* s2 = reinterpret_cast<const float*>(P + off[3]);
+  if (kind == MOE_I8)
+    return moe_fused_int8(x, P + off[0], s13, P + off[2], s2, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
+                          dtype, workspace, workspace_bytes, stream);
+  if (kind == MOE_F8E4M3)
+    return moe_fused_fp8(x, P + off[0], s13, P + off[2], s2, ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk,
+                         dtype, workspace, workspace_bytes, stream);
+  if (kind != dtype) return fail(MOE_ERR_INVALID_ARG, "16-bit packed weights must have the activation dtype");
+  return moe_fused(x, P + off[0], P + off[2], ids, ids_dtype, tw, w_dtype, out, T, H, I, E, topk, dtype, workspace,
+                   workspace_bytes, stream);
+}
+
 // ---------------------------------------------------------------------------- expert parallel
 size_t moe_ep_plan_workspace_bytes(int64_t T, int64_t W) {
   if (T <= 0 || W <= 0) return 256;
