@@ -1,0 +1,55 @@
+"""GPU: ``run_kernel`` on the reference harness's remaining judge-style shapes
+(初审材料/源代码/benchmark/remote_bench.py:20-28): case 1 (16 experts, H=2048, I=8192), case 4
+(one expert, 24 full blocks, I=8192), case 5 (one expert, a single partial block, I=8192) and
+case 6 (one expert, 24 full blocks, I=128); cases 0, 2 and 3 are in test_run_kernel_gpu.py.
+fp32 torch reference on the GPU; tolerance |out - ref| <= 1e-2 + 1e-2 * |ref|, pad rows zero.
+
+The file name sorts after the other GPU test files, so a run that stops at the first failure has
+run them all.
+"""
+import math
+
+import pytest
+import torch
+
+import cases
+from muxi_race_b200 import device_status, run_kernel
+from oracle.moe_ref import run_kernel_ref_f32
+
+pytestmark = pytest.mark.gpu
+RTOL = ATOL = 1e-2
+
+CASES = {
+    1: dict(experts=16, hidden=2048, intermediate=8192, valid=2272, high_experts=8, low_size=124),
+    4: dict(experts=1, hidden=2048, intermediate=8192, valid=3072, high_experts=1, low_size=0),
+    5: dict(experts=1, hidden=2048, intermediate=8192, valid=127, high_experts=0, low_size=127),
+    6: dict(experts=1, hidden=2048, intermediate=128, valid=3072, high_experts=1, low_size=0),
+}
+
+
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_run_kernel_remote_bench_case(cuda_device, case):
+    c = CASES[case]
+    dev = cuda_device
+    gs = cases.make_group_sizes(c)
+    assert int(gs.sum()) == c["valid"]
+    go, gpo, gidx = cases.metadata(gs)
+    P, E, H, I = int(gpo[-1]), c["experts"], c["hidden"], c["intermediate"]
+    g = torch.Generator(device=dev).manual_seed(100 + case)
+    x = torch.randn((P, H), generator=g, device=dev).half()
+    gate = (torch.randn((E, I, H), generator=g, device=dev) / math.sqrt(H)).half()
+    up = (torch.randn((E, I, H), generator=g, device=dev) / math.sqrt(H)).half()
+    down = (torch.randn((E, H, I), generator=g, device=dev) / math.sqrt(I)).half()
+    routed = torch.rand((c["valid"],), generator=g, device=dev)
+    meta = [t.to(dev) for t in (gs, go, gpo, gidx)]
+    out = torch.full((P, H), float("nan"), dtype=torch.float16, device=dev)
+    run_kernel(x, gate, up, down, routed, *meta, out)
+    ref = run_kernel_ref_f32(x, gate, up, down, routed, *meta)
+    torch.cuda.synchronize()
+    assert device_status() == 0
+    o, r = out.float().cpu(), ref.float().cpu()
+    bad = (o - r).abs() > ATOL + RTOL * r.abs()
+    assert int(bad.sum()) == 0, f"case {case}: {int(bad.sum())} elements outside tolerance"
+    gsl, gpol = gs.tolist(), gpo.tolist()
+    for e, n in enumerate(gsl):
+        assert torch.count_nonzero(o[gpol[e] + n:gpol[e + 1]]) == 0, f"pad rows of expert {e} not zero"
