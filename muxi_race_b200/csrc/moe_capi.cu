@@ -287,7 +287,8 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
     {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
     {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8}, {"tn", 256, 1, 6, 4, 1, 1, 0, 4, 1},
 };
-static_assert(kNumTileCfg * 36 <= 64 * 16, "smem attribute bits");
+// raise_smem bits: ((mode 0..2 x bf16 x operand kind 0..2) x tile x A path), 54 per tile
+static_assert(kNumTileCfg * 54 <= 64 * 16, "smem attribute bits");
 
 // Defaults, measured on B200. Stage1: 256a4b5e8 (single CTA, 8 epilogue warps: the SiLU*up
 // epilogue no longer holds up the next unit; cfg2 Stage1 0.52 vs 0.60-0.73 ms). Stage2, chosen per
@@ -389,7 +390,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
   if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3 + AMODE;
+  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 3 + AMODE;
   constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma, KPB>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
@@ -415,7 +416,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = 1;
   args_l.gu_swap = 0;
   args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2 + (I8 ? 1 : 0)) * kNumTileCfg + tcfg) * 3;
+  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 3;
   constexpr int smem = PairRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   static int max_pairs[kMaxDevices] = {};
@@ -471,7 +472,7 @@ template <int MODE, typename OutT>
 int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t stream) {
   constexpr int AST = 6, BST = 4;
   auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST>;
-  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 2) * kNumTileCfg * 3 + tcfg * 3 + 2;
+  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3) * kNumTileCfg * 3 + tcfg * 3 + 2;
   constexpr int smem = TnRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
