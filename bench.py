@@ -280,31 +280,71 @@ def bench_ours(args, world, rank, local):
     else:
         stages["stage2"] = stage_ms(3, 4)
 
-    # ---- end to end through the public API with host buffers
+    # ---- end to end through the public API with host buffers: every step uploads its inputs
+    #      from pinned host memory and downloads its result; by default through HostPipeline
+    #      (copies of consecutive calls overlapped with compute on two copy streams), with the
+    #      serial copy -> call -> copy loop as the fallback and with --e2e serial
     hosts = [t.cpu().pin_memory() for t in [x] + ins]
-    devs = [torch.empty_like(t) for t in [x] + ins]
     out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
 
-    def e2e_step():
-        for d, h in zip(devs, hosts):
-            d.copy_(h, non_blocking=True)
-        fn(*devs, out)
-        out_h.copy_(out, non_blocking=True)
+    def e2e_serial():
+        devs = [torch.empty_like(t) for t in [x] + ins]
 
-    torch.cuda.synchronize()
-    barrier(world)  # the ranks enter the end-to-end phase together
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e2.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+        def step():
+            for d, h in zip(devs, hosts):
+                d.copy_(h, non_blocking=True)
+            fn(*devs, out)
+            out_h.copy_(out, non_blocking=True)
+
+        torch.cuda.synchronize()
+        barrier(world)  # the ranks enter the end-to-end phase together
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(args.steps):
+            step()
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return s2.elapsed_time(e2) / args.steps
+
+    def e2e_overlapped():
+        from muxi_race_b200.host_pipeline import HostPipeline
+
+        pipe = HostPipeline(fn, [x] + ins, out)
+        torch.cuda.synchronize()
+        barrier(world)
+        for _ in range(args.warmup):
+            pipe.submit(hosts, out_h)
+        pipe.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        pipe.up.wait_event(s2)  # the first upload starts inside the timed region
+        for _ in range(args.steps):
+            pipe.submit(hosts, out_h)
+        pipe.join(stream)  # the last download ends inside it
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return s2.elapsed_time(e2) / args.steps
+
+    e2e_mode = "serial (copy, call, copy on one stream)"
+    if args.e2e == "overlapped":
+        try:
+            e2e_local = e2e_overlapped()
+            e2e_mode = "overlapped (HostPipeline: uploads and downloads of consecutive calls on two copy streams)"
+        except Exception as ex:  # noqa: BLE001 - fall back to the serial measurement, and say so
+            torch.cuda.synchronize()
+            e2e_mode = f"serial after HostPipeline failed ({type(ex).__name__}: {ex})"
+            e2e_local = e2e_serial()
+    else:
+        e2e_local = e2e_serial()
+    e2e_ms = max_over_ranks(e2e_local, world)
     clock_info = clocks.stop()  # sampled across both timed regions
     h2d = sum(h.numel() * h.element_size() for h in hosts)
     d2h = out_h.numel() * out_h.element_size()
@@ -358,7 +398,7 @@ def bench_ours(args, world, rank, local):
                           "tensor_peak_frac_measured": round(flops / (ms * 1e-3) / (peaks["bf16_tflops"] * 1e12), 4)},
         "roofline": roofline,
         "e2e": {"value": round(world * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "transfers": e2e_mode},
         # per call: alignment (count or router, scan, scatter), block groups, gather, Stage1, Stage2;
         # 8-bit routes add the intermediate requantisation, the ordered combine its two kernels
         "gpu_launches": args.steps * (8 if q8 else 9 if variant == "ordered" else 7),
@@ -677,6 +717,8 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
                     help="run_kernel: the reference drop-in on the reference's contest case --case")
     ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))
+    ap.add_argument("--e2e", default="overlapped", choices=["overlapped", "serial"],
+                    help="end-to-end leg: host transfers overlapped across calls (HostPipeline) or serial")
     ap.add_argument("--variant", default="default", choices=["default", "ordered", "router", "fp8"],
                     help="single-GPU fused call: ordered (deterministic) combine, routing from router logits "
                          "on the device, or the fp8 route")

@@ -143,3 +143,12 @@ def test_peer_memory_ep_host_checks():
                                 0, None)
     assert rc == -1 and b"regions" in lib.moe_last_error()
     assert lib.moe_ep_region_alloc(0, None) == -1
+
+
+def test_host_pipeline_needs_cuda_tensors():
+    from muxi_race_b200.host_pipeline import HostPipeline
+
+    with pytest.raises(ValueError, match="CUDA"):
+        HostPipeline(lambda *a: None, [torch.zeros(4)], torch.zeros(4))
+    with pytest.raises(ValueError, match="depth"):
+        HostPipeline(lambda *a: None, [torch.zeros(4)], torch.zeros(4), depth=0)
