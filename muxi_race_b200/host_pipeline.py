@@ -14,7 +14,8 @@ kernels (PCIe / C2C copies in each direction run beside HBM-bound compute).
 
 Ordering per buffer slot: upload waits until the slot's previous call has consumed its inputs;
 compute waits for its upload and for the slot's previous download; download waits for compute.
-All waits are stream-event waits: nothing blocks the host except ``synchronize``.
+All waits are stream-event waits: nothing blocks the host except ``synchronize``. The caller keeps
+each submitted host tensor unchanged (inputs) and unread (output) until ``synchronize`` returns.
 """
 from __future__ import annotations
 
