@@ -8,6 +8,8 @@ Entry points:
   moe_align(...)       device-side routing metadata
   fused_topk(...)      softmax top-k routing of router logits; fused_moe_router(...) routes + runs
   pack_weights(...)    one-buffer weight format (16-bit, int8 or fp8); fused_moe_packed(...) runs on it
+  host_pipeline.HostPipeline  host-buffer calls with transfers overlapped across calls
+  graphs.GraphedMoE    one call captured into a CUDA graph and replayed
   ep.ExpertParallelMoE expert-parallel fused MoE over torch.distributed (NCCL all-to-all)
 
 All compute runs in hand-written CUDA kernels of ``libmoe_b200.so`` (C ABI in
