@@ -10,6 +10,8 @@ Entry points:
   pack_weights(...)    one-buffer weight format (16-bit, int8 or fp8); fused_moe_packed(...) runs on it
   host_pipeline.HostPipeline  host-buffer calls with transfers overlapped across calls
   graphs.GraphedMoE    one call captured into a CUDA graph and replayed
+  torch_ops            torch.ops.muxi_race_b200.{fused_moe, fused_moe_int8, fused_moe_fp8, fused_topk,
+                       run_kernel} (import to register)
   ep.ExpertParallelMoE expert-parallel fused MoE over torch.distributed (NCCL all-to-all)
 
 All compute runs in hand-written CUDA kernels of ``libmoe_b200.so`` (C ABI in
