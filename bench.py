@@ -663,6 +663,63 @@ def bench_run_kernel(args):
     }), flush=True)
 
 
+def bench_sweep(args):
+    """Tile sweep (tuning, one GPU): for each configuration name in --sweep, force it for the
+    stage(s) given by --sweep-stage and time the fused call on --config with stage-boundary events;
+    each output is compared with the automatic choice's output (max |diff|, relative L2) and the
+    device status word is checked. One JSON line per configuration, then a summary line."""
+    import muxi_race_b200 as m
+    from muxi_race_b200 import _lib
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
+
+    dev = torch.device("cuda", 0)
+    cfg = CONFIGS[args.config]
+    w13, w2 = make_weights(cfg, seed=0, device=dev)
+    x = make_hidden(cfg, seed=1, device=dev)
+    ids, tw = make_routing(cfg, seed=2, device=dev)
+    ref = m.fused_moe(x, w13, w2, ids, tw)
+    torch.cuda.synchronize()
+    assert m.device_status() == 0
+    stream = torch.cuda.current_stream(dev)
+    rows = []
+    for name in [t for t in args.sweep.split(",") if t]:
+        rec = {"tile": name, "stage": args.sweep_stage, "config": cfg.name}
+        try:
+            _lib.set_tile(args.sweep_stage, name)
+            out = torch.empty_like(ref)
+            for _ in range(args.warmup):
+                m.fused_moe(x, w13, w2, ids, tw, out=out)
+            torch.cuda.synchronize()
+            st = m.device_status()
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+            for row in evs:
+                for e in row:
+                    e.record(stream)
+            torch.cuda.synchronize()
+            for k in range(args.steps):
+                _lib.set_profile_events(evs[k])
+                m.fused_moe(x, w13, w2, ids, tw, out=out)
+            _lib.set_profile_events(None)
+            torch.cuda.synchronize()
+            st |= m.device_status()
+            ms = lambda a, b: sum(r[a].elapsed_time(r[b]) for r in evs) / args.steps  # noqa: E731
+            d = (out.float() - ref.float())
+            rec.update({"status": st, "ms_call": round(ms(0, 4), 4), "ms_stage1": round(ms(2, 3), 4),
+                        "ms_stage2": round(ms(3, 4), 4), "max_abs_diff": float(d.abs().max()),
+                        "rel_l2": float(d.norm() / ref.float().norm())})
+        except Exception as ex:  # noqa: BLE001 - report and go on with the next configuration
+            rec["error"] = f"{type(ex).__name__}: {ex}"
+        finally:
+            _lib.set_profile_events(None)
+            _lib.set_tile(0, None)
+        rows.append(rec)
+        print(json.dumps(rec), flush=True)
+    ok = [r for r in rows if r.get("status") == 0 and r.get("rel_l2", 1.0) < 1e-2]
+    best = min(ok, key=lambda r: r["ms_call"]) if ok else None
+    print(json.dumps({"sweep": cfg.name, "stage": args.sweep_stage, "best": best and best["tile"],
+                      "best_ms_call": best and best["ms_call"], "n": len(rows), "passed": len(ok)}), flush=True)
+
+
 # ----------------------------------------------------------------------------- reference arm
 def bench_reference(args, world, rank):
     """The reference's CPU operator (oracle port of its PyTorch implementation) on the host cores."""
@@ -717,6 +774,10 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
                     help="run_kernel: the reference drop-in on the reference's contest case --case")
     ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))
+    ap.add_argument("--sweep", default="",
+                    help="tuning: comma-separated tile names to time one by one (prints one line each)")
+    ap.add_argument("--sweep-stage", type=int, default=1, choices=[0, 1, 2],
+                    help="stage the swept tile is forced for (0 = both)")
     ap.add_argument("--e2e", default="overlapped", choices=["overlapped", "serial"],
                     help="end-to-end leg: host transfers overlapped across calls (HostPipeline) or serial")
     ap.add_argument("--variant", default="default", choices=["default", "ordered", "router", "fp8"],
@@ -724,6 +785,9 @@ def main():
                          "on the device, or the fp8 route")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.sweep:
+        bench_sweep(args)
+        return
     if args.path == "run_kernel":
         bench_run_kernel(args)
         return
