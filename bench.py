@@ -440,7 +440,7 @@ def bench_ep(args, world, rank, local):
     ids, tw = make_routing(cfg, seed=2 + rank, device=dev, T=T_rank)
     p2p = args.ep_mode == "p2p"
     if p2p:
-        moe = PeerMemoryEP(w13, w2, placement, max_tokens=T_rank, topk=cfg.topk)
+        moe = PeerMemoryEP(w13, w2, placement, max_tokens=T_rank, topk=cfg.topk, combine=args.ep_combine)
     else:
         moe = ExpertParallelMoE(w13, w2, placement, chunks=args.ep_chunks)
     n_chunks = 1 if p2p else args.ep_chunks
@@ -570,8 +570,10 @@ def bench_ep(args, world, rank, local):
                                    f"top-{cfg.topk}, {T_rank} tokens per rank, {T_rank * world} in total",
                        "tokens_per_rank": T_rank, "parallelism": f"ep{world}", "experts_per_rank": len(mine),
                        "placement": "balanced (greedy LPT from an 8192-token calibration sample)",
-                       "ep_exchange": ("peer memory: NVLink loads of the token rows and partial outputs "
-                                       "inside the library's kernels, flag barriers; no collectives library")
+                       "ep_exchange": ("peer memory: NVLink loads of the token rows and "
+                                       + ("Stage2 adding into the home ranks' regions (push combine)"
+                                          if args.ep_combine == "push" else "loads of the partial outputs")
+                                       + " inside the library's kernels, flag barriers; no collectives library")
                        if p2p else f"NCCL all_to_all_single, {n_chunks} chunk(s)",
                        "l2": "inputs larger than L2 (expert weights streamed per step)"},
             "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
@@ -584,7 +586,7 @@ def bench_ep(args, world, rank, local):
             # per chunk: plan 4 (pair keys + 3 alignment), pack 1, local MoE 7 (3 alignment, block
             # groups, gather, Stage1, Stage2), combine 1
             # p2p: stage, 2 barriers, route, local MoE 7, combine = 12
-            "gpu_launches": args.steps * (12 if p2p else 13 * n_chunks),
+            "gpu_launches": args.steps * ((11 if args.ep_combine == "push" else 12) if p2p else 13 * n_chunks),
             "clocks": clock_info,
         }), flush=True)
 
@@ -769,6 +771,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-mode", default="nccl", choices=["p2p", "nccl"],
                     help="expert parallelism: NCCL all-to-all exchange, or over peer memory in the library's kernels")
+    ap.add_argument("--ep-combine", default="pull", choices=["pull", "push"],
+                    help="peer-memory mode: pull the owners' partial rows after the second barrier, or push them "
+                         "from Stage2's epilogue into the home ranks' regions")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallelism: token chunks whose exchanges overlap the local MoE of the others")
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],

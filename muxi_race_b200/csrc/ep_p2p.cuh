@@ -16,8 +16,15 @@
 // gather those token rows from the peers' x, run the grouped GEMMs, Stage2 combining into its own
 // y -> barrier -> out[t] = sum over the owners o of token t's experts of y_o[s * T_max + t], read
 // from the owners' regions in ascending rank order (deterministic given the partials).
-// Peer data is read with L2-only loads (ld.global.cg); nothing but the barrier flags is written
-// to peer memory, and no load uses a tensor map or cluster multicast.
+// Peer data is read with L2-only loads (ld.global.cg); in this (pull) mode nothing but the barrier
+// flags is written to peer memory, and no load uses a tensor map or cluster multicast.
+//
+// Push combine (moe_ep_p2p_compute_push): the home rank s zeroes its y rows [0, T) before the
+// first barrier; Stage2's epilogue on every owner adds each route's weighted row straight into
+// row t of the home rank's y (vector red.add to peer memory, tile by tile, overlapping the GEMM);
+// each epilogue thread fences at system scope before its kernel ends; after the second barrier the
+// home rank's y rows [0, T) are its output (copied out by moe_ep_p2p_push_finish). The pull kernel
+// and its NVLink reads after the second barrier disappear; the sum order is that of the atomics.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -139,19 +146,20 @@ __global__ void ep_p2p_route_kernel(const uint64_t* __restrict__ regions, EpRegi
   }
 }
 
-// xs[route_slot[r]] = x row of token (s, t) of route r, read from rank s's region; and zero
-// this rank's y rows of every token with at least one local route (the Stage2 combine target).
-// One warp per work item, 16-byte vectors.
+// xs[route_slot[r]] = x row of token (s, t) of route r, read from rank s's region; and, with
+// zero_served (pull combine), zero this rank's y rows of every token with at least one local route
+// (the Stage2 combine target). One warp per work item, 16-byte vectors.
 template <typename T>
 __global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int T_max,
                                         int topk, int W, const int32_t* __restrict__ route_slot,
-                                        const int32_t* __restrict__ local_ids, int H, T* __restrict__ xs) {
+                                        const int32_t* __restrict__ local_ids, int H, T* __restrict__ xs,
+                                        int zero_served) {
   const int lane = threadIdx.x & 31;
   const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
   const int vecs = H / 8;
   const long long R = static_cast<long long>(W) * T_max * topk;
-  const long long rows = static_cast<long long>(W) * T_max;
+  const long long rows = zero_served ? static_cast<long long>(W) * T_max : 0;
   uint4* y = reinterpret_cast<uint4*>(regions[rank] + static_cast<uint64_t>(L.y));
   for (long long item = warp_id; item < R + rows; item += n_warps) {
     if (item < R) {
@@ -187,7 +195,8 @@ __global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, Ep
 // Bulk-copy variant of gather_rows_peer_kernel (selected with MOE_B200_EP_GATHER=bulk): lane 0
 // of each warp moves whole token rows with the bulk-copy engine, peer row -> shared memory
 // (cp.async.bulk with an mbarrier) -> xs (cp.async.bulk store), two rows in flight per warp. Then
-// all threads zero the served partial rows as in gather_rows_peer_kernel. Dynamic shared memory:
+// all threads zero the served partial rows as in gather_rows_peer_kernel (with zero_served). Dynamic
+// shared memory:
 // kEpBulkWarps * 2 rows of H * 2 bytes, plus the mbarriers.
 constexpr int kEpBulkWarps = 4;
 __device__ __forceinline__ void bulk_load_row(uint32_t dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -208,7 +217,7 @@ template <typename T>
 __global__ void __launch_bounds__(kEpBulkWarps * 32)
     gather_rows_peer_bulk_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int T_max, int topk,
                                  int W, const int32_t* __restrict__ route_slot, const int32_t* __restrict__ local_ids,
-                                 int H, T* __restrict__ xs, uint32_t* status) {
+                                 int H, T* __restrict__ xs, uint32_t* status, int zero_served) {
   extern __shared__ __align__(128) uint8_t ep_smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t row_bytes = static_cast<uint32_t>(H) * 2u;
@@ -273,7 +282,7 @@ __global__ void __launch_bounds__(kEpBulkWarps * 32)
   __syncwarp();
   // zero this rank's partial rows of every token with at least one local route
   const int vecs = H / 8;
-  const long long rows = static_cast<long long>(W) * T_max;
+  const long long rows = zero_served ? static_cast<long long>(W) * T_max : 0;
   uint4* y = reinterpret_cast<uint4*>(regions[rank] + static_cast<uint64_t>(L.y));
   for (long long tok = gw; tok < rows; tok += nw) {
     bool served = false;

@@ -978,6 +978,7 @@ struct PeerSource {
   const uint64_t* regions;
   EpRegion L;
   int rank, W, T_max;
+  bool push;  // Stage2 adds into the home ranks' y rows instead of this rank's partial block
 };
 
 // Routing from router logits: the router kernel writes `ids` / `tw` (the fused call's topk_ids /
@@ -1042,6 +1043,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   const double bpe = static_cast<double>(R) / (peer ? peer->W : 1) / static_cast<double>(E) / kBM + 0.5;
   const TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe), tc2 = usable_cfg(2, I, elt, lsu, bpe);
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
+  if (peer && peer->push && t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no push combine");
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
 
   // 1. routing metadata
@@ -1085,29 +1087,31 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
              (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps <= kEpBulkMaxSmem) {
     // bulk-copy gather: whole rows through shared memory, one CTA of 4 warps per SM
     const size_t smem = (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps;
+    const int zero_served = peer->push ? 0 : 1;
     if (dtype == MOE_F16) {
       MOE_CUDA(cudaFuncSetAttribute(gather_rows_peer_bulk_kernel<__half>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       gather_rows_peer_bulk_kernel<__half><<<sms, kEpBulkWarps * 32, smem, s>>>(
           peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
-          static_cast<const int32_t*>(ids), (int)H, static_cast<__half*>(xs), status);
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__half*>(xs), status, zero_served);
     } else {
       MOE_CUDA(cudaFuncSetAttribute(gather_rows_peer_bulk_kernel<__nv_bfloat16>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       gather_rows_peer_bulk_kernel<__nv_bfloat16><<<sms, kEpBulkWarps * 32, smem, s>>>(
           peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
-          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs), status);
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs), status, zero_served);
     }
     MOE_CUDA(cudaGetLastError());
   } else if (peer) {  // token rows from the ranks' regions; zero the served partial rows
+    const int zero_served = peer->push ? 0 : 1;
     if (dtype == MOE_F16)
       gather_rows_peer_kernel<__half><<<gblocks, 256, 0, s>>>(peer->regions, peer->L, peer->rank, peer->T_max,
                                                               (int)topk, peer->W, slot, static_cast<const int32_t*>(ids),
-                                                              (int)H, static_cast<__half*>(xs));
+                                                              (int)H, static_cast<__half*>(xs), zero_served);
     else
       gather_rows_peer_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
           peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot,
-          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs));
+          static_cast<const int32_t*>(ids), (int)H, static_cast<__nv_bfloat16*>(xs), zero_served);
     MOE_CUDA(cudaGetLastError());
   } else if (dtype == MOE_F16) {
     if (fp8)
@@ -1216,6 +1220,11 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a2.status = status;
   a2.a_ptr = a2_src;
   a2.a_row_bytes = I * elt;
+  if (peer && peer->push) {  // push combine: Stage2 adds into the home ranks' y rows
+    a2.out_regions = peer->regions;
+    a2.out_region_off = peer->L.y;
+    a2.out_T_max = peer->T_max;
+  }
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
   if (!int8) {
@@ -1720,11 +1729,10 @@ size_t moe_ep_p2p_workspace_bytes(int64_t T_max, int64_t topk, int64_t W, int64_
   return fused_layout(W * T_max, topk, E_local, H, I, false, false).total + ep_p2p_extra_bytes(T_max, topk, W);
 }
 
-int moe_ep_p2p_compute(const uint64_t* regions, void* own_region, int rank, int W, int64_t T_max, int64_t H, int64_t I,
-                       int64_t topk,
-                       const int32_t* expert_rank, const int32_t* expert_local, int64_t E, const void* w13,
-                       const void* w2, int64_t E_local, int dtype, void* workspace, size_t workspace_bytes,
-                       void* stream) {
+static int ep_p2p_compute(bool push, const uint64_t* regions, void* own_region, int rank, int W, int64_t T_max,
+                          int64_t H, int64_t I, int64_t topk, const int32_t* expert_rank, const int32_t* expert_local,
+                          int64_t E, const void* w13, const void* w2, int64_t E_local, int dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
   t_last_error.clear();
   MOE_TRY(ep_p2p_check(T_max, H, topk, W));
   if (!regions || !own_region || rank < 0 || rank >= W || !expert_rank || !expert_local || E < 1 || E_local < 1)
@@ -1743,11 +1751,57 @@ int moe_ep_p2p_compute(const uint64_t* regions, void* own_region, int rank, int 
   ep_p2p_route_kernel<<<sms * 4, 256, 0, s>>>(regions, L, W, (int)T_max, (int)topk, expert_rank, expert_local, (int)E,
                                               rank, local_ids, local_w);
   MOE_CUDA(cudaGetLastError());
-  PeerSource peer{regions, L, rank, W, (int)T_max};
+  PeerSource peer{regions, L, rank, W, (int)T_max, push};
   void* y = static_cast<uint8_t*>(own_region) + L.y;
   return fused_common(false, own_region, w13, nullptr, w2, nullptr, local_ids, MOE_I32,
                       local_w, MOE_F32, y, W * T_max, H, I, E_local, topk, dtype, workspace,
                       need - ep_p2p_extra_bytes(T_max, topk, W), stream, &peer);
+}
+
+int moe_ep_p2p_compute(const uint64_t* regions, void* own_region, int rank, int W, int64_t T_max, int64_t H, int64_t I,
+                       int64_t topk, const int32_t* expert_rank, const int32_t* expert_local, int64_t E,
+                       const void* w13, const void* w2, int64_t E_local, int dtype, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return ep_p2p_compute(false, regions, own_region, rank, W, T_max, H, I, topk, expert_rank, expert_local, E, w13, w2,
+                        E_local, dtype, workspace, workspace_bytes, stream);
+}
+
+int moe_ep_p2p_compute_push(const uint64_t* regions, void* own_region, int rank, int W, int64_t T_max, int64_t H,
+                            int64_t I, int64_t topk, const int32_t* expert_rank, const int32_t* expert_local,
+                            int64_t E, const void* w13, const void* w2, int64_t E_local, int dtype, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  return ep_p2p_compute(true, regions, own_region, rank, W, T_max, H, I, topk, expert_rank, expert_local, E, w13, w2,
+                        E_local, dtype, workspace, workspace_bytes, stream);
+}
+
+// Push combine, home side: zero y rows [0, T) of this rank's region (before the first barrier),
+// and copy them out as the forward's output (after the second barrier).
+int moe_ep_p2p_push_prepare(void* own_region, int64_t T, int64_t T_max, int64_t H, int64_t topk, int W, int dtype,
+                            void* stream) {
+  t_last_error.clear();
+  MOE_TRY(ep_p2p_check(T_max, H, topk, W));
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
+  if (!own_region) return fail(MOE_ERR_INVALID_ARG, "null region");
+  if (T == 0) return MOE_OK;
+  const EpRegion L = ep_region_layout(T_max, H, topk, W);
+  MOE_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(own_region) + L.y, 0, static_cast<size_t>(T) * H * 2,
+                           static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
+}
+
+int moe_ep_p2p_push_finish(const void* own_region, int64_t T, int64_t T_max, int64_t H, int64_t topk, int W, int dtype,
+                           void* out, void* stream) {
+  t_last_error.clear();
+  MOE_TRY(ep_p2p_check(T_max, H, topk, W));
+  if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
+  if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
+  if (!own_region || !out) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (T == 0) return MOE_OK;
+  const EpRegion L = ep_region_layout(T_max, H, topk, W);
+  MOE_CUDA(cudaMemcpyAsync(out, static_cast<const uint8_t*>(own_region) + L.y, static_cast<size_t>(T) * H * 2,
+                           cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+  return MOE_OK;
 }
 
 int moe_ep_p2p_combine(const uint64_t* regions, int rank, int W, int64_t T, int64_t T_max, int64_t H, int64_t topk,

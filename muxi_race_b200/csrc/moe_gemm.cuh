@@ -109,6 +109,11 @@ struct GemmArgs {
   // Stage2 output: out [rows or tokens, ldo]
   void* out;
   int ldo;
+  // Stage2Comb into other GPUs' memory (expert parallelism, push combine): token row
+  // s * out_T_max + t is added into row t of (OutT*)(out_regions[s] + out_region_off); NULL: out
+  const uint64_t* out_regions;
+  long long out_region_off;
+  int out_T_max;
   // Stage2Pad: reference metadata and routed weights
   const int* group_sizes;
   const int* group_offsets;
@@ -321,7 +326,12 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     float sa = 1.0f;
     if (Q8) sa = args.a_scale[p];
     OutT* out = reinterpret_cast<OutT*>(args.out);
-    const size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
+    size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
+    if (MODE == kStage2Comb && args.out_regions != nullptr && valid) {  // the token's home rank
+      const int home = token / args.out_T_max;
+      out = reinterpret_cast<OutT*>(args.out_regions[home] + static_cast<uint64_t>(args.out_region_off));
+      orow = static_cast<size_t>(token - home * args.out_T_max);
+    }
 #pragma unroll 1
     for (int c = c_begin; c < c_end; c += 32) {
       const int col0 = n0 + c;
@@ -702,6 +712,9 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     }
   }
 
+  // push combine: this thread's reductions into peer memory are performed system-wide before
+  // the kernel ends (the flag barrier that follows publishes them to the home ranks)
+  if (MODE == kStage2Comb && args.out_regions != nullptr) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

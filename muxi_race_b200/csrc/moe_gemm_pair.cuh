@@ -263,6 +263,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
     }
   }
 
+  if (MODE == kStage2Comb && args.out_regions != nullptr) __threadfence_system();  // push combine
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its pair may still touch its shared memory or TMEM
   if (warp == 1) {

@@ -321,10 +321,18 @@ class PeerMemoryEP:
     ``max_tokens`` bounds the tokens per rank per forward; every rank must construct the module
     (collective: the IPC handles are exchanged through ``group``) and call ``forward`` the same
     number of times; ``close`` is collective too.
+
+    ``combine="push"``: instead of the pull after the second barrier, Stage2's epilogue adds each
+    route's weighted row straight into its token's home rank's region over NVLink (overlapping the
+    GEMM); the home zeroes those rows before the first barrier and copies them out after the
+    second. The summation order of a token's routes is then that of the atomics.
     """
 
     def __init__(self, w_gate_up_local: torch.Tensor, w_down_local: torch.Tensor, placement: ExpertPlacement,
-                 max_tokens: int, topk: int, group: Optional[dist.ProcessGroup] = None):
+                 max_tokens: int, topk: int, group: Optional[dist.ProcessGroup] = None, combine: str = "pull"):
+        if combine not in ("pull", "push"):
+            raise ValueError("combine must be 'pull' or 'push'")
+        self.push = combine == "push"
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -383,19 +391,26 @@ class PeerMemoryEP:
         if x.dtype != self.dtype:
             raise ValueError("hidden_states dtype must match the weights")
         stream = _stream(self.device)
+        dt = _DTYPES[self.dtype]
         _lib.call("moe_ep_p2p_stage", self._region, x.data_ptr(), ids.data_ptr(), _ID_DTYPES[ids.dtype], w.data_ptr(),
-                  _W_DTYPES[w.dtype], T, self.T_max, self.H, self.k, self.world, _DTYPES[self.dtype], stream)
+                  _W_DTYPES[w.dtype], T, self.T_max, self.H, self.k, self.world, dt, stream)
+        if self.push:
+            _lib.call("moe_ep_p2p_push_prepare", self._region, T, self.T_max, self.H, self.k, self.world, dt, stream)
         self._barrier(stream)
         ws = _workspace(("ep_p2p", self.device, self.T_max, self.k, self.world, self.E_local, stream), self._ws_bytes,
                         self.device)
-        _lib.call("moe_ep_p2p_compute", self.regions.data_ptr(), self._region, self.rank, self.world, self.T_max,
-                  self.H, self.I, self.k, self.expert_rank.data_ptr(), self.expert_local.data_ptr(), self.E,
-                  self.w13.data_ptr(), self.w2.data_ptr(), self.E_local, _DTYPES[self.dtype], ws.data_ptr(), ws.numel(),
-                  stream)
+        _lib.call("moe_ep_p2p_compute_push" if self.push else "moe_ep_p2p_compute", self.regions.data_ptr(),
+                  self._region, self.rank, self.world, self.T_max, self.H, self.I, self.k,
+                  self.expert_rank.data_ptr(), self.expert_local.data_ptr(), self.E, self.w13.data_ptr(),
+                  self.w2.data_ptr(), self.E_local, dt, ws.data_ptr(), ws.numel(), stream)
         self._barrier(stream)
         out = torch.empty((T, self.H), dtype=self.dtype, device=self.device)
-        _lib.call("moe_ep_p2p_combine", self.regions.data_ptr(), self.rank, self.world, T, self.T_max, self.H, self.k,
-                  self.expert_rank.data_ptr(), self.E, _DTYPES[self.dtype], out.data_ptr(), stream)
+        if self.push:
+            _lib.call("moe_ep_p2p_push_finish", self._region, T, self.T_max, self.H, self.k, self.world, dt,
+                      out.data_ptr(), stream)
+        else:
+            _lib.call("moe_ep_p2p_combine", self.regions.data_ptr(), self.rank, self.world, T, self.T_max, self.H,
+                      self.k, self.expert_rank.data_ptr(), self.E, dt, out.data_ptr(), stream)
         return out
 
     __call__ = forward

@@ -143,6 +143,14 @@ def test_peer_memory_ep_host_checks():
                                 0, None)
     assert rc == -1 and b"regions" in lib.moe_last_error()
     assert lib.moe_ep_region_alloc(0, None) == -1
+    # push combine entry points: the same checks, no device pointer touched
+    rc = lib.moe_ep_p2p_compute_push(None, None, 0, W, T, H, 2048, k, None, None, 256, None, None, 32, _lib.MOE_F16,
+                                     None, 0, None)
+    assert rc == -1 and b"regions" in lib.moe_last_error()
+    assert lib.moe_ep_p2p_push_prepare(None, T + 1, T, H, k, W, _lib.MOE_F16, None) == -1
+    assert lib.moe_ep_p2p_push_prepare(None, 0, T, H, k, W, _lib.MOE_F16, None) == -1  # null region
+    assert lib.moe_ep_p2p_push_finish(None, 4, T, H, k, W, _lib.MOE_F32, None, None) == -1
+    assert b"dtype" in lib.moe_last_error()
 
 
 def test_host_pipeline_needs_cuda_tensors():

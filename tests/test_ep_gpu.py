@@ -78,8 +78,9 @@ def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="n
         placement = ExpertPlacement.balanced(loads, world)
         mine = placement.local_experts(rank)
         sl = slice(rank * T_per_rank, (rank + 1) * T_per_rank)
-        if mode == "p2p":
-            moe = PeerMemoryEP(w13[mine].contiguous(), w2[mine].contiguous(), placement, max_tokens=T_per_rank, topk=k)
+        if mode in ("p2p", "p2p_push"):
+            moe = PeerMemoryEP(w13[mine].contiguous(), w2[mine].contiguous(), placement, max_tokens=T_per_rank, topk=k,
+                               combine="push" if mode == "p2p_push" else "pull")
         else:
             moe = ExpertParallelMoE(w13[mine].contiguous(), w2[mine].contiguous(), placement)
         out = moe(x[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous())
@@ -95,10 +96,10 @@ def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="n
         res["bad"] = int((err > 1e-2 + 1e-2 * ref.abs()).sum()) + int((err3 > 1e-2 + 1e-2 * ref3.abs()).sum())
         res["max_err"] = max(float(err.max()), float(err3.max()))
         res["repeat_max_diff"] = float((out2.float() - out.float()).abs().max())
-        res["counts"] = moe.last_counts if mode != "p2p" else None
+        res["counts"] = moe.last_counts if mode == "nccl" else None
         from muxi_race_b200 import device_status
         res["status"] = device_status()
-        if mode == "p2p":
+        if mode != "nccl":
             moe.close()
         dist.barrier()
         dist.destroy_process_group()
@@ -109,7 +110,7 @@ def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="n
         json.dump(res, f)
 
 
-@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p_push"])
 @pytest.mark.parametrize("skew", [0.0, 1.1])
 def test_ep_multi_gpu_matches_oracle(cuda_device, tmp_path, skew, mode):
     """NCCL all-to-all mode and peer-memory mode against the single-process oracle, including a
@@ -135,7 +136,7 @@ def test_ep_multi_gpu_matches_oracle(cuda_device, tmp_path, skew, mode):
         assert r["bad"] == 0, r
         assert r["repeat_max_diff"] < 2e-2, r
         assert r["status"] == 0, r
-    if mode == "p2p":
+    if mode != "nccl":
         return
     # what rank a sends to rank b, rank b receives from rank a
     for a in range(world):
