@@ -638,13 +638,18 @@ def bench_run_kernel(args):
     routed = torch.rand((c["valid"],), generator=g, device=dev)
     meta = [t.to(dev) for t in (gs, go, gpo, gidx)]
     out = torch.empty((P, H), dtype=torch.float16, device=dev)
+    call = lambda: m.run_kernel(x, gate, up, down, routed, *meta, out)  # noqa: E731
+    if args.graph:  # one CUDA-graph launch per call instead of the library's launches
+        from muxi_race_b200.graphs import GraphedMoE
+
+        call = GraphedMoE(lambda xx, rr, oo: m.run_kernel(xx, gate, up, down, rr, *meta, oo), x, routed, out).replay
     for _ in range(args.warmup):
-        m.run_kernel(x, gate, up, down, routed, *meta, out)
+        call()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        m.run_kernel(x, gate, up, down, routed, *meta, out)
+        call()
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
@@ -655,7 +660,8 @@ def bench_run_kernel(args):
         "metric": f"run_kernel ms/call, contest case {args.case}", "value": round(ms, 4), "unit": "ms",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": False,
         "config": {"workload": f"reference drop-in run_kernel, contest case {args.case}: E={E} H={H} I={I} "
-                               f"valid rows={c['valid']} padded rows={P}", "dtype": "fp16"},
+                               f"valid rows={c['valid']} padded rows={P}", "dtype": "fp16",
+                   "launch": "CUDA graph replay" if args.graph else "direct"},
         "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
         "roofline_ms": round(max(flops / (peaks['bf16_tflops'] * 1e12), (wbytes + 2 * P * H * 2) / (peaks["hbm_gbs"] * 1e9)) * 1e3, 4),
         "reference_c500": {"ms": c["c500_ms"], "contest_torch_ms": c["c500_torch_ms"],
@@ -779,6 +785,7 @@ def main():
     ap.add_argument("--path", default="fused", choices=["fused", "run_kernel"],
                     help="run_kernel: the reference drop-in on the reference's contest case --case")
     ap.add_argument("--case", type=int, default=3, choices=sorted(CONTEST))
+    ap.add_argument("--graph", action="store_true", help="--path run_kernel: replay the call as a CUDA graph")
     ap.add_argument("--sweep", default="",
                     help="tuning: comma-separated tile names to time one by one (prints one line each)")
     ap.add_argument("--sweep-stage", type=int, default=1, choices=[0, 1, 2],
