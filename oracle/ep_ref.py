@@ -126,3 +126,26 @@ def p2p_combine_ref(partials, all_ids, expert_rank, rank, T_max, dtype):
         m = (owners == o).any(dim=1)
         out[m] += partials[o][rank * T_max: rank * T_max + T][m].float()
     return out.to(dtype)
+
+
+def p2p_push_ref(all_x, all_ids, all_w, expert_rank, expert_local, T_max, w13_by_rank, w2_by_rank):
+    """Push combine: every owner o adds, for each virtual route (s, t, j) it owns, weight * expert(x)
+    into row t of home rank s's output (the destination map of the Stage2 epilogue in push mode:
+    virtual token s * T_max + t -> rank s, row t). Returns one [T_s, H] fp32 output per rank."""
+    W = len(all_x)
+    k = all_ids[0].shape[1]
+    H = all_x[0].shape[1]
+    outs = [torch.zeros((x.shape[0], H), dtype=torch.float32) for x in all_x]
+    for o in range(W):
+        local = p2p_local_routes_ref(all_ids, expert_rank, expert_local, o, T_max)
+        for r in torch.nonzero(local >= 0).flatten().tolist():
+            token = r // k                     # virtual token id s * T_max + t
+            home, t = token // T_max, token % T_max
+            j = r % k
+            x = all_x[home][t:t + 1]
+            e_local = int(local[r])
+            one = torch.zeros((1, 1), dtype=torch.int64)
+            w = all_w[home][t:t + 1, j:j + 1].float()
+            outs[home][t] += fused_moe_ref(x, w13_by_rank[o][e_local:e_local + 1], w2_by_rank[o][e_local:e_local + 1],
+                                           one, w)[0]
+    return outs

@@ -1,11 +1,12 @@
 """CPU: the peer-memory expert-parallel decomposition (virtual routes, per-owner partial blocks,
-pull-combine over the owners) reproduces the single-process oracle, with a different token count
+pull-combine over the owners; and the push combine's destination map) reproduces the
+single-process oracle, with a different token count
 on every simulated rank and a skewed placement. The CUDA kernels of the mode are checked against
 the oracle on GPUs (tests/test_ep_gpu.py); this pins the decomposition they implement."""
 import torch
 
 from muxi_race_b200.ep import ExpertPlacement
-from oracle.ep_ref import p2p_combine_ref, p2p_local_routes_ref, p2p_partials_ref
+from oracle.ep_ref import p2p_combine_ref, p2p_local_routes_ref, p2p_partials_ref, p2p_push_ref
 from oracle.moe_ref import fused_moe_ref
 
 
@@ -36,3 +37,10 @@ def test_p2p_decomposition_matches_oracle():
         out = p2p_combine_ref(partials, ids, placement.expert_rank, r, T_max, torch.float32)
         ref = fused_moe_ref(xs[r], w13, w2, ids[r], ws[r])
         torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+
+    # push combine: each owner adds its routes' rows straight into the home rank's output rows
+    pushed = p2p_push_ref(xs, ids, ws, placement.expert_rank, placement.expert_local, T_max,
+                          [w13[placement.local_experts(o)] for o in range(W)],
+                          [w2[placement.local_experts(o)] for o in range(W)])
+    for r in range(W):
+        torch.testing.assert_close(pushed[r], fused_moe_ref(xs[r], w13, w2, ids[r], ws[r]), rtol=1e-5, atol=1e-5)
