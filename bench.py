@@ -738,7 +738,7 @@ def bench_reference(args, world, rank):
     cfg = CONFIGS[args.config]
     x = make_hidden(cfg, device="cpu")
     ids, tw = make_routing(cfg, device="cpu")
-    budget = max(2.0, min(15.0, 150.0 / max(1, args.steps + args.warmup)))
+    budget = max(0.2, min(args.cpu_budget, 150.0 / max(1, args.steps + args.warmup)))
     for _ in range(args.warmup):
         cpu_sample(cfg, ids, tw, x, budget_s=budget)
     tot_f = tot_t = 0.0
@@ -773,7 +773,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="cfg3")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU work for cpu_baseline")
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of CPU work for cpu_baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep-mode", default="nccl", choices=["p2p", "nccl"],
                     help="expert parallelism: NCCL all-to-all exchange, or over peer memory in the library's kernels")
