@@ -215,6 +215,19 @@ MOE_API int moe_fused_ordered(const void* hidden_states, const void* w_gate_up, 
 MOE_API int moe_router_topk(const void* logits, int logits_dtype, int64_t num_tokens, int64_t num_experts,
                             int64_t topk, int renormalize, int32_t* topk_ids, float* topk_weights, void* stream);
 
+/* moe_router_grouped_topk: group-limited sigmoid routing (the DeepSeek-V3 router). s =
+ *   sigmoid(logits); selection scores c = s + bias (bias [E] fp32, or NULL); the experts form
+ *   n_group equal groups, each scored by the sum of its two largest c; the topk_group best groups
+ *   stay eligible; topk_ids = the topk largest c among their experts (descending; same total order
+ *   and tie rule as moe_router_topk); topk_weights = s at those ids, divided by their sum (+1e-20)
+ *   when renormalize != 0, times scale.
+ *   Requirements: 1 <= n_group <= 32, E % n_group == 0, 1 <= topk_group <= n_group,
+ *   1 <= topk <= min(32, topk_group * E / n_group). */
+MOE_API int moe_router_grouped_topk(const void* logits, int logits_dtype, const float* bias, int64_t num_tokens,
+                                    int64_t num_experts, int64_t n_group, int64_t topk_group, int64_t topk,
+                                    int renormalize, float scale, int32_t* topk_ids, float* topk_weights,
+                                    void* stream);
+
 MOE_API int moe_fused_router(const void* hidden_states, const void* w_gate_up, const void* w_down,
                              const void* logits, int logits_dtype, int renormalize, int32_t* topk_ids,
                              float* topk_weights, void* out, int64_t num_tokens, int64_t hidden,

@@ -75,6 +75,8 @@ SIGNATURES = {
         _int,
         [_c_void_p] * 4 + [_int, _c_void_p, _int, _c_void_p] + [_i64] * 5 + [_int, _c_void_p, _size, _c_void_p],
     ),
+    "moe_router_grouped_topk": (_int, [_c_void_p, _int, _c_void_p, _i64, _i64, _i64, _i64, _i64, _int,
+                                       ctypes.c_float, _c_void_p, _c_void_p, _c_void_p]),
     "moe_router_topk": (_int, [_c_void_p, _int, _i64, _i64, _i64, _int, _c_void_p, _c_void_p, _c_void_p]),
     "moe_fused_router": (
         _int,

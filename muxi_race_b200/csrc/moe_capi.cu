@@ -735,6 +735,32 @@ int launch_router(const void* logits, int logits_dtype, int64_t T, int64_t E, in
                          n_chunks, sms, s);
 }
 
+template <typename LogitT>
+int launch_router_grouped_t(const LogitT* logits, const float* bias, int64_t T, int64_t E, int64_t n_group,
+                            int64_t topk_group, int64_t topk, int renorm, float scale, int32_t* ids, float* w, int sms,
+                            cudaStream_t s) {
+  const int64_t want = (T + kRouterWarps - 1) / kRouterWarps;
+  const int grid = static_cast<int>(want < (int64_t)sms * 16 ? want : (int64_t)sms * 16);
+  const int threads = kRouterWarps * 32;
+  const size_t smem = sizeof(float) * kRouterWarps * static_cast<size_t>(E);
+#define MOE_ROUTER_G_CASE(V)                                                                                  \
+  if (E <= 32 * (V)) {                                                                                        \
+    router_grouped_kernel<LogitT, V><<<grid, threads, smem, s>>>(logits, bias, (int)T, (int)E, (int)n_group,  \
+                                                                 (int)topk_group, (int)topk, renorm, scale,   \
+                                                                 ids, w);                                     \
+    MOE_CUDA(cudaGetLastError());                                                                             \
+    return MOE_OK;                                                                                            \
+  }
+  MOE_ROUTER_G_CASE(1)
+  MOE_ROUTER_G_CASE(2)
+  MOE_ROUTER_G_CASE(4)
+  MOE_ROUTER_G_CASE(8)
+  MOE_ROUTER_G_CASE(16)
+  MOE_ROUTER_G_CASE(32)
+#undef MOE_ROUTER_G_CASE
+  return fail(MOE_ERR_INVALID_ARG, "num_experts must be <= %d", 32 * 32);
+}
+
 }  // namespace
 }  // namespace moe
 
@@ -936,6 +962,36 @@ int64_t moe_max_padded_rows(int64_t R, int64_t E, int64_t bm) {
 
 size_t moe_align_workspace_bytes(int64_t R, int64_t E) {
   return round_up(sizeof(int) * static_cast<size_t>(align_chunks(R)) * static_cast<size_t>(E > 0 ? E : 0), 256);
+}
+
+int moe_router_grouped_topk(const void* logits, int logits_dtype, const float* bias, int64_t T, int64_t E,
+                            int64_t n_group, int64_t topk_group, int64_t topk, int renormalize, float scale,
+                            int32_t* ids, float* w, void* stream) {
+  t_last_error.clear();
+  if (logits_dtype != MOE_F32 && logits_dtype != MOE_F16 && logits_dtype != MOE_BF16)
+    return fail(MOE_ERR_INVALID_ARG, "router logits must be fp32, fp16 or bf16");
+  if (E < 1 || E > kAlignMaxExperts) return fail(MOE_ERR_INVALID_ARG, "num_experts must be in [1, %d]", kAlignMaxExperts);
+  if (n_group < 1 || n_group > 32 || E % n_group != 0)
+    return fail(MOE_ERR_INVALID_ARG, "num_expert_group must be in [1, 32] and divide num_experts");
+  if (topk_group < 1 || topk_group > n_group) return fail(MOE_ERR_INVALID_ARG, "topk_group must be in [1, num_expert_group]");
+  if (topk < 1 || topk > kRouterMaxTopk || topk > topk_group * (E / n_group))
+    return fail(MOE_ERR_INVALID_ARG, "topk must be in [1, min(%d, topk_group * experts per group)]", kRouterMaxTopk);
+  if (T < 0 || T * topk > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "bad token count");
+  if (T == 0) return MOE_OK;
+  if (!logits || !ids || !w) return fail(MOE_ERR_INVALID_ARG, "null tensor argument");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rn = renormalize ? 1 : 0;
+  if (logits_dtype == MOE_F32)
+    return launch_router_grouped_t(static_cast<const float*>(logits), bias, T, E, n_group, topk_group, topk, rn, scale,
+                                   ids, w, sms, s);
+  if (logits_dtype == MOE_F16)
+    return launch_router_grouped_t(static_cast<const __half*>(logits), bias, T, E, n_group, topk_group, topk, rn,
+                                   scale, ids, w, sms, s);
+  return launch_router_grouped_t(static_cast<const __nv_bfloat16*>(logits), bias, T, E, n_group, topk_group, topk, rn,
+                                 scale, ids, w, sms, s);
 }
 
 int moe_router_topk(const void* logits, int logits_dtype, int64_t T, int64_t E, int64_t topk, int renormalize,

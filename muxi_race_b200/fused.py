@@ -197,6 +197,43 @@ def fused_topk(
     return w, ids
 
 
+def grouped_topk(
+    hidden_states: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    e_score_correction_bias: Optional[torch.Tensor] = None,
+    routed_scaling_factor: float = 1.0,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Group-limited sigmoid routing in one kernel (the DeepSeek-V3 router):
+    (topk_weights [T, k] fp32, topk_ids [T, k] int32).
+
+    Scores s = sigmoid(gating_output); experts are chosen by s + e_score_correction_bias within the
+    topk_group best of num_expert_group groups (group score = sum of its two best); weights are s
+    at the chosen ids, renormalised when ``renormalize``, times ``routed_scaling_factor``.
+    """
+    T = int(hidden_states.shape[0])
+    _check(gating_output.dim() == 2 and gating_output.shape[0] == T, "gating_output must be [T, E]")
+    _check(gating_output.is_cuda and gating_output.is_contiguous(), "gating_output must be a contiguous CUDA tensor")
+    _check(gating_output.dtype in _LOGIT_DTYPES, "gating_output must be fp32, fp16 or bf16")
+    E = int(gating_output.shape[1])
+    bias_ptr = None
+    if e_score_correction_bias is not None:
+        b = e_score_correction_bias
+        _check(b.is_cuda and b.dtype == torch.float32 and b.is_contiguous() and b.numel() == E,
+               "e_score_correction_bias must be a contiguous fp32 CUDA tensor [E]")
+        bias_ptr = b.data_ptr()
+    dev = gating_output.device
+    ids = torch.empty((T, topk), dtype=torch.int32, device=dev)
+    w = torch.empty((T, topk), dtype=torch.float32, device=dev)
+    _lib.call("moe_router_grouped_topk", gating_output.data_ptr(), _LOGIT_DTYPES[gating_output.dtype], bias_ptr, T, E,
+              num_expert_group, topk_group, topk, int(bool(renormalize)), float(routed_scaling_factor), ids.data_ptr(),
+              w.data_ptr(), _stream(dev))
+    return w, ids
+
+
 def fused_moe_router(
     hidden_states: torch.Tensor,
     w_gate_up: torch.Tensor,

@@ -17,6 +17,11 @@ comparable bit for bit:
 
 Parity of the ids is pinned against ``torch.topk(torch.softmax(logits))`` on tie-free inputs
 (``tests/test_router_ref.py``); with ties torch leaves the order unspecified and this oracle fixes it.
+
+``router_grouped_ref`` restates group-limited sigmoid routing (the published DeepSeek-V3 router:
+sigmoid scores, a per-expert selection bias, groups scored by the sum of their two best biased
+scores, the best ``topk_group`` groups eligible, weights = unbiased scores renormalised and scaled)
+with the same total selection order.
 """
 from __future__ import annotations
 
@@ -45,3 +50,39 @@ def router_topk_ref(logits: torch.Tensor, topk: int, renormalize: bool = True):
     if renormalize:
         w = w / w.sum(-1, keepdim=True)
     return w.contiguous(), ids
+
+
+def router_grouped_ref(logits: torch.Tensor, topk: int, n_group: int, topk_group: int, bias=None,
+                       renormalize: bool = True, scale: float = 1.0):
+    """(topk_weights [T, k] fp32, topk_ids [T, k] int32, margins) on CPU. ``margins`` [T] is, per
+    token, the smallest relative gap at the selection boundaries (groups and experts), to tell
+    near-ties (where a one-ulp difference in the sigmoid may change the choice) from real order."""
+    lf = logits.detach().to(torch.float32).cpu()
+    T, E = lf.shape
+    s = torch.sigmoid(lf)
+    c = s + (bias.detach().float().cpu() if bias is not None else 0.0)
+    gs = E // n_group
+    cg = c.view(T, n_group, gs)
+    top2 = torch.sort(cg, dim=-1, descending=True).values
+    gscore = top2[..., 0] + top2[..., 1] if gs > 1 else top2[..., 0]
+    gkeys = order_keys(gscore).astype(np.int64)
+    gorder = np.argsort(-gkeys, axis=1, kind="stable")
+    sel = np.zeros((T, n_group), dtype=bool)
+    np.put_along_axis(sel, gorder[:, :topk_group], True, axis=1)
+    keys = order_keys(c).astype(np.int64)
+    eligible = np.repeat(sel, gs, axis=1)
+    keys = np.where(eligible, keys, -1)
+    ids = np.argsort(-keys, axis=1, kind="stable")[:, :topk].astype(np.int32)
+    w = torch.gather(s, 1, torch.from_numpy(ids).long())
+    if renormalize:
+        w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    w = w * scale
+    # boundary gaps (relative): group topk_group vs topk_group + 1, expert topk vs topk + 1
+    gsorted = torch.sort(gscore, dim=-1, descending=True).values
+    cm = torch.where(torch.from_numpy(eligible), c, torch.full_like(c, -float("inf")))
+    csorted = torch.sort(cm, dim=-1, descending=True).values
+    inf = torch.full((T,), float("inf"))
+    ggap = (gsorted[:, topk_group - 1] - gsorted[:, topk_group]).abs() if topk_group < n_group else inf
+    cgap = (csorted[:, topk - 1] - csorted[:, topk]).abs() if topk < topk_group * gs else inf
+    margins = torch.minimum(ggap / gsorted[:, 0].abs().clamp_min(1e-30), cgap / csorted[:, 0].abs().clamp_min(1e-30))
+    return w.contiguous(), torch.from_numpy(np.ascontiguousarray(ids)), margins

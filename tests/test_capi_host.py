@@ -80,6 +80,12 @@ def test_router_argument_checks():
                                   None, 0, None)
         assert rc == -1 and msg in lib.moe_last_error(), (dt, T, E, k, lib.moe_last_error())
     assert lib.moe_router_topk(None, _lib.MOE_F32, 0, 256, 8, 1, None, None, None) == 0
+    # grouped routing: groups must divide the experts, topk_group <= groups, topk within reach
+    for (E, ng, tg, k), msg in [((256, 7, 4, 8), b"divide"), ((256, 8, 9, 8), b"topk_group"),
+                                ((256, 64, 1, 8), b"num_expert_group"), ((64, 8, 1, 9), b"topk")]:
+        rc = lib.moe_router_grouped_topk(None, _lib.MOE_F32, None, 8, E, ng, tg, k, 1, 1.0, None, None, None)
+        assert rc == -1 and msg in lib.moe_last_error(), (E, ng, tg, k, lib.moe_last_error())
+    assert lib.moe_router_grouped_topk(None, _lib.MOE_F32, None, 0, 256, 8, 4, 8, 1, 2.5, None, None, None) == 0
     rc = lib.moe_router_topk(None, _lib.MOE_F32, 4, 256, 8, 1, None, None, None)
     assert rc == -1 and b"null" in lib.moe_last_error()
 

@@ -67,3 +67,35 @@ def test_low_precision_logits_order_by_value():
         rest = [e for e in range(64) if e not in set(ids[t].tolist())]
         for e in rest:
             assert f[t, e].item() < last_v or (f[t, e].item() == last_v and e > last_e)
+
+
+def grouped_plain(logits, topk, n_group, topk_group, bias, scale):
+    """Group-limited sigmoid routing written the plain torch way (topk + masks), for comparison."""
+    T, E = logits.shape
+    scores = torch.sigmoid(logits)
+    sfc = scores + bias
+    gscore = sfc.view(T, n_group, -1).topk(2, dim=-1).values.sum(-1)
+    gidx = torch.topk(gscore, topk_group, dim=-1).indices
+    gmask = torch.zeros((T, n_group), dtype=torch.bool).scatter_(1, gidx, True)
+    emask = gmask.unsqueeze(-1).expand(T, n_group, E // n_group).reshape(T, E)
+    ids = torch.topk(sfc.masked_fill(~emask, float("-inf")), topk, dim=-1).indices
+    w = scores.gather(1, ids)
+    return w / (w.sum(-1, keepdim=True) + 1e-20) * scale, ids
+
+
+@pytest.mark.parametrize("T,E,n_group,topk_group,k", [(300, 256, 8, 4, 8), (200, 64, 4, 2, 6), (100, 96, 3, 3, 5)])
+def test_grouped_oracle_matches_plain_torch(T, E, n_group, topk_group, k):
+    from oracle.router_ref import router_grouped_ref
+
+    g = torch.Generator().manual_seed(E + k)
+    logits = torch.randn((T, E), generator=g)
+    bias = torch.randn(E, generator=g) * 0.05
+    w, ids, margins = router_grouped_ref(logits, k, n_group, topk_group, bias, True, 2.5)
+    w_p, ids_p = grouped_plain(logits, k, n_group, topk_group, bias, 2.5)
+    sure = margins > 1e-6  # tokens without a boundary near-tie (nearly all of them)
+    assert int(sure.sum()) >= 0.95 * T
+    assert torch.equal(ids.long()[sure], ids_p[sure])  # both descending by biased score
+    torch.testing.assert_close(w[sure], w_p[sure])
+    torch.testing.assert_close(w.sum(-1), torch.full((T,), 2.5))
+    # every chosen expert lies in one of the topk_group chosen groups
+    assert max(torch.unique(ids[t].long() // (E // n_group)).numel() for t in range(T)) <= topk_group
