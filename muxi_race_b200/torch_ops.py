@@ -10,6 +10,8 @@ through CUDA-graph capture, and through meta / fake-tensor shape propagation.
 
 The eager implementations are the Python entry points of this package (C ABI underneath).
 """
+from typing import Optional
+
 import torch
 from torch import Tensor
 
@@ -57,6 +59,21 @@ def fused_topk(gating_output: Tensor, topk: int, renormalize: bool) -> tuple[Ten
 
 @fused_topk.register_fake
 def _fused_topk_fake(gating_output, topk, renormalize):
+    T = gating_output.shape[0]
+    return (gating_output.new_empty((T, topk), dtype=torch.float32),
+            gating_output.new_empty((T, topk), dtype=torch.int32))
+
+
+@torch.library.custom_op("muxi_race_b200::grouped_topk", mutates_args=())
+def grouped_topk(gating_output: Tensor, topk: int, renormalize: bool, num_expert_group: int, topk_group: int,
+                 e_score_correction_bias: Optional[Tensor], routed_scaling_factor: float) -> tuple[Tensor, Tensor]:
+    return _fused.grouped_topk(gating_output, gating_output, topk, renormalize, num_expert_group, topk_group,
+                               e_score_correction_bias, routed_scaling_factor)
+
+
+@grouped_topk.register_fake
+def _grouped_topk_fake(gating_output, topk, renormalize, num_expert_group, topk_group, e_score_correction_bias,
+                       routed_scaling_factor):
     T = gating_output.shape[0]
     return (gating_output.new_empty((T, topk), dtype=torch.float32),
             gating_output.new_empty((T, topk), dtype=torch.int32))

@@ -5,7 +5,7 @@ import muxi_race_b200.torch_ops  # noqa: F401 - registers torch.ops.muxi_race_b2
 
 
 def test_ops_registered():
-    for name in ("fused_moe", "fused_moe_int8", "fused_moe_fp8", "fused_topk", "run_kernel"):
+    for name in ("fused_moe", "fused_moe_int8", "fused_moe_fp8", "fused_topk", "grouped_topk", "run_kernel"):
         assert hasattr(torch.ops.muxi_race_b200, name), name
 
 
@@ -27,3 +27,5 @@ def test_meta_shapes():
     logits = torch.empty((T, E), dtype=torch.float32, **m)
     tw, tid = torch.ops.muxi_race_b200.fused_topk(logits, k, True)
     assert tw.shape == (T, k) and tw.dtype == torch.float32 and tid.dtype == torch.int32
+    gw, gi = torch.ops.muxi_race_b200.grouped_topk(logits, k, True, 4, 2, None, 2.5)
+    assert gw.shape == (T, k) and gi.dtype == torch.int32
