@@ -207,6 +207,7 @@ def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids
     k = topk_ids.shape[1]
     dev = hidden_states.device
     xq, xs = quantize(hidden_states)
+    xq = xq.to(torch.float64)  # exact for int8 and e4m3 values; indexed below as float64
     ids = topk_ids.reshape(-1).to(torch.int64)
     w = topk_weights.reshape(-1).to(torch.float32)
     out = torch.zeros((T, H), dtype=torch.float32, device=dev)
@@ -217,7 +218,7 @@ def fused_moe_int8_ref(hidden_states, w13_q, w13_scale, w2_q, w2_scale, topk_ids
         if routes.numel() == 0:
             continue
         tok = routes // k
-        a = xq[tok].to(torch.float64)
+        a = xq[tok]
         acc = a @ w13_q[e].to(torch.float64).T  # exact int32-range sums
         deq = acc.to(torch.float32) * xs[tok].unsqueeze(1) * w13s[e].unsqueeze(0)
         g, u = deq[:, :I], deq[:, I:]
