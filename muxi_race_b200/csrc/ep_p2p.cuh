@@ -192,6 +192,51 @@ __global__ void gather_rows_peer_kernel(const uint64_t* __restrict__ regions, Ep
   }
 }
 
+// Deduplicating variant of gather_rows_peer_kernel (selected with MOE_B200_EP_GATHER=dedup,
+// topk <= 32): one warp per virtual token (s, t) instead of per route. A token usually has several
+// of its top-k experts on one rank (top-8 over 2 ranks: ~4), and the per-route kernel reads its row
+// over NVLink once per route; here the warp reads it once and stores it into every local slot of
+// the token (lane j holds slot j; the slots are broadcast one by one). With zero_served it also
+// zeroes the token's partial row, as gather_rows_peer_kernel does.
+template <typename T>
+__global__ void gather_rows_peer_dedup_kernel(const uint64_t* __restrict__ regions, EpRegion L, int rank, int T_max,
+                                              int topk, int W, const int32_t* __restrict__ route_slot, int H,
+                                              T* __restrict__ xs, int zero_served) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const int vecs = H / 8;
+  const long long rows = static_cast<long long>(W) * T_max;
+  uint4* y = reinterpret_cast<uint4*>(regions[rank] + static_cast<uint64_t>(L.y));
+  for (long long tok = warp_id; tok < rows; tok += n_warps) {
+    const int my_slot = lane < topk ? route_slot[tok * topk + lane] : -1;
+    const unsigned local = __ballot_sync(0xffffffffu, my_slot >= 0);
+    if (local == 0u) continue;
+    const int s = static_cast<int>(tok / T_max);
+    const long long t = tok - static_cast<long long>(s) * T_max;
+    const uint4* src = ep_at<uint4>(regions, s, L.x) + t * vecs;
+    constexpr int U = 8;  // 16-byte loads in flight per lane
+    for (int v0 = lane; v0 < vecs; v0 += 32 * U) {
+      uint4 tmp[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (v0 + u * 32 < vecs) tmp[u] = __ldcg(src + v0 + u * 32);
+      for (unsigned m = local; m != 0u; m &= m - 1u) {
+        const int j = __ffs(static_cast<int>(m)) - 1;
+        const int slot = __shfl_sync(0xffffffffu, my_slot, j);
+        uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<size_t>(slot) * H);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + u * 32 < vecs) dst[v0 + u * 32] = tmp[u];
+      }
+    }
+    if (zero_served) {
+      uint4* dst = y + tok * vecs;
+      for (int v = lane; v < vecs; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 // Bulk-copy variant of gather_rows_peer_kernel (selected with MOE_B200_EP_GATHER=bulk): lane 0
 // of each warp moves whole token rows with the bulk-copy engine, peer row -> shared memory
 // (cp.async.bulk with an mbarrier) -> xs (cp.async.bulk store), two rows in flight per warp. Then

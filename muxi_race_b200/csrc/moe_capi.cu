@@ -355,13 +355,17 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   if (t.tn && (lsu || elt != 2 || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
-// Peer-memory EP gather: MOE_B200_EP_GATHER=bulk selects gather_rows_peer_bulk_kernel (bulk
-// copies through shared memory) instead of the per-lane 16-byte load loop.
+// Peer-memory EP gather: MOE_B200_EP_GATHER = bulk selects gather_rows_peer_bulk_kernel (bulk
+// copies through shared memory), dedup gather_rows_peer_dedup_kernel (each token row read once
+// per rank, stored into all its local slots); unset: the per-route 16-byte load loop.
 constexpr size_t kEpBulkMaxSmem = 220 * 1024;
-static bool ep_gather_bulk() {
-  static const bool v = [] {
+enum EpGather : int { kEpGatherRoute = 0, kEpGatherBulk = 1, kEpGatherDedup = 2 };
+static int ep_gather_mode() {
+  static const int v = [] {
     const char* e = getenv("MOE_B200_EP_GATHER");
-    return e && strcmp(e, "bulk") == 0;
+    if (e && strcmp(e, "bulk") == 0) return (int)kEpGatherBulk;
+    if (e && strcmp(e, "dedup") == 0) return (int)kEpGatherDedup;
+    return (int)kEpGatherRoute;
   }();
   return v;
 }
@@ -1139,7 +1143,19 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_CUDA(cudaGetLastError());
       MOE_CUDA(cudaMemsetAsync(amax, 0, sizeof(float) * (size_t)L.P_max, s));
     }
-  } else if (peer && ep_gather_bulk() &&
+  } else if (peer && ep_gather_mode() == kEpGatherDedup && topk <= 32) {
+    // one warp per virtual token: its row crosses NVLink once, then lands in all its local slots
+    const int zero_served = peer->push ? 0 : 1;
+    if (dtype == MOE_F16)
+      gather_rows_peer_dedup_kernel<__half><<<gblocks, 256, 0, s>>>(peer->regions, peer->L, peer->rank,
+                                                                    peer->T_max, (int)topk, peer->W, slot, (int)H,
+                                                                    static_cast<__half*>(xs), zero_served);
+    else
+      gather_rows_peer_dedup_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(
+          peer->regions, peer->L, peer->rank, peer->T_max, (int)topk, peer->W, slot, (int)H,
+          static_cast<__nv_bfloat16*>(xs), zero_served);
+    MOE_CUDA(cudaGetLastError());
+  } else if (peer && ep_gather_mode() == kEpGatherBulk &&
              (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps <= kEpBulkMaxSmem) {
     // bulk-copy gather: whole rows through shared memory, one CTA of 4 warps per SM
     const size_t smem = (size_t)kEpBulkWarps * 2 * (size_t)H * 2 + 16 * kEpBulkWarps;

@@ -58,8 +58,10 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="nccl"):
+def _ep_worker(rank, world, port, out_dir, T_per_rank, E, H, I, k, skew, mode="nccl", env=None):
     import torch.distributed as dist
+
+    os.environ.update(env or {})  # library switches (read on first use, in this process only)
 
     from muxi_race_b200.workloads import MoeConfig, make_hidden, make_routing, make_weights
     from oracle.moe_ref import fused_moe_ref
