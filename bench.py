@@ -575,7 +575,8 @@ def bench_ep(args, world, rank, local):
                        "ep_exchange": ("peer memory: NVLink loads of the token rows and "
                                        + ("Stage2 adding into the home ranks' regions (push combine)"
                                           if args.ep_combine == "push" else "loads of the partial outputs")
-                                       + " inside the library's kernels, flag barriers; no collectives library")
+                                       + " inside the library's kernels, flag barriers; no collectives library; "
+                                       + f"token gather: {os.environ.get('MOE_B200_EP_GATHER') or 'per route'}")
                        if p2p else f"NCCL all_to_all_single, {n_chunks} chunk(s)",
                        "l2": "inputs larger than L2 (expert weights streamed per step)"},
             "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
