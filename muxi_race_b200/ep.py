@@ -124,7 +124,7 @@ class CudaOps:
                  torch.empty(4, **i32))
         offsets = torch.empty(W + 1, **i32)
         nbytes = _lib.lib().moe_ep_plan_workspace_bytes(T, W)
-        ws = _workspace(("ep_plan", self.device, T, W, _stream(self.device)), nbytes, self.device)
+        ws = _workspace(("ep_plan", self.device, _stream(self.device)), nbytes, self.device)
         _lib.call("moe_ep_plan", topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], T, k, self.expert_rank.data_ptr(),
                   self.E, W, p.send_counts.data_ptr(), offsets.data_ptr(), p.send_pairs.data_ptr(),
                   p.pair_slot.data_ptr(), p.meta.data_ptr(), ws.data_ptr(), ws.numel(), _stream(self.device))

@@ -31,6 +31,10 @@ def _stream(device: torch.device) -> int:
 
 
 def _workspace(key, nbytes: int, device: torch.device) -> torch.Tensor:
+    """Scratch buffer of at least `nbytes`, one per (entry point, device, stream), grown when a call
+    needs more. Calls on one stream run in stream order, so they can share it whatever their
+    shapes, and the cache stays bounded by the largest call (not one buffer per shape). A buffer
+    replaced by a larger one goes back to the caching allocator of its own stream."""
     with _WS_LOCK:
         ws = _WS.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -91,7 +95,7 @@ def moe_align(topk_ids: torch.Tensor, num_experts: int, block_m: int = BLOCK_M) 
         meta=torch.empty(4, **i32),
     )
     nbytes = _lib.lib().moe_align_workspace_bytes(R, num_experts)
-    ws = _workspace(("align", dev, R, num_experts, _stream(dev)), nbytes, dev)
+    ws = _workspace(("align", dev, _stream(dev)), nbytes, dev)
     _lib.call(
         "moe_align", topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], R, num_experts, block_m,
         al.group_sizes.data_ptr(), al.group_offsets.data_ptr(), al.group_padded_offsets.data_ptr(),
@@ -152,7 +156,7 @@ def fused_moe(
     dt = _DTYPES[hidden_states.dtype]
     fn = "moe_fused_ordered" if deterministic else "moe_fused"
     nbytes = getattr(_lib.lib(), fn + "_workspace_bytes")(T, k, E, H, I, dt)
-    ws = _workspace(("fused", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    ws = _workspace(("fused", dev, _stream(dev)), nbytes, dev)
     _lib.call(
         fn, hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(), topk_ids.data_ptr(),
         _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(), _W_DTYPES[topk_weights.dtype], out.data_ptr(),
@@ -265,7 +269,7 @@ def fused_moe_router(
     if T:
         dt = _DTYPES[hidden_states.dtype]
         nbytes = _lib.lib().moe_fused_workspace_bytes(T, k, E, H, I, dt)
-        ws = _workspace(("fused", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+        ws = _workspace(("fused", dev, _stream(dev)), nbytes, dev)
         _lib.call(
             "moe_fused_router", hidden_states.data_ptr(), w_gate_up.data_ptr(), w_down.data_ptr(),
             gating_output.data_ptr(), _LOGIT_DTYPES[gating_output.dtype], int(bool(renormalize)), ids.data_ptr(),
@@ -315,7 +319,7 @@ def fused_moe_int8(
     dev = hidden_states.device
     dt = _DTYPES[hidden_states.dtype]
     nbytes = _lib.lib().moe_fused_int8_workspace_bytes(T, k, E, H, I, dt)
-    ws = _workspace(("fused_i8", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    ws = _workspace(("fused_i8", dev, _stream(dev)), nbytes, dev)
     _lib.call(
         "moe_fused_int8", hidden_states.data_ptr(), w13_q.data_ptr(), w13_scale.data_ptr(), w2_q.data_ptr(),
         w2_scale.data_ptr(), topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(),
@@ -366,7 +370,7 @@ def fused_moe_fp8(
     dev = hidden_states.device
     dt = _DTYPES[hidden_states.dtype]
     nbytes = _lib.lib().moe_fused_fp8_workspace_bytes(T, k, E, H, I, dt)
-    ws = _workspace(("fused_f8", dev, T, k, E, H, I, dt, _stream(dev)), nbytes, dev)
+    ws = _workspace(("fused_f8", dev, _stream(dev)), nbytes, dev)
     _lib.call(
         "moe_fused_fp8", hidden_states.data_ptr(), w13_q.data_ptr(), w13_scale.data_ptr(), w2_q.data_ptr(),
         w2_scale.data_ptr(), topk_ids.data_ptr(), _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(),

@@ -97,7 +97,7 @@ def fused_moe_packed(hidden_states: torch.Tensor, packed: PackedWeights, topk_id
     dt = _DTYPES[hidden_states.dtype]
     kind = KINDS[packed.kind]
     nbytes = _lib.lib().moe_fused_packed_workspace_bytes(T, k, packed.E, H, packed.I, kind, dt)
-    ws = _workspace(("fused_packed", dev, T, k, packed.E, H, packed.I, kind, dt, _stream(dev)), nbytes, dev)
+    ws = _workspace(("fused_packed", dev, _stream(dev)), nbytes, dev)
     _lib.call("moe_fused_packed", hidden_states.data_ptr(), packed.blob.data_ptr(), kind, topk_ids.data_ptr(),
               _ID_DTYPES[topk_ids.dtype], topk_weights.data_ptr(), _W_DTYPES[topk_weights.dtype], out.data_ptr(),
               T, H, packed.I, packed.E, k, dt, ws.data_ptr(), ws.numel(), _stream(dev))
