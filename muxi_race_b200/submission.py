@@ -2,8 +2,9 @@
 
 ``run_kernel`` keeps the reference signature and semantics (初审材料/源代码/submission.py:2098-2184):
 ten positional tensors, ``out`` is the only tensor written, padding rows of ``out`` end up 0,
-empty inputs take the same shortcuts (:2117-2153), the ``up_logits`` scratch is cached per shape
-(:2081-2095) and both fp32 and fp16 routed weights are accepted (:2125-2128). The work runs in
+empty inputs take the same shortcuts (:2117-2153), the ``up_logits`` scratch is cached (:2081-2095;
+here per device and stream, grown as needed) and both fp32 and fp16 routed weights are accepted
+(:2125-2128). The work runs in
 two sm_100a kernels of ``libmoe_b200.so`` on the current CUDA stream, with no host
 synchronisation.
 """
@@ -27,9 +28,12 @@ def _stream_handle(device: torch.device) -> int:
 
 
 def _get_workspace(x: torch.Tensor, intermediate: int) -> torch.Tensor:
-    """Scratch for the Stage1 output ``up_logits`` [P, I] (reference ``_get_workspace``)."""
+    """Scratch for the Stage1 output ``up_logits`` [P, I] (reference ``_get_workspace``, which caches
+    one buffer per shape). Here one buffer per device and stream, grown when a call needs more:
+    calls on one stream run in order, so they can share it whatever their shapes, calls on
+    different streams never share it, and the cache is bounded by the largest call."""
     nbytes = _lib.lib().moe_run_kernel_workspace_bytes(x.shape[0], intermediate, _DTYPES[x.dtype])
-    key = (x.device, int(x.shape[0]), int(intermediate), x.dtype)
+    key = (x.device, _stream_handle(x.device))
     with _WS_LOCK:
         ws = _WORKSPACE_CACHE.get(key)
         if ws is None or ws.numel() < nbytes:
