@@ -15,9 +15,9 @@
 //           warp) combine SiLU(gate) * up with one shuffle. Lane l of quadrant q owns feature
 //           16q + 8(l >> 4) + (l & 7) and writes U[token][feature] for 32 tokens per TMEM load:
 //           16 gate lanes store 32 contiguous bytes of one token row per instruction.
-//   Stage2  the 128 weight rows are 128 output features; lane m writes feature n0 + m of every
-//           token: lane pairs combine two features into one f16x2 / bf16x2 reduction (combine
-//           into the token-major output) or store (padded layout).
+//   Stage2  the 128 weight rows are 128 output features; lane m holds feature n0 + m of every
+//           token: lanes 8g .. 8g+7 pack their eight features into one 16-byte reduction (combine
+//           into the token-major output) or store (padded layout) issued by lane 8g.
 // Roles, rings, bounded waits and drains are those of moe_gemm_kernel (warp 0 weights, warp 6
 // tokens, warp 1 MMA issuer and TMEM owner, warps 2..5 epilogue); two 256-column accumulator
 // slots, so an epilogue overlaps the next unit's main loop.
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         OutT* out = reinterpret_cast<OutT*>(args.out);
         const int h = nt * kBM + 32 * q + lane;  // output feature of this lane
-        const bool pair_lane = (lane & 1) == 0;
+        const bool lead_lane = (lane & 7) == 0;  // gathers features h .. h + 7 into one 16-byte op
         for (int c0 = 0; c0 < rows; c0 += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
@@ -362,19 +362,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float sc = __shfl_sync(0xffffffffu, scale, j);
             const float mine = __uint_as_float(v[j]) * sc;
             const float next = __shfl_down_sync(0xffffffffu, mine, 1);
-            if (row >= 0 && pair_lane && h < args.N) {
+            // lane 8g collects the f16x2 pairs of lanes 8g, 8g+2, 8g+4, 8g+6: features h .. h + 7
+            const uint32_t pk0 = Elt<OutT>::pack2(mine, next);
+            const uint32_t pk1 = __shfl_down_sync(0xffffffffu, pk0, 2);
+            const uint32_t pk2 = __shfl_down_sync(0xffffffffu, pk0, 4);
+            const uint32_t pk3 = __shfl_down_sync(0xffffffffu, pk0, 6);
+            if (row >= 0 && lead_lane && h < args.N) {
               OutT* dst = out + static_cast<size_t>(row) * args.ldo + h;
-              if (h + 1 < args.N) {
-                const uint32_t pk = Elt<OutT>::pack2(mine, next);
+              if (h + 8 <= args.N) {  // 16-byte aligned: h % 8 == 0 and ldo % 8 == 0
+                const uint4 val = make_uint4(pk0, pk1, pk2, pk3);
                 if (MODE == kStage2Pad)
-                  *reinterpret_cast<uint32_t*>(dst) = pk;
+                  *reinterpret_cast<uint4*>(dst) = val;
                 else
-                  red_add_x2(dst, pk);
-              } else if (MODE == kStage2Pad) {
-                if constexpr (Elt<OutT>::kBF16)
-                  *dst = __float2bfloat16_rn(mine);
-                else
-                  *dst = __float2half_rn(mine);
+                  red_add_v4(dst, val);
+              } else {  // a tile edge that is not a multiple of 8 features: pairs, then a single
+                const uint32_t pks[4] = {pk0, pk1, pk2, pk3};
+#pragma unroll
+                for (int q2 = 0; q2 < 4; ++q2) {
+                  const int hh = h + 2 * q2;
+                  if (hh + 1 < args.N) {
+                    if (MODE == kStage2Pad)
+                      *reinterpret_cast<uint32_t*>(dst + 2 * q2) = pks[q2];
+                    else
+                      red_add_x2(dst + 2 * q2, pks[q2]);
+                  } else if (hh < args.N && MODE == kStage2Pad) {
+                    dst[2 * q2] = reinterpret_cast<const OutT*>(&pks[q2])[0];  // the pair's low half
+                  }
+                }
               }
             }
           }
