@@ -14,7 +14,7 @@
 //           8a + r and lane 16a + 8 + r its up feature, so a lane and its partner lane ^ 8 (same
 //           warp) combine SiLU(gate) * up with one shuffle. Lane l of quadrant q owns feature
 //           16q + 8(l >> 4) + (l & 7) and writes U[token][feature] for 32 tokens per TMEM load:
-//           16 gate lanes store 32 contiguous bytes of one token row per instruction.
+//           lanes 0 and 16 gather their eight gate lanes' results into one 16-byte store each.
 //   Stage2  the 128 weight rows are 128 output features; lane m holds feature n0 + m of every
 //           token: lanes 8g .. 8g+7 pack their eight features into one 16-byte reduction (combine
 //           into the token-major output) or store (padded layout) issued by lane 8g.
@@ -309,7 +309,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int prow0 = args.group_padded_offsets[e] + row0;  // stacked row of the chunk's first token
       if (MODE == kStage1) {
         OutT* U = reinterpret_cast<OutT*>(args.U);
-        const bool gate_lane = (lane & 8) == 0;
+        // gate lanes 0-7 and 16-23 hold features f0 .. f0 + 7 and f0 + 8 .. f0 + 15; lanes 0 and 16
+        // gather their group's eight results into one 16-byte store per token
+        const bool lead_lane = (lane & 15) == 0;
         const int f = nt * 64 + 16 * q + 8 * (lane >> 4) + (lane & 7);
         for (int c0 = 0; c0 < rows; c0 += 32) {
           uint32_t v[32];
@@ -319,14 +321,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) {
             const float mine = __uint_as_float(v[j]);
             const float other = __shfl_xor_sync(0xffffffffu, mine, 8);
-            if (gate_lane && c0 + j < rows && f < args.N) {
-              const float h = silu_mul(mine, other);
-              OutT hv;
-              if constexpr (Elt<OutT>::kBF16)
-                hv = __float2bfloat16_rn(h);
-              else
-                hv = __float2half_rn(h);
-              U[static_cast<size_t>(prow0 + c0 + j) * args.ldu + f] = hv;
+            const float h = silu_mul(mine, other);  // meaningful on the gate lanes
+            const float h1 = __shfl_down_sync(0xffffffffu, h, 1);
+            const uint32_t pk0 = Elt<OutT>::pack2(h, h1);
+            const uint32_t pk1 = __shfl_down_sync(0xffffffffu, pk0, 2);
+            const uint32_t pk2 = __shfl_down_sync(0xffffffffu, pk0, 4);
+            const uint32_t pk3 = __shfl_down_sync(0xffffffffu, pk0, 6);
+            if (lead_lane && c0 + j < rows && f < args.N) {
+              OutT* dst = U + static_cast<size_t>(prow0 + c0 + j) * args.ldu + f;
+              if (f + 8 <= args.N) {  // 16-byte aligned: f % 8 == 0 and ldu % 8 == 0
+                *reinterpret_cast<uint4*>(dst) = make_uint4(pk0, pk1, pk2, pk3);
+              } else {
+                const uint32_t pks[4] = {pk0, pk1, pk2, pk3};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  if (f + i < args.N) dst[i] = reinterpret_cast<const OutT*>(pks)[i];
+              }
             }
           }
         }
