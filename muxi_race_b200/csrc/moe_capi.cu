@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "../../include/moe_b200.h"
 #include "ep_kernels.cuh"
@@ -352,7 +353,7 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return safe;
   if (t.bn == 128 && stage != 1) return safe;
   if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
-  if (t.tn && (lsu || elt != 2 || (K * elt) % kKBytes != 0)) return safe;
+  if (t.tn && (lsu || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
 // Peer-memory EP gather: MOE_B200_EP_GATHER = bulk selects gather_rows_peer_bulk_kernel (bulk
@@ -451,32 +452,33 @@ struct TnMaps {
   CUtensorMap w, x128, x64, x32, x16;
 };
 
-int make_tn_x_maps(TnMaps* m, const void* rows_base, int64_t rows, int64_t K, const char* what) {
-  MOE_TRY(make_tmap(&m->x128, rows_base, 2, rows, K, 128, what));
-  MOE_TRY(make_tmap(&m->x64, rows_base, 2, rows, K, 64, what));
-  MOE_TRY(make_tmap(&m->x32, rows_base, 2, rows, K, 32, what));
-  MOE_TRY(make_tmap(&m->x16, rows_base, 2, rows, K, 16, what));
+int make_tn_x_maps(TnMaps* m, const void* rows_base, int elt, int64_t rows, int64_t K, const char* what) {
+  MOE_TRY(make_tmap(&m->x128, rows_base, elt, rows, K, 128, what));
+  MOE_TRY(make_tmap(&m->x64, rows_base, elt, rows, K, 64, what));
+  MOE_TRY(make_tmap(&m->x32, rows_base, elt, rows, K, 32, what));
+  MOE_TRY(make_tmap(&m->x16, rows_base, elt, rows, K, 16, what));
   return MOE_OK;
 }
 
 // Stage1 weights of the fused path: 5-D map {k-block elements, 8 rows, gate/up, 8-row groups,
 // k-blocks} over w_gate_up [E, 2I, H] (gate rows at e*2I + f, up rows I further), box
 // {64, 8, 2, 8, 1}: 64 gate and 64 up rows interleaved by 8-row atoms.
-int make_tn_w13_map(CUtensorMap* map, const void* w13, int64_t E, int64_t H, int64_t I) {
-  if (I % 8 != 0 || (H * 2) % kKBytes != 0) return fail(MOE_ERR_UNSUPPORTED, "operand-swapped Stage1 needs I a multiple of 8 and H a multiple of 64");
-  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(kKBytes / 2), 8, 2, static_cast<cuuint64_t>((2 * E * I - I) / 8),
-                              static_cast<cuuint64_t>(H * 2 / kKBytes)};
-  const cuuint64_t strides[4] = {static_cast<cuuint64_t>(H * 2), static_cast<cuuint64_t>(I * H * 2),
-                                 static_cast<cuuint64_t>(8 * H * 2), static_cast<cuuint64_t>(kKBytes)};
-  const cuuint32_t box[5] = {static_cast<cuuint32_t>(kKBytes / 2), 8, 2, 8, 1};
-  return encode_map(map, w13, 2, 5, dims, strides, box, "w_gate_up (operand-swapped)");
+int make_tn_w13_map(CUtensorMap* map, const void* w13, int elt, int64_t E, int64_t H, int64_t I) {
+  if (I % 8 != 0 || (H * elt) % kKBytes != 0)
+    return fail(MOE_ERR_UNSUPPORTED, "operand-swapped Stage1 needs I a multiple of 8 and whole 128-byte k-blocks");
+  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(kKBytes / elt), 8, 2,
+                              static_cast<cuuint64_t>((2 * E * I - I) / 8), static_cast<cuuint64_t>(H * elt / kKBytes)};
+  const cuuint64_t strides[4] = {static_cast<cuuint64_t>(H * elt), static_cast<cuuint64_t>(I * H * elt),
+                                 static_cast<cuuint64_t>(8 * H * elt), static_cast<cuuint64_t>(kKBytes)};
+  const cuuint32_t box[5] = {static_cast<cuuint32_t>(kKBytes / elt), 8, 2, 8, 1};
+  return encode_map(map, w13, elt, 5, dims, strides, box, "w_gate_up (operand-swapped)");
 }
 
-template <int MODE, typename OutT>
+template <int MODE, typename OutT, int Q8>
 int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t stream) {
   constexpr int AST = 6, BST = 4;
-  auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST>;
-  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3) * kNumTileCfg * 3 + tcfg * 3 + 2;
+  auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST, Q8>;
+  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + Q8) * kNumTileCfg * 3 + tcfg * 3 + 2;
   constexpr int smem = TnRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
@@ -488,10 +490,10 @@ int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_un
   return MOE_OK;
 }
 
-template <int MODE>
+template <int MODE, int Q8 = kQ16>
 int launch_tn_rt(int dtype, int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t s) {
-  return dtype == MOE_F16 ? launch_tn<MODE, __half>(dev, tcfg, m, args, max_units, s)
-                          : launch_tn<MODE, __nv_bfloat16>(dev, tcfg, m, args, max_units, s);
+  return dtype == MOE_F16 ? launch_tn<MODE, __half, Q8>(dev, tcfg, m, args, max_units, s)
+                          : launch_tn<MODE, __nv_bfloat16, Q8>(dev, tcfg, m, args, max_units, s);
 }
 
 // One grouped GEMM stage with the chosen tile configuration.
@@ -1299,24 +1301,24 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   }
 
   const int max_tiles1 = (int)L.nblk_max * a1.n_tiles, max_tiles2 = (int)L.nblk_max * a2.n_tiles;
+  // the operand-swapped kernel (tile "tn"): weights as the MMA's M side, tokens as N
+  TnArgs tn{};
+  tn.n_entries_dev = tn_count;
+  tn.entries = tn_entries;
+  tn.E = (int)E;
+  tn.group_sizes = gs;
+  tn.group_offsets = go;
+  tn.group_padded_offsets = gpo;
+  tn.R = (int)R;
+  tn.sorted_route_ids = sorted;
+  tn.topk = (int)topk;
+  tn.nblk = (int)L.nblk_max;
+  tn.status = status;
   if (!int8) {
-    // the operand-swapped kernel (tile "tn"): weights as the MMA's M side, tokens as N
-    TnArgs tn{};
-    tn.n_entries_dev = tn_count;
-    tn.entries = tn_entries;
-    tn.E = (int)E;
-    tn.group_sizes = gs;
-    tn.group_offsets = go;
-    tn.group_padded_offsets = gpo;
-    tn.R = (int)R;
-    tn.sorted_route_ids = sorted;
-    tn.topk = (int)topk;
-    tn.nblk = (int)L.nblk_max;
-    tn.status = status;
     if (t1.tn) {
       TnMaps tm{};
-      MOE_TRY(make_tn_w13_map(&tm.w, w13, E, H, I));
-      MOE_TRY(make_tn_x_maps(&tm, xs, L.P_max, H, "gathered hidden_states"));
+      MOE_TRY(make_tn_w13_map(&tm.w, w13, 2, E, H, I));
+      MOE_TRY(make_tn_x_maps(&tm, xs, 2, L.P_max, H, "gathered hidden_states"));
       TnArgs t = tn;
       t.K = (int)H;
       t.N = (int)I;
@@ -1357,7 +1359,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     } else if (t2.tn) {
       TnMaps tm{};
       MOE_TRY(make_tmap(&tm.w, w2, 2, E * H, I, kBM, "w_down"));
-      MOE_TRY(make_tn_x_maps(&tm, U, L.P_max, I, "intermediate"));
+      MOE_TRY(make_tn_x_maps(&tm, U, 2, L.P_max, I, "intermediate"));
       TnArgs t = tn;
       t.K = (int)I;
       t.N = (int)H;
@@ -1372,38 +1374,70 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
     }
     prof_record(4, s);
-  } else if (fp8) {
-    // as the int8 route below, with e4m3 operands and fp32 accumulation (TMA A path only)
-    MOE_TRY((launch_stage_rt<kStage1, kQF8, kATma>(dtype, false, tc1, dev, m1, a1, max_tiles1, s)));
-    prof_record(3, s);
-    if (dtype == MOE_F16)
-      quantize_rows_q8_kernel<__half, kQF8><<<sms * 4, 256, 0, s>>>(
-          static_cast<const __half*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
-          reinterpret_cast<float*>(ws + L.uscale));
-    else
-      quantize_rows_q8_kernel<__nv_bfloat16, kQF8><<<sms * 4, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
-          reinterpret_cast<float*>(ws + L.uscale));
-    MOE_CUDA(cudaGetLastError());
-    prof_record(4, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, kQF8, kATma>(dtype, false, tc2, dev, m2, a2, max_tiles2, s)));
-    prof_record(5, s);
   } else {
-    // Stage1 int8 writes U (16-bit) and its per-row amax; rows are re-quantised for Stage2.
-    MOE_TRY((launch_stage_rt<kStage1, true, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
-    prof_record(3, s);
-    if (dtype == MOE_F16)
-      quantize_rows_q8_kernel<__half><<<sms * 4, 256, 0, s>>>(static_cast<const __half*>(U), L.P_max, (int)I, meta,
-                                                              amax, reinterpret_cast<int8_t*>(ws + L.uq),
-                                                              reinterpret_cast<float*>(ws + L.uscale));
-    else
-      quantize_rows_q8_kernel<__nv_bfloat16><<<sms * 4, 256, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
-          reinterpret_cast<float*>(ws + L.uscale));
-    MOE_CUDA(cudaGetLastError());
-    prof_record(4, s);
-    MOE_TRY((launch_stage_rt<kStage2Comb, true, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
-    prof_record(5, s);
+    // 8-bit routes (int8; fp8 with e4m3 operands, fp32 accumulation, TMA A path only): Stage1
+    // writes U (16-bit) and its per-row amax; the rows are re-quantised for Stage2
+    auto run8 = [&](auto kind) -> int {
+      constexpr int Q = decltype(kind)::value;
+      if (t1.tn) {
+        TnMaps tm{};
+        MOE_TRY(make_tn_w13_map(&tm.w, w13, 1, E, H, I));
+        MOE_TRY(make_tn_x_maps(&tm, xs, 1, L.P_max, H, "quantised hidden_states"));
+        TnArgs t = tn;
+        t.K = (int)H;
+        t.N = (int)I;
+        t.n_tiles = (int)((I + 63) / 64);
+        t.w_group_per_expert = 2 * I / 8;
+        t.U = U;
+        t.ldu = (int)I;
+        t.a_scale = xscale;
+        t.b_scale = w13_scale;
+        t.b_scale_rows = (int)(2 * I);
+        t.b_up_offset = (int)I;
+        t.row_amax = amax;
+        MOE_TRY((launch_tn_rt<kStage1, Q>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s)));
+      } else if constexpr (Q == kQF8) {
+        MOE_TRY((launch_stage_rt<kStage1, kQF8, kATma>(dtype, false, tc1, dev, m1, a1, max_tiles1, s)));
+      } else {
+        MOE_TRY((launch_stage_rt<kStage1, kQI8, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
+      }
+      prof_record(3, s);
+      if (dtype == MOE_F16)
+        quantize_rows_q8_kernel<__half, Q><<<sms * 4, 256, 0, s>>>(
+            static_cast<const __half*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
+            reinterpret_cast<float*>(ws + L.uscale));
+      else
+        quantize_rows_q8_kernel<__nv_bfloat16, Q><<<sms * 4, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(U), L.P_max, (int)I, meta, amax, reinterpret_cast<int8_t*>(ws + L.uq),
+            reinterpret_cast<float*>(ws + L.uscale));
+      MOE_CUDA(cudaGetLastError());
+      prof_record(4, s);
+      if (t2.tn) {
+        TnMaps tm{};
+        MOE_TRY(make_tmap(&tm.w, w2, 1, E * H, I, kBM, "w_down"));
+        MOE_TRY(make_tn_x_maps(&tm, ws + L.uq, 1, L.P_max, I, "quantised intermediate"));
+        TnArgs t = tn;
+        t.K = (int)I;
+        t.N = (int)H;
+        t.n_tiles = (int)((H + kBM - 1) / kBM);
+        t.b_rows_per_expert = (int)H;
+        t.out = out;
+        t.ldo = (int)H;
+        t.routed = tw;
+        t.routed_dtype = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
+        t.a_scale = reinterpret_cast<const float*>(ws + L.uscale);
+        t.b_scale = w2_scale;
+        t.b_scale_rows = (int)H;
+        MOE_TRY((launch_tn_rt<kStage2Comb, Q>(dtype, dev, tc2, tm, t, (int)L.nblk_max * t.n_tiles, s)));
+      } else if constexpr (Q == kQF8) {
+        MOE_TRY((launch_stage_rt<kStage2Comb, kQF8, kATma>(dtype, false, tc2, dev, m2, a2, max_tiles2, s)));
+      } else {
+        MOE_TRY((launch_stage_rt<kStage2Comb, kQI8, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
+      }
+      prof_record(5, s);
+      return MOE_OK;
+    };
+    MOE_TRY(fp8 ? run8(std::integral_constant<int, kQF8>{}) : run8(std::integral_constant<int, kQI8>{}));
   }
   return MOE_OK;
 }

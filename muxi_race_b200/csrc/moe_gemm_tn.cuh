@@ -64,6 +64,12 @@ struct TnArgs {
   const int* sorted_route_ids;  // Stage2Comb
   int topk;
   int nblk;                     // 128-row blocks of the stacked row space
+  // 8-bit kinds: per stacked row (token) and per weight row scales, Stage1 row amax of U
+  const float* a_scale;         // [stacked rows]
+  const float* b_scale;         // [E * b_scale_rows]
+  int b_scale_rows;             // weight rows per expert in b_scale (2I Stage1, H Stage2)
+  int b_up_offset;              // Stage1: the up rows' offset inside an expert (I)
+  float* row_amax;              // Stage1: per stacked row amax of U (requantisation), may be null
   uint32_t* status;
 };
 
@@ -125,7 +131,8 @@ __device__ __forceinline__ void tn_load_x(uint8_t* dst, const CUtensorMap* m128,
 // tmW: Stage1 5-D map {64, 8, 2, groups, k-blocks} over the gate/up rows (box {64, 8, 2, 8, 1}),
 //      Stage2 2-D map {K, rows} (box 128 rows). tmX*: the stacked token rows (Stage1 xs, Stage2
 //      U) with boxes of 128 / 64 / 32 / 16 rows.
-template <int MODE, typename OutT, int AST, int BST>
+// Q8: operand kind (kQ16, kQI8, kQF8; the 8-bit kinds dequantise with a_scale x b_scale).
+template <int MODE, typename OutT, int AST, int BST, int Q8 = kQ16>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_tn_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX128,
                        const __grid_constant__ CUtensorMap tmX64, const __grid_constant__ CUtensorMap tmX32,
@@ -183,8 +190,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int num_units = *args.n_entries_dev * args.n_tiles;
-  const int num_kb = (args.K * 2 + kKBytes - 1) / kKBytes;
-  constexpr int kKElems = kKBytes / 2;
+  constexpr int kElt = Q8 ? 1 : 2;
+  const int num_kb = (args.K * kElt + kKBytes - 1) / kKBytes;
+  constexpr int kKElems = kKBytes / kElt;
 
   if (warp == 0 || warp == 6) {
     // ---------------------------------------------------------------- producers
@@ -241,7 +249,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc0 = idesc_f16(Elt<OutT>::kBF16, kBM, 16) & ~(0x3Fu << 17);  // N set per unit
+      const uint32_t idesc0 = (Q8 == kQF8 ? idesc_f8(kBM, 16)
+                               : Q8     ? idesc_i8(kBM, 16)
+                                        : idesc_f16(Elt<OutT>::kBF16, kBM, 16)) &
+                              ~(0x3Fu << 17);  // N set per unit
       int sw = 0, sx = 0;
       uint32_t pw = 0, px = 0;
       uint32_t slot_cnt = 0;
@@ -267,8 +278,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t w_addr = smem_u32(ring_w + sw * kTnWBytes);
           const uint32_t x_addr = smem_u32(ring_x + sx * kTnXBytes);
 #pragma unroll
-          for (int k = 0; k < kKBytes / 32; ++k)
-            mma_f16(d_tmem, smem_desc_sw128(w_addr + k * 32), smem_desc_sw128(x_addr + k * 32), idesc, (kb | k) != 0);
+          for (int k = 0; k < kKBytes / 32; ++k) {
+            const uint64_t wd = smem_desc_sw128(w_addr + k * 32), xd = smem_desc_sw128(x_addr + k * 32);
+            if (Q8 == kQF8)
+              mma_f8(d_tmem, wd, xd, idesc, (kb | k) != 0);
+            else if (Q8)
+              mma_i8(d_tmem, wd, xd, idesc, (kb | k) != 0);
+            else
+              mma_f16(d_tmem, wd, xd, idesc, (kb | k) != 0);
+          }
           tc_commit(&emptyW[sw]);
           tc_commit(&emptyX[sx]);
           if (++sw == AST) {
@@ -312,16 +330,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         // gate lanes 0-7 and 16-23 hold features f0 .. f0 + 7 and f0 + 8 .. f0 + 15; lanes 0 and 16
         // gather their group's eight results into one 16-byte store per token
         const bool lead_lane = (lane & 15) == 0;
+        const bool gate_lane = (lane & 8) == 0;
         const int f = nt * 64 + 16 * q + 8 * (lane >> 4) + (lane & 7);
+        // 8-bit kinds: this lane's weight row scale (its gate or up row of feature f)
+        float sb = 1.0f;
+        if (Q8 && f < args.N)
+          sb = args.b_scale[static_cast<size_t>(e) * args.b_scale_rows + (gate_lane ? 0 : args.b_up_offset) + f];
         for (int c0 = 0; c0 < rows; c0 += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
+          // 8-bit kinds: lane l holds the activation scale of token c0 + l
+          const float sa_l = (Q8 && c0 + lane < rows) ? args.a_scale[prow0 + c0 + lane] : 1.0f;
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float mine = __uint_as_float(v[j]);
+            const float sa = Q8 ? __shfl_sync(0xffffffffu, sa_l, j) : 1.0f;
+            const float mine = Q8 ? acc_f32<Q8>(v[j]) * sa * sb : __uint_as_float(v[j]);
             const float other = __shfl_xor_sync(0xffffffffu, mine, 8);
             const float h = silu_mul(mine, other);  // meaningful on the gate lanes
+            if (Q8 && args.row_amax) {  // per stacked row amax of U over this warp's 16 features
+              float m = (gate_lane && f < args.N) ? fabsf(h) : 0.0f;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+              if (lane == 0 && c0 + j < rows)
+                atomicMax(reinterpret_cast<int*>(args.row_amax) + prow0 + c0 + j, __float_as_int(m));
+            }
             const float h1 = __shfl_down_sync(0xffffffffu, h, 1);
             const uint32_t pk0 = Elt<OutT>::pack2(h, h1);
             const uint32_t pk1 = __shfl_down_sync(0xffffffffu, pk0, 2);
@@ -344,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         OutT* out = reinterpret_cast<OutT*>(args.out);
         const int h = nt * kBM + 32 * q + lane;  // output feature of this lane
         const bool lead_lane = (lane & 7) == 0;  // gathers features h .. h + 7 into one 16-byte op
+        const float sb = (Q8 && h < args.N) ? args.b_scale[static_cast<size_t>(e) * args.b_scale_rows + h] : 1.0f;
         for (int c0 = 0; c0 < rows; c0 += 32) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_row + c0, v);
@@ -365,12 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+          if (Q8 && c0 + lane < rows) scale *= args.a_scale[p];  // 8-bit: the token's activation scale
           tmem_ld_wait();
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int row = __shfl_sync(0xffffffffu, dst_row, j);
             const float sc = __shfl_sync(0xffffffffu, scale, j);
-            const float mine = __uint_as_float(v[j]) * sc;
+            const float mine = (Q8 ? acc_f32<Q8>(v[j]) * sb : __uint_as_float(v[j])) * sc;
             const float next = __shfl_down_sync(0xffffffffu, mine, 1);
             // lane 8g collects the f16x2 pairs of lanes 8g, 8g+2, 8g+4, 8g+6: features h .. h + 7
             const uint32_t pk0 = Elt<OutT>::pack2(mine, next);
