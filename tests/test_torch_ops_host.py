@@ -29,3 +29,19 @@ def test_meta_shapes():
     assert tw.shape == (T, k) and tw.dtype == torch.float32 and tid.dtype == torch.int32
     gw, gi = torch.ops.muxi_race_b200.grouped_topk(logits, k, True, 4, 2, None, 2.5)
     assert gw.shape == (T, k) and gi.dtype == torch.int32
+
+
+def test_export_keeps_the_op_as_one_node():
+    """torch.export traces a model that calls the op on meta tensors (no GPU): the op stays one
+    opaque graph node next to the surrounding aten ops."""
+    class Block(torch.nn.Module):
+        def forward(self, x, w13, w2, ids, w):
+            return torch.ops.muxi_race_b200.fused_moe(x, w13, w2, ids, w) * 2
+
+    m = dict(device="meta")
+    args = (torch.empty(64, 256, dtype=torch.float16, **m), torch.empty(8, 256, 256, dtype=torch.float16, **m),
+            torch.empty(8, 256, 128, dtype=torch.float16, **m), torch.empty(64, 2, dtype=torch.int32, **m),
+            torch.empty(64, 2, **m))
+    ep = torch.export.export(Block(), args)
+    targets = [str(n.target) for n in ep.graph.nodes if n.op == "call_function"]
+    assert targets.count("muxi_race_b200.fused_moe.default") == 1, targets
