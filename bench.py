@@ -217,6 +217,8 @@ def bench_ours(args, world, rank, local):
     cfg = CONFIGS[args.config]
     peaks, peak_kind = load_peaks()
     variant = args.variant
+    if cfg.int8 and variant in ("ordered", "router"):
+        raise SystemExit(f"--variant {variant} runs the fp16/bf16 route; {cfg.name} is an int8 configuration")
     q8 = cfg.int8 or variant == "fp8"
 
     w13, w2 = make_weights(cfg, seed=0, device=dev)
