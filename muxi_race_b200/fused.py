@@ -171,10 +171,10 @@ _LOGIT_DTYPES = {torch.float32: _lib.MOE_F32, torch.float16: _lib.MOE_F16, torch
 
 def _check_logits(gating_output: torch.Tensor, T: int, topk: int) -> int:
     _check(gating_output.dim() == 2 and gating_output.shape[0] == T, "gating_output must be [T, E]")
-    _check(gating_output.is_cuda and gating_output.is_contiguous(), "gating_output must be a contiguous CUDA tensor")
     _check(gating_output.dtype in _LOGIT_DTYPES, "gating_output must be fp32, fp16 or bf16")
     E = int(gating_output.shape[1])
     _check(1 <= topk <= min(E, 32), "topk must be in [1, min(E, 32)]")
+    _check(gating_output.is_cuda and gating_output.is_contiguous(), "gating_output must be a contiguous CUDA tensor")
     return E
 
 

@@ -166,3 +166,25 @@ def test_host_pipeline_needs_cuda_tensors():
         HostPipeline(lambda *a: None, [torch.zeros(4)], torch.zeros(4))
     with pytest.raises(ValueError, match="depth"):
         HostPipeline(lambda *a: None, [torch.zeros(4)], torch.zeros(4), depth=0)
+
+
+def test_python_argument_checks_without_a_gpu():
+    """Shape and dtype errors of the Python entry points are reported before any device work."""
+    from muxi_race_b200 import fused_moe, fused_topk
+    from muxi_race_b200.packed import PackedWeights, fused_moe_packed, packed_layout
+
+    x = torch.zeros(16, 64, dtype=torch.float16)
+    w13 = torch.zeros(4, 64, 64, dtype=torch.float16)   # 2I = 64 -> I = 32
+    w2 = torch.zeros(4, 64, 32, dtype=torch.float16)
+    ids = torch.zeros(16, 2, dtype=torch.int32)
+    w = torch.zeros(16, 2)
+    with pytest.raises(ValueError, match="w_down shape"):
+        fused_moe(x, w13, torch.zeros(4, 64, 16, dtype=torch.float16), ids, w)
+    with pytest.raises(ValueError, match="topk_ids and topk_weights"):
+        fused_moe(x, w13, w2, ids, torch.zeros(16, 3))
+    with pytest.raises(ValueError, match="topk"):
+        fused_topk(x, torch.zeros(16, 8), 9)
+    _, total = packed_layout(4, 64, 32, "fp16")
+    p = PackedWeights(torch.zeros(total, dtype=torch.uint8), 4, 64, 32, "fp16")
+    with pytest.raises(ValueError, match="hidden size"):
+        fused_moe_packed(torch.zeros(16, 128, dtype=torch.float16), p, ids, w)
