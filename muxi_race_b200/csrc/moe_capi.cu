@@ -942,6 +942,9 @@ int moe_run_kernel_noalloc(const void* x, const void* gate_w, const void* up_w, 
                            const int32_t* gpo, const int32_t* gidx, void* out, int64_t P, int64_t H, int64_t I,
                            int64_t E, int64_t R, int64_t nblk, int dtype, void* stream) {
   t_last_error.clear();
+  // the sizes are checked before the byte count is formed from them (no wrap-around of P * I)
+  MOE_TRY(check_common(H, I, E, dtype, 8));
+  if (P < 0 || P > (int64_t(1) << 31) - 1) return fail(MOE_ERR_INVALID_ARG, "total_padded_tokens out of range");
   const size_t need = moe_run_kernel_workspace_bytes(P, I, dtype);
   if (need > MOE_NOALLOC_WORKSPACE_BYTES)
     return fail(MOE_ERR_WORKSPACE,

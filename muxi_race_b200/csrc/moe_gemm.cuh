@@ -174,6 +174,12 @@ template <> struct Elt<__half> {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  // max(|lo|, |hi|) of a packed pair, in fp32
+  static __device__ __forceinline__ float amax2(uint32_t v) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+    return fmaxf(fabsf(f.x), fabsf(f.y));
+  }
+  static __device__ __forceinline__ float round(float a) { return __half2float(__float2half_rn(a)); }
   static constexpr bool kBF16 = false;
 };
 template <> struct Elt<__nv_bfloat16> {
@@ -181,6 +187,11 @@ template <> struct Elt<__nv_bfloat16> {
     __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
   }
+  static __device__ __forceinline__ float amax2(uint32_t v) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+    return fmaxf(fabsf(f.x), fabsf(f.y));
+  }
+  static __device__ __forceinline__ float round(float a) { return __bfloat162float(__float2bfloat16_rn(a)); }
   static constexpr bool kBF16 = true;
 };
 
@@ -290,8 +301,10 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
           u1 = __uint_as_float(u[j + 1]);
         }
         const float h0 = silu_mul(g0, u0), h1 = silu_mul(g1, u1);
-        if (Q8 && col0 + j < args.N) amax = fmaxf(amax, fmaxf(fabsf(h0), fabsf(h1)));
         packed[j / 2] = Elt<OutT>::pack2(h0, h1);
+        // the requantisation scale comes from the values as stored (rounded to OutT), the same
+        // values the quantiser then reads
+        if (Q8 && col0 + j < args.N) amax = fmaxf(amax, Elt<OutT>::amax2(packed[j / 2]));
       }
       OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
 #pragma unroll

@@ -349,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float other = __shfl_xor_sync(0xffffffffu, mine, 8);
             const float h = silu_mul(mine, other);  // meaningful on the gate lanes
             if (Q8 && args.row_amax) {  // per stacked row amax of U over this warp's 16 features
-              float m = (gate_lane && f < args.N) ? fabsf(h) : 0.0f;
+              // of the value as stored (rounded to OutT), which the quantiser then reads
+              float m = (gate_lane && f < args.N) ? fabsf(Elt<OutT>::round(h)) : 0.0f;
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
               if (lane == 0 && c0 + j < rows)

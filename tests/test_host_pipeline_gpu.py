@@ -3,9 +3,6 @@ with compute) gives every call the result of a direct ``fused_moe`` on the same 
 token rows and routing per call, more calls than buffer slots, results compared after one final
 synchronize. Tolerance: the fused tests' |a - b| <= 1e-2 + 1e-2 |b| (the top-k combine's atomic
 order differs between runs).
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import pytest
 import torch

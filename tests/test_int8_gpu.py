@@ -40,7 +40,7 @@ def int8_case(cfg, T, dev):
     (MoeConfig("small", 0, 512, 256, 8, 2, torch.float16), 200),
     (MoeConfig("small_bf16", 0, 256, 384, 6, 3, torch.bfloat16), 77),
     (CONFIGS["cfg4"], 512),
-])
+], ids=lambda v: v.name if isinstance(v, MoeConfig) else f"T{v}")
 def test_fused_int8(cuda_device, cfg, T):
     x, w13, w2, w13q, w13s, w2q, w2s, ids, w = int8_case(cfg, T, cuda_device)
     out = fused_moe_int8(x, w13q, w13s, w2q, w2s, ids, w)

@@ -7,9 +7,6 @@ reference operator: relative L2 error <= 1e-1 — e4m3 keeps 3 fraction bits and
 quantises four operands (activations, gate/up weights, the intermediate, down weights), which
 the CPU oracle puts at about 6.5e-2 on the cfg1 case — plus an elementwise sanity bound
 |out - ref| <= 0.2 * max|ref| that catches localised corruption.
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import pytest
 import torch
@@ -49,7 +46,7 @@ def fp8_case(cfg, T, dev):
     (MoeConfig("small_bf16", 0, 256, 384, 6, 3, torch.bfloat16), 77),
     (MoeConfig("two_block_groups", 0, 1024, 512, 4, 2, torch.float16), 1500),
     (CONFIGS["cfg4"], 512),
-])
+], ids=lambda v: v.name if isinstance(v, MoeConfig) else f"T{v}")
 def test_fused_fp8(cuda_device, cfg, T):
     x, w13, w2, w13q, w13s, w2q, w2s, ids, w = fp8_case(cfg, T, cuda_device)
     out = fused_moe_fp8(x, w13q, w13s, w2q, w2s, ids, w)

@@ -5,10 +5,12 @@ only the operator's own tensors, so it cannot hand the operator a scratch buffer
 Stage1 intermediate in the library's static device buffer instead. This test calls it through
 the C ABI twice in a row (different inputs, so the second call runs over the first call's leftover
 buffer contents) and checks each output against the existing ``moe_run_kernel`` entry point with
-a caller-allocated workspace, with the tolerance of the other run_kernel tests
-(|a - b| <= 1e-2 + 1e-2 * |b|). It also checks that a problem too large for the buffer is refused.
+a caller-allocated workspace and against the CPU oracle ``run_kernel_ref_f32`` (the reference's own
+PyTorch operator), with the tolerance of the other run_kernel tests (|a - b| <= 1e-2 + 1e-2 * |b|).
+It also checks that a problem too large for the buffer is refused.
 
-The file name sorts last so that a run stopping at the first failure has run every other test.
+The file name sorts after every other test file (``test_zzzzz_`` > ``test_zzzz_``), so a run that
+stops at the first failure has run every other test before this one.
 """
 import math
 
@@ -17,6 +19,7 @@ import torch
 
 import cases
 from muxi_race_b200 import _lib
+from oracle.moe_ref import run_kernel_ref_f32
 
 pytestmark = pytest.mark.gpu
 RTOL = ATOL = 1e-2
@@ -63,7 +66,10 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_device):
         a, b = out_static.float().cpu(), out_ref.float().cpu()
         assert not torch.isnan(a).any()
         bad = (a - b).abs() > ATOL + RTOL * b.abs()
-        assert int(bad.sum()) == 0, f"seed {seed}: {int(bad.sum())} elements differ"
+        assert int(bad.sum()) == 0, f"seed {seed}: {int(bad.sum())} elements differ from moe_run_kernel"
+        oracle = run_kernel_ref_f32(*[v.cpu() for v in t])
+        bad = (a - oracle).abs() > ATOL + RTOL * oracle.abs()
+        assert int(bad.sum()) == 0, f"seed {seed}: {int(bad.sum())} elements differ from the oracle"
 
 
 def test_noalloc_refuses_problems_larger_than_its_buffer(cuda_device):
