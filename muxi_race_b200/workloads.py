@@ -50,6 +50,10 @@ CONFIGS = {
     # ncu capture holds ~3 GB on the device instead of 24 GB
     "cfg3_e32": MoeConfig("cfg3_e32", 512, 7168, 2048, 32, 8, torch.float16, note="cfg3 shape, 32 experts"),
     "cfg4_e32": MoeConfig("cfg4_e32", 512, 7168, 2048, 32, 8, torch.float16, int8=True, note="cfg4 shape, 32 experts"),
+    # profiling case of the weight-streaming regime: cfg3_t128's ~4 rows per expert with 32 experts
+    # (2.8 GB of weights, still far above L2)
+    "cfg3_t128_e32": MoeConfig("cfg3_t128_e32", 16, 7168, 2048, 32, 8, torch.float16,
+                               note="cfg3_t128 shape, 32 experts"),
 }
 
 

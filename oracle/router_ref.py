@@ -84,5 +84,22 @@ def router_grouped_ref(logits: torch.Tensor, topk: int, n_group: int, topk_group
     inf = torch.full((T,), float("inf"))
     ggap = (gsorted[:, topk_group - 1] - gsorted[:, topk_group]).abs() if topk_group < n_group else inf
     cgap = (csorted[:, topk - 1] - csorted[:, topk]).abs() if topk < topk_group * gs else inf
+    # An exact tie between candidates computed from identical inputs is not a near-tie: any
+    # implementation computes the same score for both and breaks the tie by the lower id. With bf16
+    # logits such ties are frequent. (Expert boundary: same logit and bias; group boundary: the
+    # same two best c values.)
+    b = bias.detach().float().cpu() if bias is not None else torch.zeros(E)
+    if topk < topk_group * gs:
+        cidx = torch.sort(cm, dim=-1, descending=True, stable=True).indices
+        ea, eb = cidx[:, topk - 1], cidx[:, topk]
+        same = (lf.gather(1, ea[:, None]) == lf.gather(1, eb[:, None])).squeeze(1) & (b[ea] == b[eb])
+        cgap = torch.where((cgap == 0) & same, inf, cgap)
+    if topk_group < n_group:
+        go = torch.from_numpy(gorder).long()
+        ga, gb = go[:, topk_group - 1], go[:, topk_group]
+        t2 = top2[..., :2] if gs > 1 else top2[..., :1]
+        ar = torch.arange(T)
+        same = (t2[ar, ga] == t2[ar, gb]).all(-1)
+        ggap = torch.where((ggap == 0) & same, inf, ggap)
     margins = torch.minimum(ggap / gsorted[:, 0].abs().clamp_min(1e-30), cgap / csorted[:, 0].abs().clamp_min(1e-30))
     return w.contiguous(), torch.from_numpy(np.ascontiguousarray(ids)), margins

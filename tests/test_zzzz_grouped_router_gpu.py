@@ -5,10 +5,9 @@ The kernel's sigmoid (CUDA expf) and torch's may differ in the last bit, which c
 candidates whose scores are within rounding of each other; so ids are compared bit for bit on the
 tokens whose selection boundaries are clear (relative margin > 1e-5, checked to be >= 99% of
 them), weights there within rtol 1e-5 / atol 1e-6, and on every token the structural properties
-hold (distinct ids, at most topk_group groups, weights summing to the scale).
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
+hold (distinct ids, at most topk_group groups, weights summing to the scale). A boundary between
+candidates with identical inputs (frequent with bf16 logits) is not a near-tie: both sides compute
+the same score for both and break the tie by the lower id.
 """
 import pytest
 import torch
@@ -19,7 +18,7 @@ from oracle.router_ref import router_grouped_ref
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("E,n_group,topk_group,k", [(256, 8, 4, 8), (64, 4, 2, 6), (96, 3, 3, 5), (33, 33, 5, 3)])
+@pytest.mark.parametrize("E,n_group,topk_group,k", [(256, 8, 4, 8), (64, 4, 2, 6), (96, 3, 3, 5), (33, 11, 5, 3)])
 @pytest.mark.parametrize("with_bias", [False, True])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_grouped_router(cuda_device, E, n_group, topk_group, k, with_bias, dtype):
