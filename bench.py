@@ -420,6 +420,9 @@ def bench_ours(args, world, rank, local):
         "gpu_launches": args.steps * (8 if q8 else 9 if variant == "ordered" else 7),
         "clocks": clock_info,
     }
+    if world == 1 and cfg.name == "cfg3" and variant == "default" and not args.no_north_star:
+        # the 1-GPU denominator of the north star's scaling target (cfg5 on one GPU, same weights)
+        result["north_star_cfg5"] = time_cfg5_strong(args, 1, rank, local, w13, w2)
     if world == 1 and not args.no_cpu_baseline:
         f, dt, n, rows = cpu_sample(cfg, ids.cpu(), tw.cpu(), x.cpu(), budget_s=args.cpu_budget)
         result["cpu_baseline"] = {
@@ -430,6 +433,60 @@ def bench_ours(args, world, rank, local):
     if rank == 0:
         print(json.dumps(result), flush=True)
 
+
+
+# ----------------------------------------------------------------------------- north-star EP case
+def time_cfg5_strong(args, world, rank, local, w13_full=None, w2_full=None):
+    """The north star's expert-parallel case: cfg5 (32768 tokens in total, Zipf(1.1)-skewed routing,
+    H=7168, I=2048, E=256, top-8) split evenly over the ranks (strong scaling). On one GPU the
+    fused call on all 32768 tokens (``w13_full`` / ``w2_full``: cfg3's weights, same shapes). Returns
+    {"ms": max over ranks, "tokens_per_s", "tflops"}; every rank takes the same collective steps."""
+    import muxi_race_b200 as m
+    from muxi_race_b200.workloads import CONFIGS, make_hidden, make_routing, make_weights
+
+    dev = torch.device("cuda", local)
+    cfg = CONFIGS["cfg5"]
+    T_rank = cfg.T // world
+    steps, warm = max(3, min(args.steps, 10)), max(3, args.warmup)
+    x = make_hidden(cfg, seed=1 + rank, device=dev, T=T_rank)
+    ids, tw = make_routing(cfg, seed=2 + rank, device=dev, T=T_rank)
+    if world == 1:
+        out = torch.empty((T_rank, cfg.H), dtype=cfg.dtype, device=dev)
+        fn = lambda: m.fused_moe(x, w13_full, w2_full, ids, tw, out=out)  # noqa: E731
+        moe = None
+    else:
+        from muxi_race_b200.ep import ExpertParallelMoE, ExpertPlacement, PeerMemoryEP
+
+        cal_ids, _ = make_routing(cfg, seed=999, device=dev, T=8192)
+        loads = torch.bincount(cal_ids.flatten().long(), minlength=cfg.E).float().cpu().tolist()
+        placement = ExpertPlacement.balanced(loads, world)
+        w13, w2 = make_weights(cfg, seed=0, device=dev, experts=placement.local_experts(rank))
+        if args.ep_mode == "p2p":
+            moe = PeerMemoryEP(w13, w2, placement, max_tokens=T_rank, topk=cfg.topk, combine=args.ep_combine)
+        else:
+            moe = ExpertParallelMoE(w13, w2, placement, chunks=args.ep_chunks)
+        fn = lambda: moe(x, ids, tw)  # noqa: E731
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(steps):
+        fn()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(s0.elapsed_time(s1) / steps, world)
+    if moe is not None and hasattr(moe, "close"):
+        moe.close()
+    st = m.device_status()
+    assert st == 0, f"device status {st} after the cfg5 strong-scaling measurement"
+    return {"workload": f"cfg5: T={cfg.T} in total ({T_rank} per rank), Zipf({cfg.zipf_s}) routing, "
+                        f"H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
+            "n_gpus": world, "steps": steps, "ms": round(ms, 4), "tokens_per_s": round(cfg.T / (ms * 1e-3)),
+            "tflops": round(cfg.flops() / (ms * 1e-3) / 1e12, 2)}
 
 # ----------------------------------------------------------------------------- expert parallel
 def bench_ep(args, world, rank, local):
@@ -574,6 +631,11 @@ def bench_ep(args, world, rank, local):
     send, recv = moe.last_counts if not p2p else (None, None)
     if p2p:
         moe.close()
+    north = None
+    if not strong and not args.no_north_star:
+        del moe, w13, w2
+        torch.cuda.empty_cache()
+        north = time_cfg5_strong(args, world, rank, local)
 
     if rank == 0:
         print(json.dumps({
@@ -605,6 +667,7 @@ def bench_ep(args, world, rank, local):
             # p2p: stage, 2 barriers, route, local MoE 7, combine = 12
             "gpu_launches": args.steps * ((11 if args.ep_combine == "push" else 12) if p2p else 13 * n_chunks),
             "clocks": clock_info,
+            **({"north_star_cfg5": north} if north else {}),
         }), flush=True)
 
 
@@ -793,6 +856,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of CPU work for cpu_baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-north-star", action="store_true",
+                    help="skip the cfg5 strong-scaling measurement (north-star EP case) added to the default line")
     ap.add_argument("--ep-mode", default="nccl", choices=["p2p", "nccl"],
                     help="expert parallelism: NCCL all-to-all exchange, or over peer memory in the library's kernels")
     ap.add_argument("--ep-combine", default="pull", choices=["pull", "push"],

@@ -373,6 +373,8 @@ static int ep_gather_mode() {
 
 // Unit order (see tile_unit): MOE_B200_UNIT_ORDER = expert (default: an expert's groups side by
 // side per column tile) | group (group-major).
+constexpr int kDefaultWeightsEvictFirst = 0;
+
 int unit_order() {
   static const int v = [] {
     const char* e = getenv("MOE_B200_UNIT_ORDER");
@@ -381,16 +383,38 @@ int unit_order() {
   return v;
 }
 
+// L2 policy of the weight stream: MOE_B200_B_EVICT_FIRST = 0 (evict_normal in both stages), 1
+// (evict_first in both), 2 (evict_first in Stage2 only). Stage2 reads each weight tile once (all
+// blocks of an expert share one unit), while its combine adds every routed row into the token-major
+// output; with evict_first the streamed weights leave L2 first and the output rows stay. Stage1's
+// weight tiles are read by the expert's neighbouring units, whose second reads hit L2.
+int weights_evict_first(int mode) {
+  static const int v = [] {
+    const char* e = getenv("MOE_B200_B_EVICT_FIRST");
+    if (e && strcmp(e, "0") == 0) return 0;
+    if (e && strcmp(e, "1") == 0) return 1;
+    if (e && strcmp(e, "2") == 0) return 2;
+    return kDefaultWeightsEvictFirst;
+  }();
+  return v == 1 || (v == 2 && mode != kStage1) ? 1 : 0;
+}
+// Epilogue slot hand-back: MOE_B200_EPI_RELEASE = late hands the accumulator slot back after the
+// epilogue's stores instead of right after its TMEM reads (comparison runs only).
+int epilogue_late_release() {
+  static const int v = [] {
+    const char* e = getenv("MOE_B200_EPI_RELEASE");
+    return e && strcmp(e, "late") == 0 ? 1 : 0;
+  }();
+  return v;
+}
+
 template <int MODE, typename OutT, int I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
           int EPI = 4>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>;
-  static const int evict_first = [] {
-    const char* v = getenv("MOE_B200_B_EVICT_FIRST");  // experiments: 1 = evict_first for weights
-    return v && strcmp(v, "1") == 0 ? 1 : 0;
-  }();
   GemmArgs args_l = args;
-  args_l.b_evict_first = evict_first;
+  args_l.b_evict_first = weights_evict_first(MODE);
+  args_l.late_release = epilogue_late_release();
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
@@ -411,12 +435,9 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
 template <int MODE, typename OutT, int I8, int AST, int BST, int EPI = 4>
 int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
   auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST, EPI>;
-  static const int evict_first = [] {
-    const char* v = getenv("MOE_B200_B_EVICT_FIRST");
-    return v && strcmp(v, "1") == 0 ? 1 : 0;
-  }();
   GemmArgs args_l = args;
-  args_l.b_evict_first = evict_first;
+  args_l.b_evict_first = weights_evict_first(MODE);
+  args_l.late_release = epilogue_late_release();
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = 1;
   args_l.gu_swap = 0;

@@ -144,6 +144,7 @@ struct GemmArgs {
   // dimension: one box per stage); 1 = tmB0 gate rows and tmB1 up rows, two 2-D boxes per k-block.
   int b_split;
   int gu_swap;                // combined map based at the up rows: the tile holds [up | gate]
+  int late_release;           // epilogue hands the accumulator slot back after its stores (A/B switch)
 
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
@@ -261,12 +262,21 @@ __device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& f
 // ------------------------------------------------------------------ epilogue of one block
 // Columns [c_begin, c_end) of the block's output tile (Stage1: of the BN/2 SiLU*up outputs), in
 // chunks of 32: with 8 epilogue warps two warps share a TMEM lane quadrant, each taking half.
-template <int MODE, typename OutT, int Q8, int BN, int AMODE>
+//
+// Two phases. (1) Every chunk is read from TMEM, finished in registers (dequantisation, SiLU*up
+// or the routing weight) and packed to OutT; then `release()` hands the accumulator slot back to
+// the MMA warp. (2) The packed values are stored (Stage1 U, Stage2Pad) or added into the output
+// (Stage2Comb). The slot is free while the stores and reductions drain, so the next unit's MMAs
+// start as soon as the TMEM reads are done: this matters where a unit occupies every slot (a
+// two-block group of 256 columns fills all 512 TMEM columns).
+template <int MODE, typename OutT, int Q8, int BN, int AMODE, int SPAN, typename Release>
 __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_row, int mb, int nt, int e,
-                                               int row_in_tile, int c_begin, int c_end) {
+                                               int row_in_tile, int c_begin, Release release) {
+  static_assert(SPAN % 32 == 0 && SPAN <= 128, "columns per epilogue thread held in registers");
+  constexpr int kChunks = SPAN / 32;
   const int p = mb * kBM + row_in_tile;  // padded row of this thread
+  uint32_t packed[kChunks][16];
   if (MODE == kStage1) {
-    OutT* U = reinterpret_cast<OutT*>(args.U);
     const int n0 = nt * (BN / 2);
     float sa = 1.0f;
     if (Q8) {
@@ -274,16 +284,16 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       sa = src >= 0 ? args.a_scale[src] : 0.0f;
     }
     float amax = 0.0f;
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; c += 32) {
+    const uint32_t goff = args.gu_swap ? BN / 2 : 0;  // [gate | up] or [up | gate] columns
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      const int c = c_begin + 32 * ch;
       const int col0 = n0 + c;
-      if (col0 >= args.N) break;
+      if (col0 >= args.N) continue;  // warp-uniform
       uint32_t g[32], u[32];
-      const uint32_t goff = args.gu_swap ? BN / 2 : 0;  // [gate | up] or [up | gate] columns
       tmem_ld_32x32b_x32(t_row + goff + c, g);
       tmem_ld_32x32b_x32(t_row + (BN / 2 - goff) + c, u);
       tmem_ld_wait();
-      uint32_t packed[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         float g0, g1, u0, u1;
@@ -300,21 +310,28 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
           u0 = __uint_as_float(u[j]);
           u1 = __uint_as_float(u[j + 1]);
         }
-        const float h0 = silu_mul(g0, u0), h1 = silu_mul(g1, u1);
-        packed[j / 2] = Elt<OutT>::pack2(h0, h1);
+        packed[ch][j / 2] = Elt<OutT>::pack2(silu_mul(g0, u0), silu_mul(g1, u1));
         // the requantisation scale comes from the values as stored (rounded to OutT), the same
         // values the quantiser then reads
-        if (Q8 && col0 + j < args.N) amax = fmaxf(amax, Elt<OutT>::amax2(packed[j / 2]));
+        if (Q8 && col0 + j < args.N) amax = fmaxf(amax, Elt<OutT>::amax2(packed[ch][j / 2]));
       }
+    }
+    if (!args.late_release) release();
+    OutT* U = reinterpret_cast<OutT*>(args.U);
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      const int col0 = n0 + c_begin + 32 * ch;
+      if (col0 >= args.N) continue;
       OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
         if (col0 + v * 8 < args.N)
           *reinterpret_cast<uint4*>(dst + v * 8) =
-              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+              make_uint4(packed[ch][4 * v], packed[ch][4 * v + 1], packed[ch][4 * v + 2], packed[ch][4 * v + 3]);
       }
     }
     if (Q8 && args.row_amax) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
+    if (args.late_release) release();
   } else {
     const int n0 = nt * BN;
     float scale = 0.0f;
@@ -338,21 +355,14 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     }
     float sa = 1.0f;
     if (Q8) sa = args.a_scale[p];
-    OutT* out = reinterpret_cast<OutT*>(args.out);
-    size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
-    if (MODE == kStage2Comb && args.out_regions != nullptr && valid) {  // the token's home rank
-      const int home = token / args.out_T_max;
-      out = reinterpret_cast<OutT*>(args.out_regions[home] + static_cast<uint64_t>(args.out_region_off));
-      orow = static_cast<size_t>(token - home * args.out_T_max);
-    }
-#pragma unroll 1
-    for (int c = c_begin; c < c_end; c += 32) {
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      const int c = c_begin + 32 * ch;
       const int col0 = n0 + c;
-      if (col0 >= args.N) break;
+      if (col0 >= args.N) continue;  // warp-uniform
       uint32_t d[32];
       tmem_ld_32x32b_x32(t_row + c, d);
       tmem_ld_wait();
-      uint32_t packed[16];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
         float d0, d1;
@@ -365,23 +375,33 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
           d0 = __uint_as_float(d[j]);
           d1 = __uint_as_float(d[j + 1]);
         }
-        packed[j / 2] = valid ? Elt<OutT>::pack2(d0 * scale, d1 * scale) : 0u;
-      }
-      if (MODE == kStage2Pad) {
-        OutT* dst = out + orow * args.ldo + col0;
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (col0 + v * 8 < args.N)
-            *reinterpret_cast<uint4*>(dst + v * 8) =
-                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-      } else if (valid) {
-        OutT* dst = out + orow * args.ldo + col0;
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          if (col0 + v * 8 < args.N)
-            red_add_v4(dst + v * 8, make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]));
+        packed[ch][j / 2] = valid ? Elt<OutT>::pack2(d0 * scale, d1 * scale) : 0u;
       }
     }
+    if (!args.late_release) release();
+    OutT* out = reinterpret_cast<OutT*>(args.out);
+    size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
+    if (MODE == kStage2Comb && args.out_regions != nullptr && valid) {  // the token's home rank
+      const int home = token / args.out_T_max;
+      out = reinterpret_cast<OutT*>(args.out_regions[home] + static_cast<uint64_t>(args.out_region_off));
+      orow = static_cast<size_t>(token - home * args.out_T_max);
+    }
+#pragma unroll
+    for (int ch = 0; ch < kChunks; ++ch) {
+      const int col0 = n0 + c_begin + 32 * ch;
+      if (col0 >= args.N || (MODE == kStage2Comb && !valid)) continue;
+      OutT* dst = out + orow * args.ldo + col0;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        if (col0 + v * 8 >= args.N) continue;
+        const uint4 val = make_uint4(packed[ch][4 * v], packed[ch][4 * v + 1], packed[ch][4 * v + 2], packed[ch][4 * v + 3]);
+        if (MODE == kStage2Pad)
+          *reinterpret_cast<uint4*>(dst + v * 8) = val;
+        else
+          red_add_v4(dst + v * 8, val);
+      }
+    }
+    if (args.late_release) release();
   }
 }
 
@@ -687,7 +707,12 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     const int eg = warp >= 7 ? 1 : 0;  // column half (8 epilogue warps)
     constexpr int kCols = MODE == kStage1 ? BN / 2 : BN;
     constexpr int kSpan = kCols / (EPI / 4);
-    const int c_begin = eg * kSpan, c_end = c_begin + kSpan;
+    // columns a thread finishes per block; wider spans (BN = 512, or Stage2 BN = 256 with 4
+    // epilogue warps) are done in passes of 128 columns, the slot released after the last pass
+    // (32 for the 8-bit Stage2, whose per-column dequantisation needs the registers)
+    constexpr int kPassMax = (Q8 && MODE != kStage1) ? 32 : 128;
+    constexpr int kPass = kSpan < kPassMax ? kSpan : kPassMax;
+    const int c_begin = eg * kSpan;
     if (MODE == kStage1 && args.zero_ptr != nullptr) {
       // clear the Stage2 combine target while the first tile's main loop runs
       uint4* z = static_cast<uint4*>(args.zero_ptr);
@@ -715,11 +740,21 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
         tc_fence_after();
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * BN);
-        epilogue_block<MODE, OutT, Q8, BN, AMODE>(args, t_row, fb + j, nt, e, row_in_tile, c_begin, c_end);
-        // hand the slot back to the MMA warp
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty_bar[slot]);
+        // hands the slot back to the MMA warp once this warp's TMEM reads of it are complete
+        auto release = [&]() {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[slot]);
+        };
+        auto keep = []() {};
+#pragma unroll 1
+        for (int c0 = 0; c0 < kSpan; c0 += kPass) {
+          if (c0 + kPass < kSpan)
+            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row_in_tile, c_begin + c0, keep);
+          else
+            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row_in_tile, c_begin + c0,
+                                                             release);
+        }
         ++slot_cnt;
       }
     }

@@ -236,6 +236,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
     const int eg = warp >= 7 ? 1 : 0;  // column half (8 epilogue warps)
     constexpr int kCols = MODE == kStage1 ? kN / 2 : kN;
     constexpr int kSpan = kCols / (EPI / 4);
+    constexpr int kPassMax = (Q8 && MODE != kStage1) ? 32 : 128;  // as in moe_gemm_kernel
+    constexpr int kPass = kSpan < kPassMax ? kSpan : kPassMax;     // columns held in registers per pass
     uint32_t slot_cnt = 0;
     bool ok = true;
     for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
@@ -252,14 +254,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(96 + EPI * 32, 1)
         break;
       }
       tc_fence_after();
+      // hands the slot back to the leader's MMA warp once this warp's TMEM reads are complete
+      auto release = [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[slot]), 0));
+      };
+      auto keep = []() {};
       if (leader || nb == 2) {
         const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(slot * kN);
-        epilogue_block<MODE, OutT, Q8, kN, kATma>(args, t_row, fb + static_cast<int>(rank), nt, e, row_in_tile,
-                                                     eg * kSpan, eg * kSpan + kSpan);
+#pragma unroll 1
+        for (int c0 = 0; c0 < kSpan; c0 += kPass) {
+          if (c0 + kPass < kSpan)
+            epilogue_block<MODE, OutT, Q8, kN, kATma, kPass>(args, t_row, fb + static_cast<int>(rank), nt, e,
+                                                             row_in_tile, eg * kSpan + c0, keep);
+          else
+            epilogue_block<MODE, OutT, Q8, kN, kATma, kPass>(args, t_row, fb + static_cast<int>(rank), nt, e,
+                                                             row_in_tile, eg * kSpan + c0, release);
+        }
+      } else {
+        release();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty_bar[slot]), 0));
     }
   }
 
