@@ -81,6 +81,16 @@ MOE_API int moe_set_profile_events(void* const* events, int n);
  * into whole k-blocks) fall back to the stage's single-CTA default. */
 MOE_API int moe_set_tile(int stage, const char* name);
 
+/* Tuning hook, no reference counterpart (the reference's Stage1 reads the stacked token rows of
+ * its caller). Selects how the fused entry points' Stage1 loads its token rows, for all later
+ * calls in the process: "tma" (a gather kernel stacks the routed rows, TMA boxes read the
+ * stack), "gather" (TMA tile::gather4 loads of the token rows inside Stage1, no stacked copy) or
+ * "lsu" (cp.async gather inside Stage1); NULL or "auto" restores the default. The workspace a
+ * call needs depends on the path (the *_workspace_bytes functions follow the selection), so
+ * switch paths only between calls whose workspaces are sized after the switch. Unknown names
+ * return MOE_ERR_INVALID_ARG. The expert-parallel peer-memory mode always stacks its rows. */
+MOE_API int moe_set_a_path(const char* name);
+
 /* ------------------------------------------------------------------------------------------
  * Reference drop-in: the contest operator.
  * Replaces run_kernel(stacked_expert_tokens, gate_w, up_w, down_w, routed_expert_weights,

@@ -34,6 +34,7 @@ SIGNATURES = {
     "moe_device_status": (_int, [_c_void_p, _int, ctypes.POINTER(ctypes.c_uint32)]),
     "moe_set_profile_events": (_int, [ctypes.POINTER(_c_void_p), _int]),
     "moe_set_tile": (_int, [_int, ctypes.c_char_p]),
+    "moe_set_a_path": (_int, [ctypes.c_char_p]),
     "moe_ep_region_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "moe_ep_region_alloc": (_int, [_size, ctypes.POINTER(_c_void_p)]),
     "moe_ep_region_free": (_int, [_c_void_p]),
@@ -169,6 +170,13 @@ def set_profile_events(events) -> None:
 
 
 _prof_array = None
+
+
+def set_a_path(name) -> None:
+    """Select how the fused entry points' Stage1 loads its token rows for all later calls of the
+    process: "tma" (stacked copy read by TMA boxes), "gather" (TMA tile::gather4 of the token
+    rows inside Stage1) or "lsu"; None or "auto" restores the default."""
+    call("moe_set_a_path", None if name is None else str(name).encode())
 
 
 def set_tile(stage: int, name) -> None:

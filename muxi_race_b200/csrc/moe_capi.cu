@@ -67,7 +67,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   std::atomic<int> sms{0};
   std::atomic<uint32_t*> status{nullptr};
-  std::atomic<uint64_t> attr_done[16] = {};  // bit per kernel whose smem attribute has been raised
+  std::atomic<uint64_t> attr_done[32] = {};  // bit per kernel whose smem attribute has been raised
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -325,14 +325,31 @@ TileCfg tile_cfg(int stage) {
   return static_cast<TileCfg>(v);
 }
 
-// How the A operand is loaded (see AMode): MOE_B200_A_PATH = tma | lsu.
-bool a_path_lsu() {
-  static const bool v = [] {
-    const char* e = getenv("MOE_B200_A_PATH");
-    return e && strcmp(e, "lsu") == 0;
-  }();
+// How Stage1's A operand is loaded (see AMode): MOE_B200_A_PATH = tma (a gather kernel stacks the
+// token rows, TMA boxes read the stack) | lsu (cp.async gather in the GEMM) | gather (TMA
+// tile::gather4 loads of the token rows in the GEMM, no stacked copy). Unset: kDefaultAPath.
+enum APath : int { kAPathTma = 0, kAPathLsu = 1, kAPathGather = 2 };
+constexpr int kDefaultAPath = kAPathTma;
+int parse_a_path(const char* e) {
+  if (e && strcmp(e, "lsu") == 0) return kAPathLsu;
+  if (e && strcmp(e, "gather") == 0) return kAPathGather;
+  if (e && strcmp(e, "tma") == 0) return kAPathTma;
+  return -1;
+}
+// Selected A path: environment at first use, moe_set_a_path afterwards.
+std::atomic<int> g_a_path{-1};
+int a_path() {
+  int v = g_a_path.load(std::memory_order_acquire);
+  if (v < 0) {
+    const int env = parse_a_path(getenv("MOE_B200_A_PATH"));
+    int expected = -1;
+    g_a_path.compare_exchange_strong(expected, env >= 0 ? env : kDefaultAPath, std::memory_order_acq_rel);
+    v = g_a_path.load(std::memory_order_acquire);
+  }
   return v;
 }
+bool a_path_lsu() { return a_path() == kAPathLsu; }
+bool a_path_gather() { return a_path() == kAPathGather; }
 
 // The configuration a stage runs with for reduction length K (elements of elt bytes), given the
 // average number of 128-row blocks per expert: the selected one if any, else the per-call
@@ -356,6 +373,8 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   if (t.tn && (lsu || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
+// Stage1 configurations built for the tile::gather4 A path (single CTA, one weight k-block per box)
+bool gather_cfg(TileCfg c) { return c == kT256A4B5 || c == kT256A4B5E8 || c == kT256x2A3B4 || c == kT256x2A3B4E8; }
 // Peer-memory EP gather: MOE_B200_EP_GATHER = bulk selects gather_rows_peer_bulk_kernel (bulk
 // copies through shared memory), dedup gather_rows_peer_dedup_kernel (each token row read once
 // per rank, stored into all its local slots); unset: the per-route 16-byte load loop.
@@ -384,28 +403,24 @@ int unit_order() {
 }
 
 // L2 policy of the weight stream: MOE_B200_B_EVICT_FIRST = 0 (evict_normal in both stages), 1
-// (evict_first in both), 2 (evict_first in Stage2 only). Stage2 reads each weight tile once (all
-// blocks of an expert share one unit), while its combine adds every routed row into the token-major
-// output; with evict_first the streamed weights leave L2 first and the output rows stay. Stage1's
-// weight tiles are read by the expert's neighbouring units, whose second reads hit L2.
+// (evict_first in both), 2 (evict_first in Stage2 only); unset: kDefaultWeightsEvictFirst. Stage2
+// reads each weight tile once (all blocks of an expert share one unit), while its combine adds
+// every routed row into the token-major output; with evict_first the streamed weights leave L2
+// first and the output rows stay. Stage1's weight tiles are read by the expert's neighbouring
+// units, whose second reads hit L2. Read at each launch (a tuning switch: comparisons can flip it
+// between calls of one process).
 int weights_evict_first(int mode) {
-  static const int v = [] {
-    const char* e = getenv("MOE_B200_B_EVICT_FIRST");
-    if (e && strcmp(e, "0") == 0) return 0;
-    if (e && strcmp(e, "1") == 0) return 1;
-    if (e && strcmp(e, "2") == 0) return 2;
-    return kDefaultWeightsEvictFirst;
-  }();
+  const char* e = getenv("MOE_B200_B_EVICT_FIRST");
+  int v = kDefaultWeightsEvictFirst;
+  if (e && (strcmp(e, "0") == 0 || strcmp(e, "1") == 0 || strcmp(e, "2") == 0)) v = e[0] - '0';
   return v == 1 || (v == 2 && mode != kStage1) ? 1 : 0;
 }
 // Epilogue slot hand-back: MOE_B200_EPI_RELEASE = late hands the accumulator slot back after the
-// epilogue's stores instead of right after its TMEM reads (comparison runs only).
+// epilogue's stores instead of right after its TMEM reads (comparison runs only; read at each
+// launch).
 int epilogue_late_release() {
-  static const int v = [] {
-    const char* e = getenv("MOE_B200_EPI_RELEASE");
-    return e && strcmp(e, "late") == 0 ? 1 : 0;
-  }();
-  return v;
+  const char* e = getenv("MOE_B200_EPI_RELEASE");
+  return e && strcmp(e, "late") == 0 ? 1 : 0;
 }
 
 template <int MODE, typename OutT, int I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
@@ -419,8 +434,8 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
   if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 3 + AMODE;
-  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma, KPB>::kSmemBytes;
+  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 4 + AMODE;
+  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
@@ -442,7 +457,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = 1;
   args_l.gu_swap = 0;
   args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 3;
+  const int bit = 1024 + (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 2;
   constexpr int smem = PairRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   static int max_pairs[kMaxDevices] = {};
@@ -499,7 +514,7 @@ template <int MODE, typename OutT, int Q8>
 int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t stream) {
   constexpr int AST = 6, BST = 4;
   auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST, Q8>;
-  const int bit = ((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + Q8) * kNumTileCfg * 3 + tcfg * 3 + 2;
+  const int bit = 1024 + (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + Q8) * kNumTileCfg + tcfg) * 2 + 1;
   constexpr int smem = TnRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
@@ -596,6 +611,30 @@ int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, i
     }
   }
   return fail(MOE_ERR_UNSUPPORTED, "tile configuration %s is not available for this stage", kTiles[c].name);
+}
+
+// Stage1 with the tile::gather4 A path (configurations of gather_cfg).
+template <typename OutT, int I8>
+int launch_stage1_gather(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles,
+                         cudaStream_t stream) {
+  switch (c) {
+    case kT256A4B5:
+      return launch_gemm<kStage1, OutT, I8, 256, 1, 4, 5, kATmaGather, 1, 1>(dev, c, m, args, max_tiles, stream);
+    case kT256A4B5E8:
+      return launch_gemm<kStage1, OutT, I8, 256, 1, 4, 5, kATmaGather, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+    case kT256x2A3B4:
+      return launch_gemm<kStage1, OutT, I8, 256, 2, 3, 4, kATmaGather, 1, 1>(dev, c, m, args, max_tiles, stream);
+    case kT256x2A3B4E8:
+      return launch_gemm<kStage1, OutT, I8, 256, 2, 3, 4, kATmaGather, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+    default:
+      return fail(MOE_ERR_UNSUPPORTED, "tile configuration %s is not built for the gather4 A path", kTiles[c].name);
+  }
+}
+template <int I8>
+int launch_stage1_gather_rt(int dtype, TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, int max_tiles,
+                            cudaStream_t stream) {
+  return dtype == MOE_F16 ? launch_stage1_gather<__half, I8>(c, dev, m, args, max_tiles, stream)
+                          : launch_stage1_gather<__nv_bfloat16, I8>(c, dev, m, args, max_tiles, stream);
 }
 
 // Stage dispatch over the runtime element type and A path.
@@ -809,6 +848,14 @@ int moe_set_tile(int stage, const char* name) {
   }
   for (int st = 1; st <= 2; ++st)
     if (stage == 0 || stage == st) g_tile_sel[st - 1].store(static_cast<int>(c), std::memory_order_release);
+  return MOE_OK;
+}
+
+int moe_set_a_path(const char* name) {
+  t_last_error.clear();
+  const int v = name == nullptr || strcmp(name, "auto") == 0 ? kDefaultAPath : parse_a_path(name);
+  if (v < 0) return fail(MOE_ERR_INVALID_ARG, "unknown A path '%s' (tma, gather, lsu)", name);
+  g_a_path.store(v, std::memory_order_release);
   return MOE_OK;
 }
 
@@ -1054,7 +1101,7 @@ int moe_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t bm, 
 size_t moe_fused_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, false, a_path_lsu()).total;
+  return fused_layout(T, topk, E, H, I, false, a_path_lsu() || a_path_gather()).total;
 }
 
 // Expert parallelism over peer memory: token rows come from the ranks' regions (route r = (s *
@@ -1096,10 +1143,12 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (!aligned16(x) || !aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "hidden_states/out must be 16-byte aligned");
   if (peer && int8) return fail(MOE_ERR_UNSUPPORTED, "the int8 route has no peer-memory expert-parallel mode");
   const bool lsu = a_path_lsu() && !peer;
+  // tile::gather4 A path: Stage1 reads the token rows in place (peer mode stages them itself)
+  const bool gather = a_path_gather() && !peer;
   if (ordered && (int8 || peer)) return fail(MOE_ERR_UNSUPPORTED, "the ordered combine is for the fp16/bf16 route");
   if (fp8 && !int8) return fail(MOE_ERR_INVALID_ARG, "fp8 is an 8-bit route");
   if (fp8 && lsu) return fail(MOE_ERR_UNSUPPORTED, "the fp8 route runs on the TMA A path (MOE_B200_A_PATH=tma)");
-  const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu, ordered);
+  const FusedLayout L = fused_layout(T, topk, E, H, I, int8, lsu || gather, ordered);
   if (!workspace || workspace_bytes < L.total) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", L.total);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
 
@@ -1127,7 +1176,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   // expected blocks per expert: routes per expert / 128, plus half a block of padding (peer mode:
   // about 1 / W of the virtual routes land on this rank)
   const double bpe = static_cast<double>(R) / (peer ? peer->W : 1) / static_cast<double>(E) / kBM + 0.5;
-  const TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe), tc2 = usable_cfg(2, I, elt, lsu, bpe);
+  TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe);
+  const TileCfg tc2 = usable_cfg(2, I, elt, lsu, bpe);
+  if (gather && !gather_cfg(tc1)) tc1 = kDefaultTile1;
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   if (peer && peer->push && t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no push combine");
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
@@ -1157,11 +1208,17 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   const int gblocks = sms * 4;
   float* amax = int8 ? reinterpret_cast<float*>(ws + L.amax) : nullptr;
   float* xscale = int8 ? reinterpret_cast<float*>(ws + L.xscale) : nullptr;
-  if (lsu) {
-    if (int8) {
-      if (dtype == MOE_F16)
+  if (lsu || gather) {
+    if (int8) {  // quantised per token, once (each token's k routes share its row and scale)
+      if (dtype == MOE_F16 && fp8)
+        quantize_rows_q8_kernel<__half, kQF8><<<gblocks, 256, 0, s>>>(
+            static_cast<const __half*>(x), T, (int)H, nullptr, nullptr, static_cast<int8_t*>(xs), xscale);
+      else if (dtype == MOE_F16)
         quantize_rows_q8_kernel<__half><<<gblocks, 256, 0, s>>>(static_cast<const __half*>(x), T, (int)H, nullptr,
                                                                 nullptr, static_cast<int8_t*>(xs), xscale);
+      else if (fp8)
+        quantize_rows_q8_kernel<__nv_bfloat16, kQF8><<<gblocks, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(x), T, (int)H, nullptr, nullptr, static_cast<int8_t*>(xs), xscale);
       else
         quantize_rows_q8_kernel<__nv_bfloat16><<<gblocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), T,
                                                                        (int)H, nullptr, nullptr,
@@ -1243,7 +1300,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   prof_record(2, s);
 
   // 3. Stage1 (gate/up GEMM + SiLU*up) and 4. Stage2 (down GEMM * topk weight, combine)
-  const void* a1_src = lsu ? (int8 ? static_cast<const void*>(xs) : x) : xs;
+  const void* a1_src = (lsu || gather) ? (int8 ? static_cast<const void*>(xs) : x) : xs;
   void* a2_src = int8 ? (void*)(ws + L.uq) : U;
   StageMaps m1, m2;
   const uint8_t* w13b = static_cast<const uint8_t*>(w13);
@@ -1261,6 +1318,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     m1.a = m1.a1 = m1.b0;
     m2.a = m2.a1 = m2.b0;
     if (ordered) MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
+  } else if (gather) {  // Stage1: the token rows themselves, boxes one row high (tile::gather4)
+    MOE_TRY(make_tmap(&m1.a, a1_src, elt, T, H, 1, "hidden_states (gather4)"));
+    m1.a1 = m1.a;
+    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
   } else {
     MOE_TRY(make_a_maps(&m1, xs, elt, L.P_max, H, t1.pair ? 1 : gmax1, "gathered hidden_states"));
     MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
@@ -1291,8 +1352,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a1.sorted_route_ids = sorted;
   a1.R = (int)R;
   a1.topk = (int)topk;
-  a1.zero_ptr = lsu && !ordered ? out : nullptr;
-  a1.zero_bytes = lsu && !ordered ? T * H * 2 : 0;
+  a1.zero_ptr = (lsu || gather) && !ordered ? out : nullptr;
+  a1.zero_bytes = (lsu || gather) && !ordered ? T * H * 2 : 0;
 
   GemmArgs a2{};
   a2.K = (int)I;
@@ -1351,6 +1412,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       t.U = U;
       t.ldu = (int)I;
       MOE_TRY(launch_tn_rt<kStage1>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s));
+    } else if (gather) {
+      MOE_TRY(launch_stage1_gather_rt<kQ16>(dtype, tc1, dev, m1, a1, max_tiles1, s));
     } else {
       MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
     }
@@ -1420,6 +1483,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
         t.b_up_offset = (int)I;
         t.row_amax = amax;
         MOE_TRY((launch_tn_rt<kStage1, Q>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s)));
+      } else if (gather) {
+        MOE_TRY(launch_stage1_gather_rt<Q>(dtype, tc1, dev, m1, a1, max_tiles1, s));
       } else if constexpr (Q == kQF8) {
         MOE_TRY((launch_stage_rt<kStage1, kQF8, kATma>(dtype, false, tc1, dev, m1, a1, max_tiles1, s)));
       } else {
@@ -1476,7 +1541,7 @@ int moe_fused(const void* x, const void* w13, const void* w2, const void* ids, i
 size_t moe_fused_ordered_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, false, a_path_lsu(), true).total;
+  return fused_layout(T, topk, E, H, I, false, a_path_lsu() || a_path_gather(), true).total;
 }
 
 int moe_fused_ordered(const void* x, const void* w13, const void* w2, const void* ids, int ids_dtype, const void* tw,
@@ -1536,7 +1601,7 @@ int moe_quantize_rows_fp8(const void* w, int dtype, int64_t rows, int64_t cols, 
 size_t moe_fused_int8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, true, a_path_lsu()).total;
+  return fused_layout(T, topk, E, H, I, true, a_path_lsu() || a_path_gather()).total;
 }
 
 int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, const void* w2_q, const float* w2_scale,
@@ -1550,7 +1615,7 @@ int moe_fused_int8(const void* x, const void* w13_q, const float* w13_scale, con
 size_t moe_fused_fp8_workspace_bytes(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t I, int dtype) {
   (void)dtype;
   if (T <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
-  return fused_layout(T, topk, E, H, I, true, false).total;
+  return fused_layout(T, topk, E, H, I, true, a_path_gather()).total;
 }
 
 int moe_fused_fp8(const void* x, const void* w13_q, const float* w13_scale, const void* w2_q, const float* w2_scale,

@@ -150,18 +150,26 @@ struct GemmArgs {
 };
 
 // How the A operand reaches shared memory:
-//   kATma     one TMA box per block (rows = padded rows of the A tensor map)
-//   kALsu     cp.async by a producer warp, row p of a_ptr
-//   kAGather  cp.async by a producer warp, row sorted_route_ids[p] / topk of a_ptr: each routed
-//             row reads its token row directly (no stacked copy); padding rows are zero-filled
+//   kATma        one TMA box per block (rows = padded rows of the A tensor map)
+//   kALsu        cp.async by a producer warp, row p of a_ptr
+//   kAGather     cp.async by a producer warp, row sorted_route_ids[p] / topk of a_ptr: each routed
+//                row reads its token row directly (no stacked copy); padding rows are zero-filled
+//   kATmaGather  TMA tile::gather4 loads from a tensor map over the token rows: lane l of the
+//                producer warp fetches padded rows 4l..4l+3 of a block (token rows
+//                sorted_route_ids[p] / topk; padding rows read token row 0, whose products are
+//                never stored), 32 loads per block and k-block; no stacked copy, and the rows of
+//                a 128-row block land in the same 128B-swizzled tile as one TMA box would give
 // The LSU warp maps 8 lanes to the eight 16-byte chunks of one 128-byte row segment, so every
 // instruction moves four whole segments; it is a second load path next to the TMA unit.
-enum AMode : int { kATma = 0, kALsu = 1, kAGather = 2 };
+enum AMode : int { kATma = 0, kALsu = 1, kAGather = 2, kATmaGather = 3 };
+
+// A modes whose producer writes shared memory with cp.async (generic proxy) and a row table
+__host__ __device__ constexpr bool a_mode_lsu(int amode) { return amode == kALsu || amode == kAGather; }
 
 // Source row of padded row p for the A operand, -1 for padding.
 template <int AMODE>
 __device__ __forceinline__ long long a_source_row(const GemmArgs& args, int p) {
-  if (AMODE == kAGather) {
+  if (AMODE == kAGather || AMODE == kATmaGather) {
     const int route = args.sorted_route_ids[p];
     return (route >= 0 && route < args.R) ? static_cast<long long>(route / args.topk) : -1;
   }
@@ -420,7 +428,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
                     const GemmArgs args) {
-  using RingT = Ring<BN, GMAX, AST, BST, CPS, AMODE != kATma, KPB>;
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>;
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kBKBytes = RingT::kBKBytes;
@@ -451,7 +459,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < AST; ++s) {
-      mbar_init(&fullA[s], AMODE == kATma ? 1 : 32);  // TMA: expect_tx arrive; LSU: one per lane
+      mbar_init(&fullA[s], a_mode_lsu(AMODE) ? 32 : 1);  // TMA: expect_tx arrive; LSU: one per lane
       mbar_init(&emptyA[s], 1);
     }
     for (int s = 0; s < BST; ++s) {
@@ -467,7 +475,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if (AMODE == kATma) {
+    if (!a_mode_lsu(AMODE)) {
       tma_prefetch_desc(&tmA);
       if (GMAX > 1) tma_prefetch_desc(&tmA1);
     }
@@ -550,7 +558,57 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     // TMA from lane 0 (kATma; a full group as one box) or cp.async from all 32 lanes (LSU paths),
     // one k-block per stage, up to AST stages ahead. L2 policy evict_last: every column tile of
     // the group re-reads these rows.
-    if (AMODE != kATma || lane == 0) {
+    if (AMODE == kATmaGather) {
+      // Every lane: its four padded rows of each block of the unit as token rows, then per
+      // k-block lane 0 arms the stage with the group's bytes and each lane issues one gather4 per
+      // block (4 rows x 128 bytes at byte 512 * lane of the block's tile). The 128B swizzle is a
+      // function of the shared-memory address, so the 32 pieces form the same tile as a 128-row
+      // box (the 8-row swizzle atoms are 1024-byte aligned; a piece is half an atom).
+      const uint64_t pol = l2_policy_evict_last();
+      int st = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      int par[AST];
+#pragma unroll
+      for (int s = 0; s < AST; ++s) par[s] = -1;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int fb, nb, nt, e;
+        if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        int rows[GMAX][4];
+#pragma unroll
+        for (int j = 0; j < GMAX; ++j)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const long long src = j < nb ? a_source_row<AMODE>(args, (fb + j) * kBM + 4 * lane + i) : -1;
+            rows[j][i] = src >= 0 ? static_cast<int>(src) : 0;
+          }
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const bool got = __all_sync(0xffffffffu, mbar_wait(&emptyA[st], ph ^ 1u, abort_flag, args.status));
+          if (!got) {
+            ok = false;
+            break;
+          }
+          if (lane == 0) mbar_arrive_expect_tx(&fullA[st], static_cast<uint32_t>(nb * kABytes));
+          __syncwarp();
+          const int kx = kb * kKElems;
+#pragma unroll
+          for (int j = 0; j < GMAX; ++j)
+            if (j < nb)
+              tma_gather4(stage_a(st, j) + lane * 4 * kKBytes, &tmA, &fullA[st], kx, rows[j][0], rows[j][1],
+                          rows[j][2], rows[j][3], pol);
+          par[st] = static_cast<int>(ph);
+          if (++st == AST) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Drain: a phase completes only when every lane's loads of it have landed
+      if (lane == 0)
+        for (int s = 0; s < AST; ++s)
+          if (par[s] >= 0) mbar_wait_drain(&fullA[s], static_cast<uint32_t>(par[s]));
+      __syncwarp();
+    } else if (AMODE != kATma || lane == 0) {
       const uint64_t pol = l2_policy_evict_last();
       const long long a_k_bytes = static_cast<long long>(args.K) * (Q8 ? 1 : 2);
       int st = 0;
@@ -656,7 +714,7 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
             break;
           }
           tc_fence_after();
-          if (AMODE != kATma) fence_proxy_async_smem();  // A arrived through the generic proxy
+          if (a_mode_lsu(AMODE)) fence_proxy_async_smem();  // A arrived through the generic proxy
           const uint32_t b_addr = smem_u32(stage_b(sb)) + static_cast<uint32_t>(kk * kBKBytes);
 #pragma unroll
           for (int j = 0; j < GMAX; ++j) {

@@ -101,6 +101,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// Four rows of a 2-D tensor map whose box is one row high (tile::gather4): rows y0..y3 from column
+// x land one after another at dst (4 x the box's row bytes), completing on `bar`.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y0, int y1,
+                                            int y2, int y3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "l"(policy)
+      : "memory");
+}
 // 3-D and 4-D tiled loads: one box spans several 128-byte k-blocks and/or the gate and up halves
 // of a weight tile, so fewer, larger TMA operations carry the same bytes.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,

@@ -188,3 +188,19 @@ def test_python_argument_checks_without_a_gpu():
     p = PackedWeights(torch.zeros(total, dtype=torch.uint8), 4, 64, 32, "fp16")
     with pytest.raises(ValueError, match="hidden size"):
         fused_moe_packed(torch.zeros(16, 128, dtype=torch.float16), p, ids, w)
+
+
+def test_a_path_selection_sizes_the_workspace():
+    """The gather4 A path reads token rows in place: no stacked copy in the workspace."""
+    lib = _lib.lib()
+    args = (4096, 8, 256, 7168, 2048, _lib.MOE_F16)
+    try:
+        _lib.set_a_path("tma")
+        stacked = lib.moe_fused_workspace_bytes(*args)
+        _lib.set_a_path("gather")
+        in_place = lib.moe_fused_workspace_bytes(*args)
+        assert stacked - in_place >= 65280 * 7168 * 2  # the [P_max, H] stacked rows
+        with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
+            _lib.set_a_path("no-such-path")
+    finally:
+        _lib.set_a_path(None)
