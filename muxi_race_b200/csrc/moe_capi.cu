@@ -288,8 +288,6 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
     {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
     {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8}, {"tn", 256, 1, 6, 4, 1, 1, 0, 4, 1},
 };
-// raise_smem bits: ((mode 0..2 x bf16 x operand kind 0..2) x tile x A path), 54 per tile
-static_assert(kNumTileCfg * 54 <= 64 * 16, "smem attribute bits");
 
 // Defaults, measured on B200. Stage1: 256a4b5e8 (single CTA, 8 epilogue warps: the SiLU*up
 // epilogue no longer holds up the next unit; cfg2 Stage1 0.52 vs 0.60-0.73 ms). Stage2, chosen per
@@ -402,6 +400,20 @@ int unit_order() {
   return v;
 }
 
+// Bit of a kernel instantiation in the per-device "shared-memory attribute raised" mask: one
+// range for moe_gemm_kernel (mode x element type x operand kind x configuration x A mode), one
+// after it for the CTA-pair and operand-swapped kernels; the ranges must not overlap.
+constexpr int kSmemKinds = 3 * 2 * 3;  // stage mode x 16-bit element type x operand kind
+constexpr int kSmemBitsGemm = kSmemKinds * kNumTileCfg * 4;
+constexpr int kSmemBitsOther = kSmemKinds * kNumTileCfg * 2;
+static_assert(kSmemBitsGemm + kSmemBitsOther <= 64 * 32, "attr_done holds 32 words of bits");
+constexpr int smem_bit_gemm(int mode, bool bf16, int q8, int tcfg, int amode) {
+  return (((mode * 2 + (bf16 ? 1 : 0)) * 3 + q8) * kNumTileCfg + tcfg) * 4 + amode;
+}
+constexpr int smem_bit_other(int mode, bool bf16, int q8, int tcfg, int which) {
+  return kSmemBitsGemm + (((mode * 2 + (bf16 ? 1 : 0)) * 3 + q8) * kNumTileCfg + tcfg) * 2 + which;
+}
+
 // L2 policy of the weight stream: MOE_B200_B_EVICT_FIRST = 0 (evict_normal in both stages), 1
 // (evict_first in both), 2 (evict_first in Stage2 only); unset: kDefaultWeightsEvictFirst. Stage2
 // reads each weight tile once (all blocks of an expert share one unit), while its combine adds
@@ -434,7 +446,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
   if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 4 + AMODE;
+  const int bit = smem_bit_gemm(MODE, Elt<OutT>::kBF16, I8, tcfg, AMODE);
   constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
@@ -457,7 +469,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.b_split = 1;
   args_l.gu_swap = 0;
   args_l.b1_row_offset = m.b1_row_offset;
-  const int bit = 1024 + (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + I8) * kNumTileCfg + tcfg) * 2;
+  const int bit = smem_bit_other(MODE, Elt<OutT>::kBF16, I8, tcfg, 0);
   constexpr int smem = PairRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   static int max_pairs[kMaxDevices] = {};
@@ -514,7 +526,7 @@ template <int MODE, typename OutT, int Q8>
 int launch_tn(int dev, int tcfg, const TnMaps& m, const TnArgs& args, int max_units, cudaStream_t stream) {
   constexpr int AST = 6, BST = 4;
   auto kern = moe_gemm_tn_kernel<MODE, OutT, AST, BST, Q8>;
-  const int bit = 1024 + (((MODE * 2 + (Elt<OutT>::kBF16 ? 1 : 0)) * 3 + Q8) * kNumTileCfg + tcfg) * 2 + 1;
+  const int bit = smem_bit_other(MODE, Elt<OutT>::kBF16, Q8, tcfg, 1);
   constexpr int smem = TnRing<AST, BST>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
