@@ -370,7 +370,8 @@ def bench_ours(args, world, rank, local):
     s1_gbs = s1_bytes / (stages["stage1"] * 1e-3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", f"traffic_{cfg.name}.json")
-    if os.path.exists(tp):
+    # the committed capture is of the default fp16 call: no traffic figure for other variants
+    if os.path.exists(tp) and variant == "default" and not q8:
         with open(tp) as f:
             traffic = json.load(f).get("stage1_dram_bytes_per_launch")
     roofline = {
@@ -378,7 +379,7 @@ def bench_ours(args, world, rank, local):
         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(s1_gbs / peaks["hbm_gbs"], 4),
         "traffic": traffic, "algorithmic_bytes": s1_bytes, "peak_kind": peak_kind,
     }
-    total_bytes = cfg.weight_bytes(active) + cfg.io_bytes()
+    total_bytes = float(active) * 3 * cfg.H * cfg.I * elt + cfg.io_bytes()  # elt: 1 for int8 and fp8
     t_roof_ms = max(flops / (peaks["bf16_tflops"] * 1e12), total_bytes / (peaks["hbm_gbs"] * 1e9)) * 1e3
 
     result = {
