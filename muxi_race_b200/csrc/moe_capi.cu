@@ -296,7 +296,12 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
 // two blocks, a third less shared-memory traffic per output) is fastest (cfg2 Stage2 0.31 vs
 // 0.35 ms); below that, one-block groups would leave half of each pair idle (cfg3 at T = 128:
 // 1.6 vs 1.1 ms) and 256x2a3b4e8 (single CTA, two-block groups sharing one weight stream, 8
-// epilogue warps; cfg4 Stage2 0.83 vs 0.94 ms with 4) is used. MOE_B200_TILE /
+// epilogue warps; cfg4 Stage2 0.83 vs 0.94 ms with 4) is used. With many blocks per expert the
+// single-CTA tile wins again: an expert's several two-block groups read each weight tile at the
+// same time on neighbouring SMs (expert-interleaved unit order), so the second and later reads
+// hit L2 and the pair's shared weight stream saves nothing (cfg5, ~8.5 blocks per expert: Stage2
+// 8.9-9.2 ms single-CTA against 9.8-10.1 ms for the pairs; cfg2, ~2.5: 0.342 against 0.318 ms
+// for the pair). The pair is therefore chosen between 1.8 and 6 blocks per expert. MOE_B200_TILE /
 // MOE_B200_TILE1 / MOE_B200_TILE2 or moe_set_tile override the choice with a configuration name.
 TileCfg parse_tile(const char* v, TileCfg dflt) {
   if (v)
@@ -305,7 +310,7 @@ TileCfg parse_tile(const char* v, TileCfg dflt) {
   return dflt;
 }
 constexpr TileCfg kDefaultTile1 = kT256A4B5E8, kDefaultTile2 = kT256x2A3B4E8, kDefaultPair = kTP256A6B8;
-constexpr double kPairBlocksPerExpert = 1.8;
+constexpr double kPairBlocksPerExpert = 1.8, kPairBlocksPerExpertMax = 6.0;
 constexpr TileCfg kAuto = kNumTileCfg;
 // Selected configuration per stage (kAuto = per-call choice): environment at first use,
 // moe_set_tile afterwards.
@@ -359,7 +364,8 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   const TileCfg safe = stage == 1 ? kT256A4B5 : kT256x2A3B4;
   TileCfg c = tile_cfg(stage);
   if (c == kAuto) {
-    if (stage == 2 && !lsu && blocks_per_expert >= kPairBlocksPerExpert)
+    if (stage == 2 && !lsu && blocks_per_expert >= kPairBlocksPerExpert &&
+        blocks_per_expert < kPairBlocksPerExpertMax)
       c = kDefaultPair;
     else
       c = stage == 1 ? kDefaultTile1 : kDefaultTile2;
