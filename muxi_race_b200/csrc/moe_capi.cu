@@ -433,6 +433,15 @@ int weights_evict_first(int mode) {
   if (e && (strcmp(e, "0") == 0 || strcmp(e, "1") == 0 || strcmp(e, "2") == 0)) v = e[0] - '0';
   return v == 1 || (v == 2 && mode != kStage1) ? 1 : 0;
 }
+// M = 64 MMAs for an expert's last block when it holds at most 64 valid rows (see half_block):
+// MOE_B200_M64_TAIL = 0 | 1, unset: kDefaultM64Tail. Read at each launch.
+constexpr int kDefaultM64Tail = 0;
+int m64_tail() {
+  const char* e = getenv("MOE_B200_M64_TAIL");
+  if (e && strcmp(e, "0") == 0) return 0;
+  if (e && strcmp(e, "1") == 0) return 1;
+  return kDefaultM64Tail;
+}
 // Epilogue slot hand-back: MOE_B200_EPI_RELEASE = late hands the accumulator slot back after the
 // epilogue's stores instead of right after its TMEM reads (comparison runs only; read at each
 // launch).
@@ -448,6 +457,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   GemmArgs args_l = args;
   args_l.b_evict_first = weights_evict_first(MODE);
   args_l.late_release = epilogue_late_release();
+  args_l.m64_tail = m64_tail();
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = m.b_split;
   args_l.gu_swap = m.gu_swap;
@@ -471,6 +481,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   GemmArgs args_l = args;
   args_l.b_evict_first = weights_evict_first(MODE);
   args_l.late_release = epilogue_late_release();
+  args_l.m64_tail = 0;  // the CTA-pair kernel's MMAs are M = 256
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
   args_l.b_split = 1;
   args_l.gu_swap = 0;
@@ -985,6 +996,7 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a1.b_rows_per_expert = (int)I;
   a1.b1_row_offset = 0;
   a1.group_padded_offsets = gpo;
+  a1.group_sizes = gs;
   a1.U = U;
   a1.ldu = (int)I;
   a1.status = status;
@@ -1358,6 +1370,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a1.b_rows_per_expert = (int)(2 * I);
   a1.b1_row_offset = (int)I;
   a1.group_padded_offsets = gpo;
+  a1.group_sizes = gs;
   a1.U = U;
   a1.ldu = (int)I;
   a1.a_scale = xscale;
@@ -1385,6 +1398,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   a2.nblk = (int)L.nblk_max;
   a2.b_rows_per_expert = (int)H;
   a2.group_padded_offsets = gpo;
+  a2.group_sizes = gs;
   a2.out = out;
   a2.ldo = (int)H;
   a2.routed = tw;

@@ -145,6 +145,7 @@ struct GemmArgs {
   int b_split;
   int gu_swap;                // combined map based at the up rows: the tile holds [up | gate]
   int late_release;           // epilogue hands the accumulator slot back after its stores (A/B switch)
+  int m64_tail;               // blocks with at most 64 valid rows run M = 64 MMAs (needs group_sizes)
 
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
@@ -267,6 +268,18 @@ __device__ __forceinline__ bool tile_unit(const GemmArgs& args, int tile, int& f
   return fb >= 0 && fb + nb <= args.nblk;
 }
 
+// An expert's last block with at most 64 valid rows ("half block") runs M = 64 MMAs: half the
+// tensor-core work of an M = 128 block. Rows 64..127 of such a block are padding. The M = 64
+// accumulator occupies TMEM lanes 0-15 of each 32-lane sub-partition (row r in lane
+// r % 16 + 32 * (r / 16)), so epilogue warp q finds rows 16q..16q+15 in its lanes 0-15 and its
+// lanes 16-31 hold nothing to store. The padded-store Stage2 (which writes zeros to pad rows)
+// keeps M = 128.
+template <int MODE>
+__device__ __forceinline__ bool half_block(const GemmArgs& args, int e, int mb) {
+  if (MODE == kStage2Pad || !args.m64_tail || args.group_sizes == nullptr) return false;
+  return args.group_sizes[e] - (mb * kBM - args.group_padded_offsets[e]) <= kBM / 2;
+}
+
 // ------------------------------------------------------------------ epilogue of one block
 // Columns [c_begin, c_end) of the block's output tile (Stage1: of the BN/2 SiLU*up outputs), in
 // chunks of 32: with 8 epilogue warps two warps share a TMEM lane quadrant, each taking half.
@@ -282,7 +295,9 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
                                                int row_in_tile, int c_begin, Release release) {
   static_assert(SPAN % 32 == 0 && SPAN <= 128, "columns per epilogue thread held in registers");
   constexpr int kChunks = SPAN / 32;
-  const int p = mb * kBM + row_in_tile;  // padded row of this thread
+  // row_in_tile < 0: this lane reads TMEM with its warp but has no row (lanes 16-31 of a half block)
+  const bool has_row = row_in_tile >= 0;
+  const int p = mb * kBM + (has_row ? row_in_tile : 0);  // padded row of this thread
   uint32_t packed[kChunks][16];
   if (MODE == kStage1) {
     const int n0 = nt * (BN / 2);
@@ -329,7 +344,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 #pragma unroll
     for (int ch = 0; ch < kChunks; ++ch) {
       const int col0 = n0 + c_begin + 32 * ch;
-      if (col0 >= args.N) continue;
+      if (col0 >= args.N || !has_row) continue;
       OutT* dst = U + static_cast<size_t>(p) * args.ldu + col0;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
@@ -338,7 +353,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
               make_uint4(packed[ch][4 * v], packed[ch][4 * v + 1], packed[ch][4 * v + 2], packed[ch][4 * v + 3]);
       }
     }
-    if (Q8 && args.row_amax) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
+    if (Q8 && args.row_amax && has_row) atomicMax(reinterpret_cast<int*>(args.row_amax) + p, __float_as_int(amax));
     if (args.late_release) release();
   } else {
     const int n0 = nt * BN;
@@ -355,7 +370,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       }
     } else {
       const int route = args.sorted_route_ids[p];
-      valid = route >= 0 && route < args.R;
+      valid = has_row && route >= 0 && route < args.R;
       if (valid) {
         token = route / args.topk;
         scale = load_weight(args.routed, args.routed_dtype, route);
@@ -683,6 +698,9 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
       const uint32_t idesc = Q8 == kQF8 ? idesc_f8(kBM, kMN)
                              : Q8   ? idesc_i8(kBM, kMN)
                                     : idesc_f16(Elt<OutT>::kBF16, kBM, kMN);
+      const uint32_t idesc64 = Q8 == kQF8 ? idesc_f8(kBM / 2, kMN)
+                               : Q8   ? idesc_i8(kBM / 2, kMN)
+                                      : idesc_f16(Elt<OutT>::kBF16, kBM / 2, kMN);
       int sa = 0, sb = 0;
       uint32_t pa = 0, pb = 0;
       uint32_t slot_cnt = 0;  // accumulator slots handed out so far (slot = cnt % kSlots)
@@ -691,7 +709,10 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
         int fb, nb, nt, e;
         if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
         uint32_t d_tmem[GMAX];
+        uint32_t id_blk[GMAX];  // M = 128, or M = 64 for a half block
         int slot[GMAX];
+#pragma unroll
+        for (int j = 0; j < GMAX; ++j) id_blk[j] = (j < nb && half_block<MODE>(args, e, fb + j)) ? idesc64 : idesc;
 #pragma unroll
         for (int j = 0; j < GMAX; ++j) {
           if (j >= nb || !ok) break;
@@ -728,11 +749,11 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
                 const uint64_t bd = smem_desc_sw128(b_addr + h * (kMN * kKBytes) + k * 32);
                 const uint32_t d = d_tmem[j] + static_cast<uint32_t>(h * kMN);
                 if (Q8 == kQF8)
-                  mma_f8(d, ad, bd, idesc, (kb | k) != 0);
+                  mma_f8(d, ad, bd, id_blk[j], (kb | k) != 0);
                 else if (Q8)
-                  mma_i8(d, ad, bd, idesc, (kb | k) != 0);
+                  mma_i8(d, ad, bd, id_blk[j], (kb | k) != 0);
                 else
-                  mma_f16(d, ad, bd, idesc, (kb | k) != 0);
+                  mma_f16(d, ad, bd, id_blk[j], (kb | k) != 0);
               }
             }
           }
@@ -805,13 +826,14 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
           if (lane == 0) mbar_arrive(&tempty_bar[slot]);
         };
         auto keep = []() {};
+        // a half block's rows 16q..16q+15 sit in lanes 0-15 of quadrant q
+        const int row = half_block<MODE>(args, e, fb + j) ? (lane < 16 ? 16 * q + lane : -1) : row_in_tile;
 #pragma unroll 1
         for (int c0 = 0; c0 < kSpan; c0 += kPass) {
           if (c0 + kPass < kSpan)
-            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row_in_tile, c_begin + c0, keep);
+            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row, c_begin + c0, keep);
           else
-            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row_in_tile, c_begin + c0,
-                                                             release);
+            epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row, c_begin + c0, release);
         }
         ++slot_cnt;
       }
