@@ -653,7 +653,7 @@ def bench_ep(args, world, rank, local):
                                        + ("Stage2 adding into the home ranks' regions (push combine)"
                                           if args.ep_combine == "push" else "loads of the partial outputs")
                                        + " inside the library's kernels, flag barriers; no collectives library; "
-                                       + f"token gather: {os.environ.get('MOE_B200_EP_GATHER') or 'per route'}")
+                                       + f"token gather: {os.environ.get('MOE_B200_EP_GATHER') or 'dedup'}")
                        if p2p else f"NCCL all_to_all_single, {n_chunks} chunk(s)",
                        "l2": "inputs larger than L2 (expert weights streamed per step)"},
             "ms_per_call": round(ms, 4), "tflops_per_gpu": round(flops_total / world / (ms * 1e-3) / 1e12, 2),
@@ -859,8 +859,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-north-star", action="store_true",
                     help="skip the cfg5 strong-scaling measurement (north-star EP case) added to the default line")
-    ap.add_argument("--ep-mode", default="nccl", choices=["p2p", "nccl"],
-                    help="expert parallelism: NCCL all-to-all exchange, or over peer memory in the library's kernels")
+    ap.add_argument("--ep-mode", default="p2p", choices=["p2p", "nccl"],
+                    help="expert parallelism: over peer memory in the library's kernels (default), or NCCL all-to-all")
     ap.add_argument("--ep-combine", default="pull", choices=["pull", "push"],
                     help="peer-memory mode: pull the owners' partial rows after the second barrier, or push them "
                          "from Stage2's epilogue into the home ranks' regions")

@@ -286,11 +286,13 @@ __global__ void __launch_bounds__(kEpBulkWarps * 32)
       return reinterpret_cast<const uint8_t*>(regions[s] + static_cast<uint64_t>(L.x)) + t * row_bytes;
     };
     uint32_t phase[2] = {0u, 0u};
+    bool pending[2] = {false, false};  // a load into the buffer has been issued and not yet seen to land
     long long cur = next_valid(gw);
     int sb = 0;
     if (cur < R) {
       mbar_arrive_expect_tx(&bars[0], row_bytes);
       bulk_load_row(smem_u32(buf), src_of(cur), row_bytes, &bars[0]);
+      pending[0] = true;
     }
     bool ok = true;
     while (cur < R && ok) {
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(kEpBulkWarps * 32)
         bulk_wait_reads();  // the store that last used buffer nb has read it
         mbar_arrive_expect_tx(&bars[nb], row_bytes);
         bulk_load_row(smem_u32(buf + nb * row_bytes), src_of(nxt), row_bytes, &bars[nb]);
+        pending[nb] = true;
       }
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(&bars[sb], phase[sb])) {
@@ -311,15 +314,17 @@ __global__ void __launch_bounds__(kEpBulkWarps * 32)
       }
       if (!ok) break;
       phase[sb] ^= 1u;
+      pending[sb] = false;
       const int slot = route_slot[cur];
       bulk_store_row(xs + static_cast<size_t>(slot) * H, smem_u32(buf + sb * row_bytes), row_bytes);
       cur = nxt;
       sb = nb;
     }
-    // every load issued has landed (bounded) and every store has completed before the CTA exits
+    // after a timeout, wait (bounded) only for the loads still outstanding, then for every store;
+    // a load that has not landed by then leaves xs undefined, which the status word reports
     for (int b = 0; b < 2; ++b) {
       const uint64_t t0 = globaltimer_ns();
-      while (!ok && !mbar_try_wait(&bars[b], phase[b]) && globaltimer_ns() - t0 < MOE_WAIT_NS) {
+      while (pending[b] && !mbar_try_wait(&bars[b], phase[b]) && globaltimer_ns() - t0 < MOE_WAIT_NS) {
       }
     }
     bulk_wait_all();

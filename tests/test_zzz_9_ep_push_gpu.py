@@ -1,11 +1,9 @@
 """GPU: variants of the peer-memory expert-parallel path on one rank, against the oracle
 (|out - ref| <= 1e-2 + 1e-2 |ref|), including a forward with fewer tokens: the push combine
-(Stage2 adds into the home rank's region; home-side zeroing and copy-out), and the deduplicating
-and bulk-copy token gathers (MOE_B200_EP_GATHER=dedup / bulk). The 2-4 GPU version of the push
-combine is ``test_ep_multi_gpu_matches_oracle[p2p_push]``.
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
+(Stage2 adds into the home rank's region; home-side zeroing and copy-out), and the per-route and
+bulk-copy token gathers (MOE_B200_EP_GATHER=route / bulk; the deduplicating gather is the default
+that the other peer-memory tests run). The 2-4 GPU version of the push combine is
+``test_ep_multi_gpu_matches_oracle[p2p_push]``.
 """
 import json
 import multiprocessing as mp
@@ -17,7 +15,7 @@ from test_ep_gpu import _ep_worker, _free_port
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("mode,gather", [("p2p_push", ""), ("p2p", "dedup"), ("p2p_push", "dedup"), ("p2p", "bulk")])
+@pytest.mark.parametrize("mode,gather", [("p2p_push", ""), ("p2p", "route"), ("p2p_push", "route"), ("p2p", "bulk")])
 def test_ep_p2p_variants_single_rank_match_oracle(cuda_device, tmp_path, mode, gather):
     ctx = mp.get_context("spawn")
     port = _free_port()
