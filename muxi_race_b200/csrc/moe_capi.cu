@@ -311,12 +311,6 @@ TileCfg parse_tile(const char* v, TileCfg dflt) {
 }
 constexpr TileCfg kDefaultTile1 = kT256A4B5E8, kDefaultTile2 = kT256x2A3B4E8, kDefaultPair = kTP256A6B8;
 constexpr double kPairBlocksPerExpert = 1.8, kPairBlocksPerExpertMax = 6.0;
-// Stage1 with many blocks per expert: two-block groups (one weight stream per two blocks, L2 ->
-// SM weight bytes halved) beat one-block units, which need a free accumulator slot less often
-// but read each weight tile once per block (cfg5, ~8.5 blocks per expert: Stage1 16.6 vs
-// 17.5 ms). At cfg2-cfg4's 1.5-2.5 blocks per expert the one-block units win (cfg3 2.93 vs 3.08,
-// cfg2 0.545 vs 0.660 ms).
-constexpr double kGroupStage1BlocksPerExpert = 6.0;
 constexpr TileCfg kAuto = kNumTileCfg;
 // Selected configuration per stage (kAuto = per-call choice): environment at first use,
 // moe_set_tile afterwards.
@@ -373,8 +367,6 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
     if (stage == 2 && !lsu && blocks_per_expert >= kPairBlocksPerExpert &&
         blocks_per_expert < kPairBlocksPerExpertMax)
       c = kDefaultPair;
-    else if (stage == 1 && blocks_per_expert >= kGroupStage1BlocksPerExpert)
-      c = kT256x2A3B4E8;
     else
       c = stage == 1 ? kDefaultTile1 : kDefaultTile2;
   }
