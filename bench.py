@@ -610,20 +610,53 @@ def bench_ep(args, world, rank, local):
         tw_d.copy_(tw_h, non_blocking=True)
         out_h.copy_(moe(x_d, ids_d, tw_d), non_blocking=True)
 
-    torch.cuda.synchronize()
-    barrier(world)  # the ranks enter the end-to-end phase together
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e2.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+    def e2e_serial():
+        torch.cuda.synchronize()
+        barrier(world)  # the ranks enter the end-to-end phase together
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return s2.elapsed_time(e2) / args.steps
+
+    def e2e_overlapped():
+        # the same forwards through HostPipeline: uploads and downloads of neighbouring steps on two
+        # copy streams, one pinned host output per buffer slot; every rank submits the same steps
+        from muxi_race_b200.host_pipeline import HostPipeline
+
+        pipe = HostPipeline(lambda xx, ii, ww, oo: oo.copy_(moe(xx, ii, ww)), [x, ids, tw],
+                            torch.empty((T_rank, cfg.H), dtype=cfg.dtype, device=dev))
+        outs_h = [out_h] + [torch.empty_like(out_h).pin_memory() for _ in range(pipe.depth - 1)]
+        torch.cuda.synchronize()
+        barrier(world)
+        for i in range(args.warmup):
+            pipe.submit([x_h, ids_h, tw_h], outs_h[i % pipe.depth])
+        pipe.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s2.record(stream)
+        pipe.up.wait_event(s2)
+        for i in range(args.steps):
+            pipe.submit([x_h, ids_h, tw_h], outs_h[i % pipe.depth])
+        pipe.join(stream)
+        e2.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return s2.elapsed_time(e2) / args.steps
+
+    serial_ms = max_over_ranks(e2e_serial(), world)
+    e2e_ms, e2e_mode = serial_ms, "serial (copy, forward, copy on one stream)"
+    if args.e2e == "overlapped":
+        e2e_ms = max_over_ranks(e2e_overlapped(), world)
+        e2e_mode = "overlapped (HostPipeline: uploads and downloads of consecutive steps on two copy streams)"
     clock_info = clocks.stop() if clocks else None  # sampled across both timed regions
     st = m.device_status()
     assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after timing"
@@ -662,7 +695,9 @@ def bench_ep(args, world, rank, local):
             "rank0_rows": {"send": send, "recv": recv, "local_routes": local_routes, "local_active_experts": local_active},
             "roofline": roofline,
             "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": UNIT, "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "transfers": e2e_mode,
+                    "serial": {"value": round(flops_total / (serial_ms * 1e-3) / 1e12, 2),
+                               "ms_per_step": round(serial_ms, 4)}},
             # per chunk: plan 4 (pair keys + 3 alignment), pack 1, local MoE 7 (3 alignment, block
             # groups, gather, Stage1, Stage2), combine 1
             # p2p: stage, 2 barriers, route, local MoE 7, combine = 12
