@@ -409,14 +409,15 @@ MOE_API int moe_ep_p2p_combine(const uint64_t* regions, int rank, int world, int
                                int64_t hidden, int64_t topk, const int32_t* expert_rank, int64_t num_experts,
                                int dtype, void* out, void* stream);
 
-/* Push combine (alternative to moe_ep_p2p_combine): Stage2's epilogue adds every route's weighted
- * row straight into row t of its token's home rank's y block over NVLink, overlapping the GEMM, and
- * fences at system scope before its kernel ends. Per forward, on one stream:
- *   moe_ep_p2p_stage, moe_ep_p2p_push_prepare (zeroes this rank's y rows [0, T)),
+/* Push combine (alternative to moe_ep_p2p_combine): Stage2's epilogue stores every route's weighted
+ * row into its slot t * k + j of its token's home rank's y block over NVLink, overlapping the GEMM
+ * (plain 16-byte stores: each slot has one writer), and fences at system scope before its kernel
+ * ends. Per forward, on one stream:
+ *   moe_ep_p2p_stage, moe_ep_p2p_push_prepare (argument checks; nothing needs clearing),
  *   moe_ep_p2p_barrier(epoch), moe_ep_p2p_compute_push, moe_ep_p2p_barrier(epoch + 1),
- *   moe_ep_p2p_push_finish (copies this rank's y rows [0, T) to out).
- * Same arguments as moe_ep_p2p_compute / the region layout; the sum order of a token's routes is
- * that of the atomics (the pull combine's is fixed). */
+ *   moe_ep_p2p_push_finish (sums each own token's slots with an expert id in [0, num_experts), in
+ *   slot order, fp32, into out).
+ * Same arguments as moe_ep_p2p_compute / the region layout. */
 MOE_API int moe_ep_p2p_push_prepare(void* own_region, int64_t num_tokens, int64_t max_tokens, int64_t hidden,
                                     int64_t topk, int world, int dtype, void* stream);
 MOE_API int moe_ep_p2p_compute_push(const uint64_t* regions, void* own_region, int rank, int world,
@@ -425,7 +426,7 @@ MOE_API int moe_ep_p2p_compute_push(const uint64_t* regions, void* own_region, i
                                     const void* w13_local, const void* w2_local, int64_t local_experts, int dtype,
                                     void* workspace, size_t workspace_bytes, void* stream);
 MOE_API int moe_ep_p2p_push_finish(const void* own_region, int64_t num_tokens, int64_t max_tokens, int64_t hidden,
-                                   int64_t topk, int world, int dtype, void* out, void* stream);
+                                   int64_t topk, int world, int64_t num_experts, int dtype, void* out, void* stream);
 
 #ifdef __cplusplus
 }

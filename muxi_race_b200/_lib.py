@@ -53,7 +53,7 @@ SIGNATURES = {
                                        _c_void_p, _i64, _c_void_p, _c_void_p, _i64, _int, _c_void_p, _size,
                                        _c_void_p]),
     "moe_ep_p2p_push_prepare": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _int, _int, _c_void_p]),
-    "moe_ep_p2p_push_finish": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _int, _int, _c_void_p, _c_void_p]),
+    "moe_ep_p2p_push_finish": (_int, [_c_void_p, _i64, _i64, _i64, _i64, _int, _i64, _int, _c_void_p, _c_void_p]),
     "moe_run_kernel_workspace_bytes": (_size, [_i64, _i64, _int]),
     "moe_run_kernel": (
         _int,

@@ -9,8 +9,11 @@
 //   x[T_max, H]       rank s's hidden states
 //   ids[T_max, k]     rank s's top-k expert ids (int32)
 //   w[T_max, k]       rank s's top-k weights (fp32)
-//   y[W * T_max, H]   partial outputs rank s computed for every rank's tokens: row q * T_max + t
-//                     = sum over rank s's experts among token (q, t)'s top-k of weight * expert(x)
+//   y[max(W, k) * T_max, H]
+//                     pull combine: partial outputs rank s computed for every rank's tokens, row
+//                     q * T_max + t = sum over rank s's experts among token (q, t)'s top-k of
+//                     weight * expert(x); push combine: row t * k + j = slot j of rank s's own
+//                     token t, stored by the rank that owns that expert
 // A forward on rank s: stage its inputs in its region -> barrier -> route every rank's (token,
 // slot) pairs whose expert it owns onto its local experts (reading the peers' ids and weights),
 // gather those token rows from the peers' x, run the grouped GEMMs, Stage2 combining into its own
@@ -19,12 +22,13 @@
 // Peer data is read with L2-only loads (ld.global.cg); in this (pull) mode nothing but the barrier
 // flags is written to peer memory, and no load uses a tensor map or cluster multicast.
 //
-// Push combine (moe_ep_p2p_compute_push): the home rank s zeroes its y rows [0, T) before the
-// first barrier; Stage2's epilogue on every owner adds each route's weighted row straight into
-// row t of the home rank's y (vector red.add to peer memory, tile by tile, overlapping the GEMM);
+// Push combine (moe_ep_p2p_compute_push): Stage2's epilogue on every owner stores each route's
+// weighted row straight into its slot t * k + j of the home rank's y (16-byte stores to peer
+// memory, tile by tile, overlapping the GEMM; no atomics: every slot has exactly one writer);
 // each epilogue thread fences at system scope before its kernel ends; after the second barrier the
-// home rank's y rows [0, T) are its output (copied out by moe_ep_p2p_push_finish). The pull kernel
-// and its NVLink reads after the second barrier disappear; the sum order is that of the atomics.
+// home rank sums its token's slots locally, in slot order, in fp32 (ep_push_combine_kernel,
+// moe_ep_p2p_push_finish). The pull kernel and its NVLink reads after the second barrier
+// disappear; the routes' rows cross NVLink during the GEMM instead.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -48,7 +52,7 @@ __host__ __device__ inline EpRegion ep_region_layout(long long T_max, long long 
   L.ids = ep_round256(L.x + T_max * H * 2);
   L.w = ep_round256(L.ids + T_max * topk * 4);
   L.y = ep_round256(L.w + T_max * topk * 4);
-  L.total = ep_round256(L.y + W * T_max * H * 2);
+  L.total = ep_round256(L.y + (W > topk ? W : topk) * T_max * H * 2);
   return L;
 }
 
@@ -340,6 +344,53 @@ __global__ void __launch_bounds__(kEpBulkWarps * 32)
     if (!served) continue;
     uint4* dst = y + tok * vecs;
     for (int v = lane; v < vecs; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Push combine, home side: out[t] = sum over token t's slots j whose expert id is in [0, E) (each
+// written by that expert's owner) of y[t * k + j], in slot order, accumulated in fp32. One warp
+// per token, 8 elements per lane step; all of a token's slots are loaded before the sum.
+template <typename T>
+__global__ void ep_push_combine_kernel(const uint8_t* __restrict__ region, EpRegion L, int tokens, int H, int topk,
+                                       int E, T* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const long long warp_id = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const long long n_warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const int vecs = H / 8;
+  const int32_t* ids = reinterpret_cast<const int32_t*>(region + L.ids);
+  const uint4* y = reinterpret_cast<const uint4*>(region + L.y);
+  for (long long t = warp_id; t < tokens; t += n_warps) {
+    const int my_e = lane < topk ? ids[t * topk + lane] : -1;
+    const unsigned valid = __ballot_sync(0xffffffffu, my_e >= 0 && my_e < E);
+    for (int v = lane; v < vecs; v += 32) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (unsigned m0 = valid; m0 != 0u;) {
+        uint4 p[8];
+        int n = 0;
+        unsigned m = m0;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (m == 0u) break;
+          const int j = __ffs(static_cast<int>(m)) - 1;
+          m &= m - 1u;
+          p[u] = y[(t * topk + j) * vecs + v];
+          ++n;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u >= n) break;
+          const T* pe = reinterpret_cast<const T*>(&p[u]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] += static_cast<float>(pe[i]);
+        }
+        m0 = m;
+      }
+      uint4 r;
+      T* re = reinterpret_cast<T*>(&r);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) re[i] = static_cast<T>(acc[i]);
+      reinterpret_cast<uint4*>(out + t * static_cast<long long>(H))[v] = r;
+    }
   }
 }
 

@@ -1966,6 +1966,7 @@ static int ep_p2p_compute(bool push, const uint64_t* regions, void* own_region, 
   MOE_TRY(ep_p2p_check(T_max, H, topk, W));
   if (!regions || !own_region || rank < 0 || rank >= W || !expert_rank || !expert_local || E < 1 || E_local < 1)
     return fail(MOE_ERR_INVALID_ARG, "bad regions/rank/expert tables");
+  if (push && topk > 32) return fail(MOE_ERR_UNSUPPORTED, "the push combine supports topk <= 32");
   const size_t need = moe_ep_p2p_workspace_bytes(T_max, topk, W, E_local, H, I, dtype);
   if (!workspace || workspace_bytes < need) return fail(MOE_ERR_WORKSPACE, "workspace must hold %zu bytes", need);
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail(MOE_ERR_ALIGNMENT, "workspace must be 256-byte aligned");
@@ -2003,33 +2004,43 @@ int moe_ep_p2p_compute_push(const uint64_t* regions, void* own_region, int rank,
                         E_local, dtype, workspace, workspace_bytes, stream);
 }
 
-// Push combine, home side: zero y rows [0, T) of this rank's region (before the first barrier),
-// and copy them out as the forward's output (after the second barrier).
+// Push combine, home side: nothing to prepare (every slot a forward reads is written by its owner
+// in that forward); after the second barrier, sum each own token's slots into out.
 int moe_ep_p2p_push_prepare(void* own_region, int64_t T, int64_t T_max, int64_t H, int64_t topk, int W, int dtype,
                             void* stream) {
   t_last_error.clear();
+  (void)stream;
   MOE_TRY(ep_p2p_check(T_max, H, topk, W));
   if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
   if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
   if (!own_region) return fail(MOE_ERR_INVALID_ARG, "null region");
-  if (T == 0) return MOE_OK;
-  const EpRegion L = ep_region_layout(T_max, H, topk, W);
-  MOE_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(own_region) + L.y, 0, static_cast<size_t>(T) * H * 2,
-                           static_cast<cudaStream_t>(stream)));
   return MOE_OK;
 }
 
-int moe_ep_p2p_push_finish(const void* own_region, int64_t T, int64_t T_max, int64_t H, int64_t topk, int W, int dtype,
-                           void* out, void* stream) {
+int moe_ep_p2p_push_finish(const void* own_region, int64_t T, int64_t T_max, int64_t H, int64_t topk, int W, int64_t E,
+                           int dtype, void* out, void* stream) {
   t_last_error.clear();
   MOE_TRY(ep_p2p_check(T_max, H, topk, W));
   if (dtype != MOE_F16 && dtype != MOE_BF16) return fail(MOE_ERR_INVALID_ARG, "dtype must be MOE_F16 or MOE_BF16");
   if (T < 0 || T > T_max) return fail(MOE_ERR_INVALID_ARG, "num_tokens must be in [0, max_tokens]");
-  if (!own_region || !out) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (E < 1 || E > (int64_t(1) << 30)) return fail(MOE_ERR_INVALID_ARG, "num_experts out of range");
+  if (topk > 32) return fail(MOE_ERR_UNSUPPORTED, "the push combine supports topk <= 32");
   if (T == 0) return MOE_OK;
+  if (!own_region || !out) return fail(MOE_ERR_INVALID_ARG, "null argument");
+  if (!aligned16(out)) return fail(MOE_ERR_ALIGNMENT, "out must be 16-byte aligned");
+  int dev, sms;
+  MOE_TRY(current_device(&dev));
+  MOE_TRY(device_sms(dev, &sms));
   const EpRegion L = ep_region_layout(T_max, H, topk, W);
-  MOE_CUDA(cudaMemcpyAsync(out, static_cast<const uint8_t*>(own_region) + L.y, static_cast<size_t>(T) * H * 2,
-                           cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* region = static_cast<const uint8_t*>(own_region);
+  if (dtype == MOE_F16)
+    ep_push_combine_kernel<__half><<<sms * 8, 256, 0, s>>>(region, L, (int)T, (int)H, (int)topk, (int)E,
+                                                           static_cast<__half*>(out));
+  else
+    ep_push_combine_kernel<__nv_bfloat16><<<sms * 8, 256, 0, s>>>(region, L, (int)T, (int)H, (int)topk, (int)E,
+                                                                  static_cast<__nv_bfloat16*>(out));
+  MOE_CUDA(cudaGetLastError());
   return MOE_OK;
 }
 

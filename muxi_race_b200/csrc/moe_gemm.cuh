@@ -109,8 +109,10 @@ struct GemmArgs {
   // Stage2 output: out [rows or tokens, ldo]
   void* out;
   int ldo;
-  // Stage2Comb into other GPUs' memory (expert parallelism, push combine): token row
-  // s * out_T_max + t is added into row t of (OutT*)(out_regions[s] + out_region_off); NULL: out
+  // Stage2Comb into other GPUs' memory (expert parallelism, push combine): the row of virtual
+  // route r = (s * out_T_max + t) * topk + j is stored (not added) into row t * topk + j of
+  // (OutT*)(out_regions[s] + out_region_off), a per-route slot of token t's home rank s, which
+  // sums its token's slots after the exchange; NULL: out
   const uint64_t* out_regions;
   long long out_region_off;
   int out_T_max;
@@ -360,6 +362,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     float scale = 0.0f;
     bool valid = false;
     int token = 0;
+    int route_id = 0;
     if (MODE == kStage2Pad) {
       const int local = p - args.group_padded_offsets[e];
       valid = local >= 0 && local < args.group_sizes[e];
@@ -373,6 +376,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       valid = has_row && route >= 0 && route < args.R;
       if (valid) {
         token = route / args.topk;
+        route_id = route;
         scale = load_weight(args.routed, args.routed_dtype, route);
       }
     }
@@ -404,10 +408,11 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
     if (!args.late_release) release();
     OutT* out = reinterpret_cast<OutT*>(args.out);
     size_t orow = MODE == kStage2Pad ? static_cast<size_t>(p) : static_cast<size_t>(token);
-    if (MODE == kStage2Comb && args.out_regions != nullptr && valid) {  // the token's home rank
+    const bool push = MODE == kStage2Comb && args.out_regions != nullptr;
+    if (push && valid) {  // this route's slot at the token's home rank
       const int home = token / args.out_T_max;
       out = reinterpret_cast<OutT*>(args.out_regions[home] + static_cast<uint64_t>(args.out_region_off));
-      orow = static_cast<size_t>(token - home * args.out_T_max);
+      orow = static_cast<size_t>(route_id) - static_cast<size_t>(home) * args.out_T_max * args.topk;
     }
 #pragma unroll
     for (int ch = 0; ch < kChunks; ++ch) {
@@ -418,7 +423,7 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
       for (int v = 0; v < 4; ++v) {
         if (col0 + v * 8 >= args.N) continue;
         const uint4 val = make_uint4(packed[ch][4 * v], packed[ch][4 * v + 1], packed[ch][4 * v + 2], packed[ch][4 * v + 3]);
-        if (MODE == kStage2Pad)
+        if (MODE == kStage2Pad || push)
           *reinterpret_cast<uint4*>(dst + v * 8) = val;
         else
           red_add_v4(dst + v * 8, val);

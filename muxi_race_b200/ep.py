@@ -322,10 +322,10 @@ class PeerMemoryEP:
     (collective: the IPC handles are exchanged through ``group``) and call ``forward`` the same
     number of times; ``close`` is collective too.
 
-    ``combine="push"``: instead of the pull after the second barrier, Stage2's epilogue adds each
-    route's weighted row straight into its token's home rank's region over NVLink (overlapping the
-    GEMM); the home zeroes those rows before the first barrier and copies them out after the
-    second. The summation order of a token's routes is then that of the atomics.
+    ``combine="push"``: instead of the pull after the second barrier, Stage2's epilogue stores each
+    route's weighted row into that route's slot in its token's home rank's region over NVLink
+    (overlapping the GEMM; one writer per slot, no atomics); after the second barrier the home sums
+    each token's slots locally in slot order.
     """
 
     def __init__(self, w_gate_up_local: torch.Tensor, w_down_local: torch.Tensor, placement: ExpertPlacement,
@@ -406,7 +406,7 @@ class PeerMemoryEP:
         self._barrier(stream)
         out = torch.empty((T, self.H), dtype=self.dtype, device=self.device)
         if self.push:
-            _lib.call("moe_ep_p2p_push_finish", self._region, T, self.T_max, self.H, self.k, self.world, dt,
+            _lib.call("moe_ep_p2p_push_finish", self._region, T, self.T_max, self.H, self.k, self.world, self.E, dt,
                       out.data_ptr(), stream)
         else:
             _lib.call("moe_ep_p2p_combine", self.regions.data_ptr(), self.rank, self.world, T, self.T_max, self.H,

@@ -129,23 +129,38 @@ def p2p_combine_ref(partials, all_ids, expert_rank, rank, T_max, dtype):
 
 
 def p2p_push_ref(all_x, all_ids, all_w, expert_rank, expert_local, T_max, w13_by_rank, w2_by_rank):
-    """Push combine: every owner o adds, for each virtual route (s, t, j) it owns, weight * expert(x)
-    into row t of home rank s's output (the destination map of the Stage2 epilogue in push mode:
-    virtual token s * T_max + t -> rank s, row t). Returns one [T_s, H] fp32 output per rank."""
+    """Push combine: every owner o stores, for each virtual route r = (s * T_max + t) * k + j it owns,
+    weight * expert(x) into slot t * k + j of home rank s's slot block (the destination map of the
+    Stage2 epilogue in push mode: route r -> rank r // (T_max * k), slot r % (T_max * k)); the home
+    then sums each token's slots j = 0..k-1 whose expert id is valid, in slot order. Returns one
+    [T_s, H] fp32 output per rank and, to check that every slot has exactly one writer, the number
+    of writes per slot of each rank."""
     W = len(all_x)
     k = all_ids[0].shape[1]
     H = all_x[0].shape[1]
-    outs = [torch.zeros((x.shape[0], H), dtype=torch.float32) for x in all_x]
+    E = int(expert_rank.numel())
+    slots = [torch.zeros((T_max * k, H), dtype=torch.float32) for _ in range(W)]
+    writes = [torch.zeros(T_max * k, dtype=torch.int64) for _ in range(W)]
     for o in range(W):
         local = p2p_local_routes_ref(all_ids, expert_rank, expert_local, o, T_max)
         for r in torch.nonzero(local >= 0).flatten().tolist():
-            token = r // k                     # virtual token id s * T_max + t
-            home, t = token // T_max, token % T_max
-            j = r % k
+            home, slot = r // (T_max * k), r % (T_max * k)
+            t, j = slot // k, slot % k
             x = all_x[home][t:t + 1]
             e_local = int(local[r])
             one = torch.zeros((1, 1), dtype=torch.int64)
             w = all_w[home][t:t + 1, j:j + 1].float()
-            outs[home][t] += fused_moe_ref(x, w13_by_rank[o][e_local:e_local + 1], w2_by_rank[o][e_local:e_local + 1],
-                                           one, w)[0]
-    return outs
+            slots[home][slot] = fused_moe_ref(x, w13_by_rank[o][e_local:e_local + 1],
+                                              w2_by_rank[o][e_local:e_local + 1], one, w)[0]
+            writes[home][slot] += 1
+    outs = []
+    for s in range(W):
+        ids = all_ids[s].long()
+        T_s = ids.shape[0]
+        out = torch.zeros((T_s, H), dtype=torch.float32)
+        for t in range(T_s):
+            for j in range(k):
+                if 0 <= int(ids[t, j]) < E:
+                    out[t] += slots[s][t * k + j]
+        outs.append(out)
+    return outs, writes

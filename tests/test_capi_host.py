@@ -155,7 +155,7 @@ def test_peer_memory_ep_host_checks():
     assert rc == -1 and b"regions" in lib.moe_last_error()
     assert lib.moe_ep_p2p_push_prepare(None, T + 1, T, H, k, W, _lib.MOE_F16, None) == -1
     assert lib.moe_ep_p2p_push_prepare(None, 0, T, H, k, W, _lib.MOE_F16, None) == -1  # null region
-    assert lib.moe_ep_p2p_push_finish(None, 4, T, H, k, W, _lib.MOE_F32, None, None) == -1
+    assert lib.moe_ep_p2p_push_finish(None, 4, T, H, k, W, 64, _lib.MOE_F32, None, None) == -1
     assert b"dtype" in lib.moe_last_error()
 
 

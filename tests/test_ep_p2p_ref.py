@@ -38,9 +38,11 @@ def test_p2p_decomposition_matches_oracle():
         ref = fused_moe_ref(xs[r], w13, w2, ids[r], ws[r])
         torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
 
-    # push combine: each owner adds its routes' rows straight into the home rank's output rows
-    pushed = p2p_push_ref(xs, ids, ws, placement.expert_rank, placement.expert_local, T_max,
-                          [w13[placement.local_experts(o)] for o in range(W)],
-                          [w2[placement.local_experts(o)] for o in range(W)])
+    # push combine: each owner stores its routes' rows into per-route slots of the home rank, which
+    # sums its tokens' slots; every slot of a real route has exactly one writer
+    pushed, writes = p2p_push_ref(xs, ids, ws, placement.expert_rank, placement.expert_local, T_max,
+                                  [w13[placement.local_experts(o)] for o in range(W)],
+                                  [w2[placement.local_experts(o)] for o in range(W)])
     for r in range(W):
         torch.testing.assert_close(pushed[r], fused_moe_ref(xs[r], w13, w2, ids[r], ws[r]), rtol=1e-5, atol=1e-5)
+        assert int(writes[r].max()) <= 1 and int(writes[r].sum()) == int(((ids[r] >= 0) & (ids[r] < E)).sum())
