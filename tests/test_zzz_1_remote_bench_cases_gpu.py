@@ -3,9 +3,6 @@
 (one expert, 24 full blocks, I=8192), case 5 (one expert, a single partial block, I=8192) and
 case 6 (one expert, 24 full blocks, I=128); cases 0, 2 and 3 are in test_run_kernel_gpu.py.
 fp32 torch reference on the GPU; tolerance |out - ref| <= 1e-2 + 1e-2 * |ref|, pad rows zero.
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import math
 

@@ -5,9 +5,6 @@ Ids bit-exact (the kernel and the oracle use the same total order: fp32 value, t
 expert id). Weights within rtol 1e-5 / atol 1e-6 of torch's fp32 softmax (the kernel computes
 exp(l - max) over the selected logits with CUDA's expf). The fused output within the fused
 tests' |out - ref| <= 1e-2 + 1e-2 * |ref| of the fp32 reference.
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import pytest
 import torch

@@ -3,9 +3,6 @@
 
 Tolerance as the other fused tests: |out - ref_fp32| <= 1e-2 + 1e-2 * |ref|. Determinism:
 repeated calls on the same inputs give identical bits.
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import os
 

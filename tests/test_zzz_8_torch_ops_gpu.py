@@ -1,9 +1,6 @@
 """GPU: the PyTorch operator registrations (torch.ops.muxi_race_b200.*) run the library's kernels:
 same results as the Python entry points (|a - b| <= 1e-2 + 1e-2 |b| where the atomic combine is
 involved; identical bits for run_kernel and the router).
-
-The file name sorts after the other GPU test files, so a run that stops at the first failure has
-run them all.
 """
 import pytest
 import torch
