@@ -1209,7 +1209,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   // about 1 / W of the virtual routes land on this rank)
   const double bpe = static_cast<double>(R) / (peer ? peer->W : 1) / static_cast<double>(E) / kBM + 0.5;
   TileCfg tc1 = usable_cfg(1, H, elt, lsu, bpe);
-  const TileCfg tc2 = usable_cfg(2, I, elt, lsu, bpe);
+  TileCfg tc2 = usable_cfg(2, I, elt, lsu, bpe);
+  // the push combine runs its Stage2 on the single-CTA kernel: with the CTA-pair kernel it timed
+  // out at the bench's size while the single-CTA form passed its parity tests
+  if (peer && peer->push && kTiles[tc2].pair) tc2 = kDefaultTile2;
   if (gather && !gather_cfg(tc1)) tc1 = kDefaultTile1;
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   if (peer && peer->push && t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no push combine");
