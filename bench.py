@@ -484,10 +484,20 @@ def time_cfg5_strong(args, world, rank, local, w13_full=None, w2_full=None):
         moe.close()
     st = m.device_status()
     assert st == 0, f"device status {st} after the cfg5 strong-scaling measurement"
+    peaks, peak_kind = load_peaks()
+    tflops = cfg.flops() / (ms * 1e-3) / 1e12
+    per_gpu = tflops / world
+    burst = peaks.get("bf16_tflops")
+    sustained = peaks.get("bf16_tflops_sustained")
     return {"workload": f"cfg5: T={cfg.T} in total ({T_rank} per rank), Zipf({cfg.zipf_s}) routing, "
                         f"H={cfg.H} I={cfg.I} E={cfg.E} top-{cfg.topk}",
             "n_gpus": world, "steps": steps, "ms": round(ms, 4), "tokens_per_s": round(cfg.T / (ms * 1e-3)),
-            "tflops": round(cfg.flops() / (ms * 1e-3) / 1e12, 2)}
+            "tflops": round(tflops, 2),
+            # per GPU, against the dense 16-bit tensor peak (the north star's 60% target is of peak)
+            "tensor_peak_frac_per_gpu": {"spec_2250": round(per_gpu / 2250.0, 4),
+                                         "measured_burst": round(per_gpu / burst, 4) if burst else None,
+                                         "measured_sustained": round(per_gpu / sustained, 4) if sustained else None,
+                                         "peak_kind": peak_kind}}
 
 # ----------------------------------------------------------------------------- expert parallel
 def bench_ep(args, world, rank, local):
