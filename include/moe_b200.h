@@ -60,7 +60,8 @@ MOE_API const char* moe_last_error(void);
 
 /* Reads (and with `clear` != 0 resets) the device status word of the current device after
  * synchronising `stream`: bit 0 = a bounded pipeline wait gave up, bit 1 = an expert index
- * outside [0, E) was met, bit 2 = a route index outside [0, R). 0 means every kernel since the
+ * outside [0, E) was met, bit 2 = a route index outside [0, R), bit 3 = the single-kernel MoE's
+ * Stage2 gave up waiting for its rows' Stage1 results. 0 means every kernel since the
  * last clear completed normally. No reference counterpart (the reference has no device-side
  * error reporting). */
 MOE_API int moe_device_status(void* stream, int clear, uint32_t* status_out);
@@ -90,6 +91,18 @@ MOE_API int moe_set_tile(int stage, const char* name);
  * switch paths only between calls whose workspaces are sized after the switch. Unknown names
  * return MOE_ERR_INVALID_ARG. The expert-parallel peer-memory mode always stacks its rows. */
 MOE_API int moe_set_a_path(const char* name);
+
+/* Selects the single-kernel MoE for all later calls in the process (1) or the two stage launches
+ * (0; the default; the environment variable MOE_B200_SINGLE_KERNEL=0|1 sets the initial choice).
+ * The reference fuses nothing across its two stages; its one attempt at a single-kernel MoE is
+ * xpuoj_data/probe_v236_fused_single_kernel.py. The single kernel runs Stage1 and Stage2 of
+ * moe_run_kernel and moe_fused in one cooperative launch: each SM moves on to Stage2 units as
+ * soon as its own Stage1 units are done, and a Stage2 unit waits (bounded; status bit 3 on
+ * timeout) until every Stage1 column tile of its rows has been stored. It applies where both
+ * stages would run their default single-CTA tiles on the TMA path: 16-bit routes without the
+ * ordered combine or expert-parallel peer memory, with no tile forced by moe_set_tile and the
+ * default A path; other calls keep the two launches. Other values return MOE_ERR_INVALID_ARG. */
+MOE_API int moe_set_single_kernel(int on);
 
 /* ------------------------------------------------------------------------------------------
  * Reference drop-in: the contest operator.

@@ -35,6 +35,7 @@ SIGNATURES = {
     "moe_set_profile_events": (_int, [ctypes.POINTER(_c_void_p), _int]),
     "moe_set_tile": (_int, [_int, ctypes.c_char_p]),
     "moe_set_a_path": (_int, [ctypes.c_char_p]),
+    "moe_set_single_kernel": (_int, [_int]),
     "moe_ep_region_bytes": (_size, [_i64, _i64, _i64, _i64]),
     "moe_ep_region_alloc": (_int, [_size, ctypes.POINTER(_c_void_p)]),
     "moe_ep_region_free": (_int, [_c_void_p]),
@@ -177,6 +178,13 @@ def set_a_path(name) -> None:
     process: "tma" (stacked copy read by TMA boxes), "gather" (TMA tile::gather4 of the token
     rows inside Stage1) or "lsu"; None or "auto" restores the default."""
     call("moe_set_a_path", None if name is None else str(name).encode())
+
+
+def set_single_kernel(on: bool) -> None:
+    """Run Stage1 and Stage2 of later run_kernel / fused_moe calls as one cooperative launch
+    (True) or as two launches (False, the default); calls whose tiles or paths the single kernel
+    does not cover keep the two launches."""
+    call("moe_set_single_kernel", 1 if on else 0)
 
 
 def set_tile(stage: int, name) -> None:

@@ -452,6 +452,70 @@ int epilogue_late_release() {
   return e && strcmp(e, "late") == 0 ? 1 : 0;
 }
 
+// Single-kernel MoE (moe_single_kernel, Stage1 and Stage2 in one cooperative launch):
+// MOE_B200_SINGLE_KERNEL = 0 | 1 at first use, moe_set_single_kernel afterwards; unset:
+// kDefaultSingleKernel. Used where both stages run their default single-CTA tiles on the TMA A
+// path (fp16/bf16 routes without the ordered combine or peer memory, no tile forced).
+constexpr int kDefaultSingleKernel = 0;
+std::atomic<int> g_single_kernel{-1};
+int single_kernel() {
+  int v = g_single_kernel.load(std::memory_order_acquire);
+  if (v < 0) {
+    const char* e = getenv("MOE_B200_SINGLE_KERNEL");
+    const int env = e && strcmp(e, "1") == 0 ? 1 : (e && strcmp(e, "0") == 0 ? 0 : kDefaultSingleKernel);
+    int expected = -1;
+    g_single_kernel.compare_exchange_strong(expected, env, std::memory_order_acq_rel);
+    v = g_single_kernel.load(std::memory_order_acquire);
+  }
+  return v;
+}
+// The single kernel's shared-memory attribute bit: the operand-swapped kernel's range at a
+// configuration that kernel never runs with.
+constexpr int smem_bit_single(int mode2, bool bf16) { return smem_bit_other(mode2, bf16, kQ16, kT256A4B5E8, 1); }
+
+template <typename OutT, int MODE2>
+int launch_single(int dev, const StageMaps& m1, const GemmArgs& a1, const StageMaps& m2, const GemmArgs& a2,
+                  int max_tiles1, cudaStream_t stream) {
+  auto kern = moe_single_kernel<OutT, MODE2>;
+  GemmArgs x1 = a1, x2 = a2;
+  for (GemmArgs* x : {&x1, &x2}) {
+    x->late_release = epilogue_late_release();
+    x->m64_tail = m64_tail();
+    x->unit_order = x->group_padded_offsets ? unit_order() : 0;
+  }
+  x1.b_evict_first = weights_evict_first(kStage1);
+  x2.b_evict_first = weights_evict_first(MODE2);
+  x1.b_split = m1.b_split;
+  x1.gu_swap = m1.gu_swap;
+  if (m1.b_split) x1.b1_row_offset = m1.b1_row_offset;
+  x2.b_split = 0;
+  x2.gu_swap = 0;
+  MOE_TRY(raise_smem(dev, smem_bit_single(MODE2, Elt<OutT>::kBF16), kern, kSingleSmemBytes));
+  int sms = 0;
+  MOE_TRY(device_sms(dev, &sms));
+  const int grid = max_tiles1 < sms ? max_tiles1 : sms;
+  if (grid <= 0) return MOE_OK;
+  // cooperative: every CTA is resident at once (a Stage2 unit waits for other CTAs' Stage1 units)
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kSingleThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSingleSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MOE_CUDA(cudaLaunchKernelEx(&cfg, kern, m1.a, m1.b0, m1.b1, m2.a, m2.a1, m2.b0, x1, x2));
+  return MOE_OK;
+}
+template <int MODE2>
+int launch_single_rt(int dtype, int dev, const StageMaps& m1, const GemmArgs& a1, const StageMaps& m2,
+                     const GemmArgs& a2, int max_tiles1, cudaStream_t stream) {
+  if (dtype == MOE_F16) return launch_single<__half, MODE2>(dev, m1, a1, m2, a2, max_tiles1, stream);
+  return launch_single<__nv_bfloat16, MODE2>(dev, m1, a1, m2, a2, max_tiles1, stream);
+}
+
 template <int MODE, typename OutT, int I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
           int EPI = 4>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
@@ -722,7 +786,8 @@ int launch_align(const void* ids, int ids_dtype, int64_t R, int64_t E, int64_t b
 
 // Workspace carving for the token-major paths.
 struct FusedLayout {
-  size_t counts, gs, go, gpo, meta, gidx, groups, tn, sorted, slot, xs, xscale, u, uq, uscale, amax, y, raw, total;
+  size_t counts, gs, go, gpo, meta, gidx, groups, done, tn, sorted, slot, xs, xscale, u, uq, uscale, amax, y, raw,
+      total;
   int64_t P_max, nblk_max;
 };
 
@@ -746,6 +811,7 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.meta = take(sizeof(int) * 4);
   L.gidx = take(sizeof(int) * (size_t)L.nblk_max);
   L.groups = take(sizeof(int) * (size_t)(L.nblk_max + 1));  // block groups + their count
+  L.done = take(sizeof(uint32_t) * (size_t)L.nblk_max);      // single kernel: Stage1 counts per block
   L.tn = take(sizeof(int) * (size_t)(2 * L.nblk_max + 1));   // operand-swapped kernel: entries + count
   L.sorted = take(sizeof(int) * (size_t)L.P_max);
   L.slot = take(sizeof(int) * (size_t)R);
@@ -882,6 +948,13 @@ int moe_set_tile(int stage, const char* name) {
   return MOE_OK;
 }
 
+int moe_set_single_kernel(int on) {
+  t_last_error.clear();
+  if (on != 0 && on != 1) return fail(MOE_ERR_INVALID_ARG, "moe_set_single_kernel takes 0 or 1");
+  g_single_kernel.store(on, std::memory_order_release);
+  return MOE_OK;
+}
+
 int moe_set_a_path(const char* name) {
   t_last_error.clear();
   const int v = name == nullptr || strcmp(name, "auto") == 0 ? kDefaultAPath : parse_a_path(name);
@@ -914,13 +987,18 @@ int moe_device_status(void* stream, int clear, uint32_t* status_out) {
 }
 
 // ---------------------------------------------------------------------------- run_kernel
-// Workspace: U [P, I] (the reference's cached up_logits) + block groups [P/128] + group count.
+// Workspace: U [P, I] (the reference's cached up_logits) + block groups [P/128] + group count +
+// the single kernel's per-block Stage1 counts [P/128].
 static size_t run_kernel_u_bytes(int64_t P, int64_t I) { return round_up(static_cast<size_t>(P) * I * 2, 256); }
+static size_t run_kernel_groups_bytes(int64_t P) {
+  return round_up(sizeof(int32_t) * static_cast<size_t>(P / kBM + 1), 256);
+}
 
 size_t moe_run_kernel_workspace_bytes(int64_t P, int64_t I, int dtype) {
   (void)dtype;
   if (P <= 0 || I <= 0) return 0;
-  return run_kernel_u_bytes(P, I) + round_up(sizeof(int32_t) * static_cast<size_t>(P / kBM + 1), 256);
+  return run_kernel_u_bytes(P, I) + run_kernel_groups_bytes(P) +
+         round_up(sizeof(uint32_t) * static_cast<size_t>(P / kBM), 256);
 }
 
 int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const void* down_w, const void* routed,
@@ -958,11 +1036,19 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   void* U = workspace;
   int32_t* groups = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + run_kernel_u_bytes(P, I));
   int32_t* ngroups = groups + nblk;
+  uint32_t* done = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) + run_kernel_u_bytes(P, I) +
+                                               run_kernel_groups_bytes(P));
   const bool lsu = a_path_lsu();
   const double bpe = static_cast<double>(nblk) / static_cast<double>(E);  // blocks per expert
   TileCfg tc1 = usable_cfg(1, H, 2, lsu, bpe), tc2 = usable_cfg(2, I, 2, lsu, bpe);
   if (kTiles[tc1].tn) tc1 = kT256A4B5;  // the operand-swapped kernel runs on the fused path only
   if (kTiles[tc2].tn) tc2 = kT256x2A3B4;
+  // single-kernel MoE: both stages in one launch, on their default single-CTA tiles
+  const bool single = single_kernel() && !lsu && tile_cfg(1) == kAuto && tile_cfg(2) == kAuto;
+  if (single) {
+    tc1 = kDefaultTile1;
+    tc2 = kDefaultTile2;
+  }
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
 
@@ -981,7 +1067,7 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   m2.b1 = m2.b0;
 
   if (gmax1 > 1 || gmax2 > 1) {  // pair each expert's blocks (from group_padded_offsets)
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)nblk, groups, ngroups);
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)nblk, groups, ngroups, done, single ? (int)nblk : 0);
     MOE_CUDA(cudaGetLastError());
   }
 
@@ -1025,6 +1111,11 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   a2.a_ptr = U;
   a2.a_row_bytes = I * 2;
   const int tiles1 = (int)nblk * a1.n_tiles, tiles2 = (int)nblk * a2.n_tiles;
+  if (single) {
+    a1.block_done = a2.block_done = done;
+    a1.block_done_target = a2.block_done_target = static_cast<uint32_t>(a1.n_tiles * 8);  // x 8 epilogue warps
+    return launch_single_rt<kStage2Pad>(dtype, dev, m1, a1, m2, a2, tiles1, s);
+  }
   MOE_TRY((launch_stage_rt<kStage1, false, kALsu>(dtype, lsu, tc1, dev, m1, a1, tiles1, s)));
   MOE_TRY((launch_stage_rt<kStage2Pad, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, tiles2, s)));
   return MOE_OK;
@@ -1204,6 +1295,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   void* U = ws + L.u;
   int32_t* groups = reinterpret_cast<int32_t*>(ws + L.groups);
   int32_t* ngroups = groups + L.nblk_max;
+  uint32_t* done = reinterpret_cast<uint32_t*>(ws + L.done);
   const int elt = int8 ? 1 : 2;
   // expected blocks per expert: routes per expert / 128, plus half a block of padding (peer mode:
   // about 1 / W of the virtual routes land on this rank)
@@ -1214,6 +1306,13 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   // out at the bench's size while the single-CTA form passed its parity tests
   if (peer && peer->push && kTiles[tc2].pair) tc2 = kDefaultTile2;
   if (gather && !gather_cfg(tc1)) tc1 = kDefaultTile1;
+  // single-kernel MoE: both stages in one launch, on their default single-CTA tiles
+  const bool single = single_kernel() && !int8 && !peer && !lsu && !gather && !ordered && tile_cfg(1) == kAuto &&
+                      tile_cfg(2) == kAuto;
+  if (single) {
+    tc1 = kDefaultTile1;
+    tc2 = kDefaultTile2;
+  }
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   if (peer && peer->push && t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no push combine");
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
@@ -1226,7 +1325,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
                           counts, s));
   MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s, router != nullptr));
   if (gmax1 > 1 || gmax2 > 1) {
-    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups);
+    build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups, done,
+                                           single ? (int)L.nblk_max : 0);
     MOE_CUDA(cudaGetLastError());
   }
   int32_t* tn_entries = reinterpret_cast<int32_t*>(ws + L.tn);
@@ -1451,6 +1551,10 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_TRY(launch_tn_rt<kStage1>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s));
     } else if (gather) {
       MOE_TRY(launch_stage1_gather_rt<kQ16>(dtype, tc1, dev, m1, a1, max_tiles1, s));
+    } else if (single) {  // Stage1 and Stage2 in one launch: the Stage1 event marks the end of both
+      a1.block_done = a2.block_done = done;
+      a1.block_done_target = a2.block_done_target = static_cast<uint32_t>(a1.n_tiles * 8);  // x 8 epilogue warps
+      MOE_TRY(launch_single_rt<kStage2Comb>(dtype, dev, m1, a1, m2, a2, max_tiles1, s));
     } else {
       MOE_TRY((launch_stage_rt<kStage1, false, kAGather>(dtype, lsu, tc1, dev, m1, a1, max_tiles1, s)));
     }
@@ -1494,7 +1598,7 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       t.routed = tw;
       t.routed_dtype = w_dtype == MOE_F32 ? 0 : (w_dtype == MOE_F16 ? 1 : 2);
       MOE_TRY(launch_tn_rt<kStage2Comb>(dtype, dev, tc2, tm, t, (int)L.nblk_max * t.n_tiles, s));
-    } else {
+    } else if (!single) {
       MOE_TRY((launch_stage_rt<kStage2Comb, false, kALsu>(dtype, lsu, tc2, dev, m2, a2, max_tiles2, s)));
     }
     prof_record(4, s);

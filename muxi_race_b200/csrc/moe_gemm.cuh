@@ -82,7 +82,7 @@ template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false, 
   static_assert(kRingBytes <= kRingMax, "ring exceeds shared memory");
   static constexpr int kSlots = kTmemColsCta / BN;  // accumulator slots
   static constexpr int kRowTabBytes = ROWTAB ? GMAX * 128 * 8 : 0;  // LSU A path: source row offsets
-  static constexpr int kSmemBytes = 1024 /*align slack*/ + kRingBytes + 512 /*barriers*/ + kRowTabBytes;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kRingBytes + 512 /*control block*/ + kRowTabBytes;
   static_assert(kSmemBytes <= 232448, "exceeds the 227 KiB of shared memory a CTA may opt in to");
   static_assert(CPS == 1 || kSmemBytes + 1024 <= 233472 / 2, "two CTAs must fit in one SM's shared memory");
 };
@@ -148,6 +148,13 @@ struct GemmArgs {
   int gu_swap;                // combined map based at the up rows: the tile holds [up | gate]
   int late_release;           // epilogue hands the accumulator slot back after its stores (A/B switch)
   int m64_tail;               // blocks with at most 64 valid rows run M = 64 MMAs (needs group_sizes)
+
+  // Single-kernel MoE (moe_single_kernel): per 128-row block, a count of Stage1 results. Each
+  // Stage1 epilogue warp adds one per column tile after its stores of the block's U rows;
+  // Stage2's A producer waits until a block's count reaches block_done_target before it loads
+  // those rows. NULL: the stages are separate launches and nothing is counted.
+  uint32_t* block_done;
+  uint32_t block_done_target;
 
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
@@ -442,12 +449,20 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
 //         when args.b_split. Stage2: {K, rows} for KPB = 1, {k-block elements, rows, k-blocks}
 //         otherwise.
 //   tmB1  Stage1 with args.b_split: the up rows ({K, rows}).
-template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
-          int EPI = 4>
-__global__ void __launch_bounds__(96 + EPI * 32, CPS)
-    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
-                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
-                    const GemmArgs args) {
+// Control block after the rings: the TMEM base address (4 bytes), the abort flag (4 bytes), then
+// the mbarriers of one pipeline (two in the single-kernel MoE, one set per stage).
+constexpr int kCtlBytes = 512;
+__host__ __device__ constexpr int pipeline_bars(int ast, int bst, int slots) { return 2 * ast + 2 * bst + 2 * slots + 1; }
+
+// The roles of one grouped GEMM over its work units, on a CTA whose TMEM is allocated (the
+// address is at *tmem_slot once the CTA has synchronised) and whose abort flag is cleared: the
+// phase initialises its mbarriers at `bars`, runs the producers, the MMA issuer and the
+// epilogue, and returns once every role has drained (its loads landed, its MMAs retired).
+template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB, int EPI>
+__device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUtensorMap* tmA1_p,
+                                           const CUtensorMap* tmB0_p, const CUtensorMap* tmB1_p,
+                                           const GemmArgs& args, uint8_t* smem, uint64_t* bars,
+                                           const uint32_t* tmem_slot, volatile int* abort_flag, long long* row_tab) {
   using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>;
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
@@ -456,11 +471,12 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
   constexpr int kSlots = RingT::kSlots;
   constexpr int kHalves = BN / kMN;  // MMAs per k-step per block
   static_assert(EPI == 4 || EPI == 8, "epilogue warps");
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const CUtensorMap& tmA = *tmA_p;
+  const CUtensorMap& tmA1 = *tmA1_p;
+  const CUtensorMap& tmB0 = *tmB0_p;
+  const CUtensorMap& tmB1 = *tmB1_p;
   uint8_t* ring_b = smem;                            // [BST][KPB][BN rows x 128 B]
   uint8_t* ring_a = smem + BST * kBBytes;            // [AST][GMAX][kABytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + RingT::kRingBytes);
   uint64_t* fullA = bars;                            // [AST]
   uint64_t* emptyA = fullA + AST;                    // [AST]
   uint64_t* fullB = emptyA + AST;                    // [BST]
@@ -468,9 +484,6 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
   uint64_t* tfull_bar = emptyB + BST;                // [kSlots] per accumulator slot
   uint64_t* tempty_bar = tfull_bar + kSlots;         // [kSlots]
   uint64_t* drain_bar = tempty_bar + kSlots;         // [1] MMA warp: all issued MMAs retired
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  long long* row_tab = reinterpret_cast<long long*>(smem + RingT::kRingBytes + 512);  // [GMAX][128]
   auto stage_a = [&](int s, int j) { return ring_a + s * kAStageBytes + j * kABytes; };
   auto stage_b = [&](int s) { return ring_b + s * kBBytes; };
 
@@ -491,7 +504,6 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
       mbar_init(&tempty_bar[a], EPI);  // one arrive per epilogue warp
     }
     mbar_init(drain_bar, 1);
-    *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -501,10 +513,6 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     }
     tma_prefetch_desc(&tmB0);
     if (MODE == kStage1 && args.b_split) tma_prefetch_desc(&tmB1);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, RingT::kTmemColsCta);
-    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
@@ -640,6 +648,19 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int fb, nb, nt, e;
         if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        if (MODE != kStage1 && AMODE == kATma && args.block_done != nullptr) {
+          // single-kernel MoE: the group's U rows are complete once every Stage1 column tile of
+          // each of its blocks has published its stores (other CTAs' generic-proxy stores, read
+          // here by TMA: acquire, then the proxy fence)
+          bool dep = true;
+          for (int j = 0; j < nb && dep; ++j)
+            dep = counter_wait(args.block_done + fb + j, args.block_done_target, abort_flag, args.status);
+          if (!dep) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         if (AMODE != kATma) {
           // byte offsets of this group's source rows, -1 = zero fill
           __syncwarp();
@@ -840,11 +861,44 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
           else
             epilogue_block<MODE, OutT, Q8, BN, AMODE, kPass>(args, t_row, fb + j, nt, e, row, c_begin + c0, release);
         }
+        if (MODE == kStage1 && args.block_done != nullptr) {
+          // publish this warp's U stores of the block to the Stage2 TMA loads of any CTA
+          fence_proxy_async_global();
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(args.block_done + fb + j, 1u);
+        }
         ++slot_cnt;
       }
     }
   }
 
+}
+
+// One grouped GEMM (one stage) per launch.
+template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
+          int EPI = 4>
+__global__ void __launch_bounds__(96 + EPI * 32, CPS)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
+                    const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
+                    const GemmArgs args) {
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>;
+  static_assert(8 + 8 * pipeline_bars(AST, BST, RingT::kSlots) <= kCtlBytes, "control block");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ctl = smem + RingT::kRingBytes;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctl + 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ctl + 8);
+  long long* row_tab = reinterpret_cast<long long*>(ctl + kCtlBytes);  // [GMAX][128], LSU A paths
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) *abort_flag = 0;
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, RingT::kTmemColsCta);
+    tmem_relinquish();
+  }
+  gemm_phase<MODE, OutT, Q8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>(&tmA, &tmA1, &tmB0, &tmB1, args, smem, bars,
+                                                                        tmem_slot, abort_flag, row_tab);
   // push combine: this thread's reductions into peer memory are performed system-wide before
   // the kernel ends (the flag barrier that follows publishes them to the home ranks)
   if (MODE == kStage2Comb && args.out_regions != nullptr) __threadfence_system();
@@ -852,7 +906,66 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, RingT::kTmemColsCta);
+    tmem_dealloc(*tmem_slot, RingT::kTmemColsCta);
+  }
+}
+
+// ------------------------------------------------------------------ single-kernel MoE
+// Stage1 and Stage2 in one persistent launch (one CTA per SM, all co-resident: the launch is
+// cooperative). Each CTA runs its Stage1 units (tile 256a4b5e8: 128 SiLU*up columns per unit),
+// then, without waiting for the other CTAs, its Stage2 units (tile 256x2a3b4e8: two-block groups,
+// 256 output columns). A Stage2 unit loads a block's U rows only after every Stage1 column tile of
+// that block has published its stores (GemmArgs::block_done, counted per epilogue warp), so the
+// end of Stage1 on one SM overlaps Stage2 on the others: the separate launches' Stage1 tail, launch
+// gap and Stage2 prologue are gone; U still goes through memory. Every Stage1 unit is taken before
+// any Stage2 unit and Stage1 units wait on nothing outside their CTA, so the waits end as long as
+// all CTAs run at once (a cooperative launch guarantees it; each wait is bounded all the same).
+// The two phases keep separate mbarriers: asynchronous arrivals of the first can never meet the
+// second.
+using SingleRing1 = Ring<256, 1, 4, 5>;
+using SingleRing2 = Ring<256, 2, 3, 4>;
+constexpr int kSingleRingBytes =
+    SingleRing1::kRingBytes > SingleRing2::kRingBytes ? SingleRing1::kRingBytes : SingleRing2::kRingBytes;
+constexpr int kSingleBars1 = pipeline_bars(4, 5, SingleRing1::kSlots);
+constexpr int kSingleBars2 = pipeline_bars(3, 4, SingleRing2::kSlots);
+static_assert(8 + 8 * (kSingleBars1 + kSingleBars2) <= kCtlBytes, "control block of the single kernel");
+constexpr int kSingleSmemBytes = 1024 + kSingleRingBytes + kCtlBytes;
+constexpr int kSingleThreads = 96 + 8 * 32;
+
+template <typename OutT, int MODE2>
+__global__ void __launch_bounds__(kSingleThreads, 1)
+    moe_single_kernel(const __grid_constant__ CUtensorMap tm1A, const __grid_constant__ CUtensorMap tm1B0,
+                      const __grid_constant__ CUtensorMap tm1B1, const __grid_constant__ CUtensorMap tm2A,
+                      const __grid_constant__ CUtensorMap tm2A1, const __grid_constant__ CUtensorMap tm2B0,
+                      const GemmArgs a1, const GemmArgs a2) {
+  static_assert(MODE2 == kStage2Pad || MODE2 == kStage2Comb, "second phase is a Stage2");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ctl = smem + kSingleRingBytes;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ctl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(ctl + 4);
+  uint64_t* bars1 = reinterpret_cast<uint64_t*>(ctl + 8);
+  uint64_t* bars2 = bars1 + kSingleBars1;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) *abort_flag = 0;
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  gemm_phase<kStage1, OutT, kQ16, 256, 1, 4, 5, kATma, 1, 1, 8>(&tm1A, &tm1A, &tm1B0, &tm1B1, a1, smem, bars1,
+                                                                 tmem_slot, abort_flag, nullptr);
+  // every role of the first phase has drained: the rings and TMEM are free for Stage2
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (!*abort_flag)
+    gemm_phase<MODE2, OutT, kQ16, 256, 2, 3, 4, kATma, 1, 1, 8>(&tm2A, &tm2A1, &tm2B0, &tm2B0, a2, smem, bars2,
+                                                                 tmem_slot, abort_flag, nullptr);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(*tmem_slot, kTmemCols);
   }
 }
 
@@ -860,13 +973,16 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
 // Pairs the routing blocks of each expert: expert e owns blocks [gpo[e]/128, gpo[e+1]/128); they
 // become ceil(n/gmax) groups of up to gmax consecutive blocks, in expert order. One CTA of 1024
 // threads walks the experts in chunks of 1024 with a running base. At most max_groups groups are
-// written (offsets that describe more blocks than the row space holds are cut off there).
+// written (offsets that describe more blocks than the row space holds are cut off there). The
+// kernel also clears zero[0..n_zero) (the single-kernel MoE's per-block Stage1 counts).
 __global__ void __launch_bounds__(1024)
     build_groups_kernel(const int32_t* __restrict__ group_padded_offsets, int E, int gmax, int max_groups,
-                        int32_t* __restrict__ groups, int32_t* __restrict__ ngroups_out) {
+                        int32_t* __restrict__ groups, int32_t* __restrict__ ngroups_out,
+                        uint32_t* __restrict__ zero, int n_zero) {
   __shared__ int s_warp[32];
   __shared__ int s_base;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  for (int i = tid; i < n_zero; i += blockDim.x) zero[i] = 0u;
   if (tid == 0) s_base = 0;
   __syncthreads();
   for (int e0 = 0; e0 < E; e0 += blockDim.x) {

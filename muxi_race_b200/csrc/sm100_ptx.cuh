@@ -20,6 +20,7 @@ enum : uint32_t {
   kStatusWaitTimeout = 1u << 0,   // an mbarrier wait ran past MOE_WAIT_NS
   kStatusBadExpert = 1u << 1,     // a block/route named an expert outside [0, E)
   kStatusBadRoute = 1u << 2,      // a route index outside [0, R)
+  kStatusDepTimeout = 1u << 3,    // a wait for another CTA's results ran past MOE_WAIT_NS
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -160,6 +161,39 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // Order generic-proxy shared-memory writes before later async-proxy (tcgen05, TMA) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Order this thread's generic-proxy global-memory accesses with its async-proxy (TMA) accesses:
+// a writer issues it after its stores of data that other CTAs' TMA loads will read, a reader
+// after its acquire and before those loads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until *counter >= target (acquire, GPU scope): the counter is raised by other
+// CTAs of the same grid. Gives up like mbar_wait (abort flag, or MOE_WAIT_NS, which sets the
+// abort flag and kStatusDepTimeout).
+__device__ __forceinline__ bool counter_wait(const uint32_t* counter, uint32_t target, volatile int* abort_flag,
+                                             uint32_t* status) {
+  if (ld_acquire_gpu(counter) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (ld_acquire_gpu(counter) < target) {
+    __nanosleep(64);
+    if ((++spins & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > MOE_WAIT_NS) {
+        *abort_flag = 1;
+        if (status) atomicOr(status, kStatusDepTimeout);
+        return false;
+      }
+    }
+  }
+  return true;
 }
 
 // ---------------------------------------------------------------- tcgen05 / TMEM

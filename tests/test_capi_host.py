@@ -39,7 +39,8 @@ def test_version_and_pure_host_queries():
     assert lib.moe_max_padded_rows(1, 8, 128) == 128
     assert lib.moe_max_padded_rows(128, 8, 128) == 1152
     assert lib.moe_max_padded_rows(32768, 256, 128) == 65280
-    assert lib.moe_run_kernel_workspace_bytes(256, 2048, _lib.MOE_F16) == 256 * 2048 * 2 + 256
+    # U, then the block groups + count and the single kernel's per-block counts (256 bytes each)
+    assert lib.moe_run_kernel_workspace_bytes(256, 2048, _lib.MOE_F16) == 256 * 2048 * 2 + 256 + 256
     # the Stage1 intermediate U [P_max, I] dominates (token rows are gathered inside Stage1)
     assert lib.moe_fused_workspace_bytes(4096, 8, 256, 7168, 2048, _lib.MOE_F16) >= 65280 * 2048 * 2
 
@@ -204,3 +205,16 @@ def test_a_path_selection_sizes_the_workspace():
             _lib.set_a_path("no-such-path")
     finally:
         _lib.set_a_path(None)
+
+
+def test_single_kernel_switch():
+    """moe_set_single_kernel takes 0 or 1; anything else is refused and leaves the choice as it was."""
+    lib = _lib.lib()
+    try:
+        assert lib.moe_set_single_kernel(1) == 0
+        assert lib.moe_set_single_kernel(0) == 0
+        with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
+            _lib.call("moe_set_single_kernel", 2)
+        assert b"0 or 1" in lib.moe_last_error()
+    finally:
+        _lib.set_single_kernel(False)
