@@ -281,6 +281,12 @@ def bench_ours(args, world, rank, local):
         stages["stage2"] = stage_ms(4, 5)
     else:
         stages["stage2"] = stage_ms(3, 4)
+    # With the single-kernel MoE (the default where a call averages < 1.8 routing blocks per
+    # expert) the library records the Stage1 and Stage2 boundary events around one launch: the
+    # Stage2 interval is then empty and the Stage1 interval covers both stages.
+    single = not q8 and stages["stage2"] < 0.02 * stages["stage1"]
+    if single:
+        stages = {"align": stages["align"], "gather": stages["gather"], "single_kernel": stages["stage1"]}
 
     # ---- end to end through the public API with host buffers: every step uploads its inputs
     #      from pinned host memory and downloads its result; by default through HostPipeline
@@ -364,20 +370,30 @@ def bench_ours(args, world, rank, local):
     st = m.device_status()
     assert st == 0, f"device status {st} (bit 0 wait timeout, 1 bad expert, 2 bad route) after timing"
 
-    # ---- roofline of the dominant kernel (Stage1): algorithmic bytes per launch / launch time
+    # ---- roofline of the dominant kernel (Stage1, or the single kernel that runs both stages):
+    #      algorithmic bytes per launch / launch time. Stage1: the active experts' gate and up
+    #      weights, the routed token rows and U; Stage2: the down weights, U and the token-major
+    #      output (its combine's adds of a token's rows meet in L2).
     elt = 1 if q8 else 2
     s1_bytes = active * 2 * cfg.I * cfg.H * elt + routes * cfg.H * elt + routes * cfg.I * 2
-    s1_gbs = s1_bytes / (stages["stage1"] * 1e-3) / 1e9
+    s2_bytes = active * cfg.H * cfg.I * elt + routes * cfg.I * 2 + cfg.T * cfg.H * 2
+    if single:
+        k_name, k_bytes, k_ms, k_traffic = ("moe_single_kernel (Stage1 + Stage2)", s1_bytes + s2_bytes,
+                                            stages["single_kernel"], "single_dram_bytes_per_launch")
+    else:
+        k_name, k_bytes, k_ms, k_traffic = ("stage1 (moe_gemm_kernel<kStage1>)", s1_bytes, stages["stage1"],
+                                            "stage1_dram_bytes_per_launch")
+    k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
     traffic = None
     tp = os.path.join(ROOT, "profiles", f"traffic_{cfg.name}.json")
     # the committed capture is of the default fp16 call: no traffic figure for other variants
     if os.path.exists(tp) and variant == "default" and not q8:
         with open(tp) as f:
-            traffic = json.load(f).get("stage1_dram_bytes_per_launch")
+            traffic = json.load(f).get(k_traffic)
     roofline = {
-        "bound": "hbm", "kernel": "stage1 (moe_gemm_kernel<kStage1>)", "achieved": round(s1_gbs, 1),
-        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(s1_gbs / peaks["hbm_gbs"], 4),
-        "traffic": traffic, "algorithmic_bytes": s1_bytes, "peak_kind": peak_kind,
+        "bound": "hbm", "kernel": k_name, "achieved": round(k_gbs, 1),
+        "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(k_gbs / peaks["hbm_gbs"], 4),
+        "traffic": traffic, "algorithmic_bytes": k_bytes, "peak_kind": peak_kind,
     }
     total_bytes = float(active) * 3 * cfg.H * cfg.I * elt + cfg.io_bytes()  # elt: 1 for int8 and fp8
     t_roof_ms = max(flops / (peaks["bf16_tflops"] * 1e12), total_bytes / (peaks["hbm_gbs"] * 1e9)) * 1e3
@@ -418,7 +434,7 @@ def bench_ours(args, world, rank, local):
                 **({"output_check": e2e_checked} if e2e_checked else {})},
         # per call: alignment (count or router, scan, scatter), block groups, gather, Stage1, Stage2;
         # 8-bit routes add the intermediate requantisation, the ordered combine its two kernels
-        "gpu_launches": args.steps * (8 if q8 else 9 if variant == "ordered" else 7),
+        "gpu_launches": args.steps * (8 if q8 else 9 if variant == "ordered" else 6 if single else 7),
         "clocks": clock_info,
     }
     if world == 1 and cfg.name == "cfg3" and variant == "default" and not args.no_north_star:
@@ -597,6 +613,11 @@ def bench_ep(args, world, rank, local):
     local_active = int(torch.unique(routed[mine_mask]).numel())
     s1_flops = 2.0 * local_routes * 2 * cfg.I * cfg.H
     s1_bytes = local_active * 2 * cfg.I * cfg.H * 2 + local_routes * cfg.H * 2 + local_routes * cfg.I * 2
+    # the single-kernel MoE records the Stage1 and Stage2 events around one launch
+    single = local_ms["stage2"] < 0.02 * local_ms["stage1"]
+    if single:
+        s1_flops += 2.0 * local_routes * cfg.I * cfg.H
+        s1_bytes += local_active * cfg.H * cfg.I * 2 + local_routes * cfg.I * 2 + local_routes * cfg.H * 2
     s1_s = local_ms["stage1"] * 1e-3
     t_mem = s1_bytes / (peaks["hbm_gbs"] * 1e9)
     t_cmp = s1_flops / (peaks["bf16_tflops"] * 1e12)
@@ -606,7 +627,8 @@ def bench_ep(args, world, rank, local):
     else:
         roofline = {"bound": "hbm", "achieved": round(s1_bytes / s1_s / 1e9, 1), "peak": peaks["hbm_gbs"],
                     "unit": "GB/s", "frac": round(s1_bytes / s1_s / 1e9 / peaks["hbm_gbs"], 4)}
-    roofline.update({"kernel": "stage1 (rank 0's local fused MoE)", "traffic": None, "peak_kind": peak_kind,
+    roofline.update({"kernel": ("single kernel" if single else "stage1") + " (rank 0's local fused MoE)",
+                     "traffic": None, "peak_kind": peak_kind,
                      "algorithmic_bytes": s1_bytes, "algorithmic_flops": s1_flops})
 
     # end to end: host inputs in, output back, every step

@@ -92,17 +92,19 @@ MOE_API int moe_set_tile(int stage, const char* name);
  * return MOE_ERR_INVALID_ARG. The expert-parallel peer-memory mode always stacks its rows. */
 MOE_API int moe_set_a_path(const char* name);
 
-/* Selects the single-kernel MoE for all later calls in the process (1) or the two stage launches
- * (0; the default; the environment variable MOE_B200_SINGLE_KERNEL=0|1 sets the initial choice).
- * The reference fuses nothing across its two stages; its one attempt at a single-kernel MoE is
- * xpuoj_data/probe_v236_fused_single_kernel.py. The single kernel runs Stage1 and Stage2 of
- * moe_run_kernel and moe_fused in one cooperative launch: each SM moves on to Stage2 units as
- * soon as its own Stage1 units are done, and a Stage2 unit waits (bounded; status bit 3 on
- * timeout) until every Stage1 column tile of its rows has been stored. It applies where both
- * stages would run their default single-CTA tiles on the TMA path: 16-bit routes without the
- * ordered combine or expert-parallel peer memory, with no tile forced by moe_set_tile and the
- * default A path; other calls keep the two launches. Other values return MOE_ERR_INVALID_ARG. */
-MOE_API int moe_set_single_kernel(int on);
+/* Selects, for all later calls in the process, whether Stage1 and Stage2 of moe_run_kernel and
+ * moe_fused run as one kernel: 0 = two launches, 1 = the single kernel wherever it applies, 2 =
+ * automatic, the default (the single kernel where it applies and the call averages fewer than 1.8
+ * routing blocks of 128 rows per expert; the environment variable MOE_B200_SINGLE_KERNEL=0|1|2
+ * sets the initial mode). The reference fuses nothing across its two stages; its one attempt at a
+ * single-kernel MoE is xpuoj_data/probe_v236_fused_single_kernel.py. The single kernel is one
+ * cooperative launch: each SM moves on to Stage2 units as soon as its own Stage1 units are done,
+ * and a Stage2 unit waits (bounded; status bit 3 on timeout) until every Stage1 column tile of
+ * its rows has been stored. It applies where both stages would run their default single-CTA tiles
+ * on the TMA path: 16-bit routes without the ordered combine or expert-parallel peer memory, with
+ * no tile forced by moe_set_tile and the default A path; other calls keep the two launches. Other
+ * values return MOE_ERR_INVALID_ARG. */
+MOE_API int moe_set_single_kernel(int mode);
 
 /* ------------------------------------------------------------------------------------------
  * Reference drop-in: the contest operator.

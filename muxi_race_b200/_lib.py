@@ -180,11 +180,12 @@ def set_a_path(name) -> None:
     call("moe_set_a_path", None if name is None else str(name).encode())
 
 
-def set_single_kernel(on: bool) -> None:
-    """Run Stage1 and Stage2 of later run_kernel / fused_moe calls as one cooperative launch
-    (True) or as two launches (False, the default); calls whose tiles or paths the single kernel
-    does not cover keep the two launches."""
-    call("moe_set_single_kernel", 1 if on else 0)
+def set_single_kernel(on) -> None:
+    """Whether later run_kernel / fused_moe calls of the process run Stage1 and Stage2 as one
+    cooperative launch: True (wherever the single kernel applies), False (two launches) or None
+    (automatic, the default: where it applies and the call averages fewer than 1.8 routing blocks
+    per expert)."""
+    call("moe_set_single_kernel", 2 if on is None else (1 if on else 0))
 
 
 def set_tile(stage: int, name) -> None:

@@ -452,22 +452,32 @@ int epilogue_late_release() {
   return e && strcmp(e, "late") == 0 ? 1 : 0;
 }
 
-// Single-kernel MoE (moe_single_kernel, Stage1 and Stage2 in one cooperative launch):
-// MOE_B200_SINGLE_KERNEL = 0 | 1 at first use, moe_set_single_kernel afterwards; unset:
-// kDefaultSingleKernel. Used where both stages run their default single-CTA tiles on the TMA A
-// path (fp16/bf16 routes without the ordered combine or peer memory, no tile forced).
-constexpr int kDefaultSingleKernel = 0;
+// Single-kernel MoE (moe_single_kernel, Stage1 and Stage2 in one cooperative launch): mode 0 =
+// two launches, 1 = the single kernel wherever it applies, 2 = automatic: where it applies and the
+// call averages fewer than kPairBlocksPerExpert routing blocks per expert (the regime whose Stage2
+// is the single-CTA two-block tile by choice). It applies where both stages run their default
+// single-CTA tiles on the TMA A path (fp16/bf16 routes without the ordered combine or peer memory,
+// no tile forced). Measured against the two launches on one B200, alternating in one process:
+// cfg3 4.72 vs 4.78 ms, contest case 3 1.105 vs 1.121 ms, cfg3 at T = 128 3.44 vs 3.47 ms, but
+// cfg5 (8.5 blocks per expert) 28.13 vs 27.88 ms. MOE_B200_SINGLE_KERNEL = 0 | 1 | 2 at first use,
+// moe_set_single_kernel afterwards; unset: kDefaultSingleKernel.
+constexpr int kDefaultSingleKernel = 2;
 std::atomic<int> g_single_kernel{-1};
-int single_kernel() {
+int single_kernel_mode() {
   int v = g_single_kernel.load(std::memory_order_acquire);
   if (v < 0) {
     const char* e = getenv("MOE_B200_SINGLE_KERNEL");
-    const int env = e && strcmp(e, "1") == 0 ? 1 : (e && strcmp(e, "0") == 0 ? 0 : kDefaultSingleKernel);
+    const int env = e && (e[0] == '0' || e[0] == '1' || e[0] == '2') && e[1] == 0 ? e[0] - '0' : kDefaultSingleKernel;
     int expected = -1;
     g_single_kernel.compare_exchange_strong(expected, env, std::memory_order_acq_rel);
     v = g_single_kernel.load(std::memory_order_acquire);
   }
   return v;
+}
+// Whether a call that the single kernel covers runs it, given its average blocks per expert.
+bool single_kernel(double blocks_per_expert) {
+  const int mode = single_kernel_mode();
+  return mode == 1 || (mode == 2 && blocks_per_expert < kPairBlocksPerExpert);
 }
 // The single kernel's shared-memory attribute bit: the operand-swapped kernel's range at a
 // configuration that kernel never runs with.
@@ -948,10 +958,10 @@ int moe_set_tile(int stage, const char* name) {
   return MOE_OK;
 }
 
-int moe_set_single_kernel(int on) {
+int moe_set_single_kernel(int mode) {
   t_last_error.clear();
-  if (on != 0 && on != 1) return fail(MOE_ERR_INVALID_ARG, "moe_set_single_kernel takes 0 or 1");
-  g_single_kernel.store(on, std::memory_order_release);
+  if (mode < 0 || mode > 2) return fail(MOE_ERR_INVALID_ARG, "moe_set_single_kernel takes 0, 1 or 2");
+  g_single_kernel.store(mode, std::memory_order_release);
   return MOE_OK;
 }
 
@@ -1044,7 +1054,7 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
   if (kTiles[tc1].tn) tc1 = kT256A4B5;  // the operand-swapped kernel runs on the fused path only
   if (kTiles[tc2].tn) tc2 = kT256x2A3B4;
   // single-kernel MoE: both stages in one launch, on their default single-CTA tiles
-  const bool single = single_kernel() && !lsu && tile_cfg(1) == kAuto && tile_cfg(2) == kAuto;
+  const bool single = single_kernel(bpe) && !lsu && tile_cfg(1) == kAuto && tile_cfg(2) == kAuto;
   if (single) {
     tc1 = kDefaultTile1;
     tc2 = kDefaultTile2;
@@ -1307,8 +1317,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (peer && peer->push && kTiles[tc2].pair) tc2 = kDefaultTile2;
   if (gather && !gather_cfg(tc1)) tc1 = kDefaultTile1;
   // single-kernel MoE: both stages in one launch, on their default single-CTA tiles
-  const bool single = single_kernel() && !int8 && !peer && !lsu && !gather && !ordered && tile_cfg(1) == kAuto &&
-                      tile_cfg(2) == kAuto;
+  const bool single = single_kernel(bpe) && !int8 && !peer && !lsu && !gather && !ordered &&
+                      tile_cfg(1) == kAuto && tile_cfg(2) == kAuto;
   if (single) {
     tc1 = kDefaultTile1;
     tc2 = kDefaultTile2;

@@ -208,13 +208,15 @@ def test_a_path_selection_sizes_the_workspace():
 
 
 def test_single_kernel_switch():
-    """moe_set_single_kernel takes 0 or 1; anything else is refused and leaves the choice as it was."""
+    """moe_set_single_kernel takes 0 (two launches), 1 (single kernel) or 2 (automatic); anything
+    else is refused."""
     lib = _lib.lib()
     try:
-        assert lib.moe_set_single_kernel(1) == 0
-        assert lib.moe_set_single_kernel(0) == 0
-        with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
-            _lib.call("moe_set_single_kernel", 2)
-        assert b"0 or 1" in lib.moe_last_error()
+        for mode in (1, 0, 2):
+            assert lib.moe_set_single_kernel(mode) == 0
+        for bad in (3, -1):
+            with pytest.raises(_lib.MoeError, match="MOE_ERR_INVALID_ARG"):
+                _lib.call("moe_set_single_kernel", bad)
+        assert b"0, 1 or 2" in lib.moe_last_error()
     finally:
-        _lib.set_single_kernel(False)
+        _lib.set_single_kernel(None)

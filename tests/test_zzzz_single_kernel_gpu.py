@@ -1,6 +1,6 @@
 """GPU: the single-kernel MoE (Stage1 and Stage2 in one cooperative launch, selected with
-``moe_set_single_kernel`` / ``_lib.set_single_kernel``) against the CPU oracle and against the two
-stage launches.
+``moe_set_single_kernel`` / ``_lib.set_single_kernel``; forced on here, automatic by default)
+against the CPU oracle and against the two stage launches.
 
 Checked:
 - the reference drop-in ``run_kernel`` on the golden fixtures (the reference's own outputs) and on
@@ -35,7 +35,7 @@ def single():
     _lib.set_tile(0, None)
     _lib.set_single_kernel(True)
     yield
-    _lib.set_single_kernel(False)
+    _lib.set_single_kernel(None)
 
 
 def assert_within(out, ref, what):
