@@ -276,6 +276,7 @@ enum TileCfg {
   kT256A4B5E8,
   kT256x2A3B4E8,
   kTTN,
+  kT128x2A4B6E8,
   kNumTileCfg
 };
 constexpr TileInfo kTiles[kNumTileCfg] = {
@@ -287,6 +288,7 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
     {"p256a6b8", 256, 2, 6, 8, 1, 1, 1, 4},    {"p256a7b7", 256, 2, 7, 7, 1, 1, 1, 4},
     {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
     {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8}, {"tn", 256, 1, 6, 4, 1, 1, 0, 4, 1},
+    {"128x2a4b6e8", 128, 2, 4, 6, 1, 1, 0, 8},
 };
 
 // Defaults, measured on B200. Stage1: 256a4b5e8 (single CTA, 8 epilogue warps: the SiLU*up
@@ -372,7 +374,7 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   }
   const TileInfo& t = kTiles[c];
   if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return safe;
-  if (t.bn == 128 && stage != 1) return safe;
+  if (t.bn == 128 && stage != 1 && c != kT128x2A4B6E8) return safe;  // 128-wide Stage2: this tile only
   if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
   if (t.tn && (lsu || (K * elt) % kKBytes != 0)) return safe;
   return c;
@@ -709,6 +711,9 @@ int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, i
         break;
       case kT256x2A3B4E8:
         if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 3, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT128x2A4B6E8:  // two-block groups, 128 columns per block: two units' accumulators in TMEM
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 128, 2, 4, 6, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
         break;
 
       default:
