@@ -437,6 +437,16 @@ int weights_evict_first(int mode) {
   if (e && (strcmp(e, "0") == 0 || strcmp(e, "1") == 0 || strcmp(e, "2") == 0)) v = e[0] - '0';
   return v == 1 || (v == 2 && mode != kStage1) ? 1 : 0;
 }
+// L2 policy of the Stage2 combine's adds into the token-major output: MOE_B200_OUT_EVICT_LAST =
+// 0 (evict_normal) | 1 (evict_last: a token's rows stay in L2 between its top-k adds while the
+// weights stream past); unset: kDefaultOutEvictLast. Read at each launch.
+constexpr int kDefaultOutEvictLast = 0;
+int out_evict_last() {
+  const char* e = getenv("MOE_B200_OUT_EVICT_LAST");
+  if (e && strcmp(e, "0") == 0) return 0;
+  if (e && strcmp(e, "1") == 0) return 1;
+  return kDefaultOutEvictLast;
+}
 // M = 64 MMAs for an expert's last block when it holds at most 64 valid rows (see half_block):
 // MOE_B200_M64_TAIL = 0 | 1, unset: kDefaultM64Tail. Read at each launch.
 constexpr int kDefaultM64Tail = 0;
@@ -491,6 +501,7 @@ int launch_single(int dev, const StageMaps& m1, const GemmArgs& a1, const StageM
   auto kern = moe_single_kernel<OutT, MODE2>;
   GemmArgs x1 = a1, x2 = a2;
   for (GemmArgs* x : {&x1, &x2}) {
+    x->out_evict_last = out_evict_last();
     x->late_release = epilogue_late_release();
     x->m64_tail = m64_tail();
     x->unit_order = x->group_padded_offsets ? unit_order() : 0;
@@ -534,6 +545,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>;
   GemmArgs args_l = args;
   args_l.b_evict_first = weights_evict_first(MODE);
+  args_l.out_evict_last = out_evict_last();
   args_l.late_release = epilogue_late_release();
   args_l.m64_tail = m64_tail();
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;
@@ -558,6 +570,7 @@ int launch_pair(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   auto kern = moe_gemm_pair_kernel<MODE, OutT, I8, AST, BST, EPI>;
   GemmArgs args_l = args;
   args_l.b_evict_first = weights_evict_first(MODE);
+  args_l.out_evict_last = out_evict_last();
   args_l.late_release = epilogue_late_release();
   args_l.m64_tail = 0;  // the CTA-pair kernel's MMAs are M = 256
   args_l.unit_order = args.group_padded_offsets ? unit_order() : 0;

@@ -141,6 +141,7 @@ struct GemmArgs {
   long long zero_bytes;
 
   int b_evict_first;          // weight loads with the L2 evict_first policy
+  int out_evict_last;         // Stage2Comb: the combine's adds with the L2 evict_last policy
   int unit_order;             // 0 = group-major units, 1 = per expert column-tile-major (tile_unit)
   // Stage1 weight maps: 0 = tmB0 covers gate and up rows as one tensor (the gate/up offset is a
   // dimension: one box per stage); 1 = tmB0 gate rows and tmB1 up rows, two 2-D boxes per k-block.
@@ -222,6 +223,18 @@ __device__ __forceinline__ void red_add_v4(__half* p, uint4 v) {
 __device__ __forceinline__ void red_add_v4(__nv_bfloat16* p, uint4 v) {
   asm volatile("red.global.add.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
                "r"(v.w)
+               : "memory");
+}
+
+// The same adds with an L2 cache policy (the combine's target rows kept with evict_last).
+__device__ __forceinline__ void red_add_v4(__half* p, uint4 v, uint64_t pol) {
+  asm volatile("red.global.add.L2::cache_hint.noftz.v4.f16x2 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void red_add_v4(__nv_bfloat16* p, uint4 v, uint64_t pol) {
+  asm volatile("red.global.add.L2::cache_hint.noftz.v4.bf16x2 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w), "l"(pol)
                : "memory");
 }
 
@@ -432,6 +445,8 @@ __device__ __forceinline__ void epilogue_block(const GemmArgs& args, uint32_t t_
         const uint4 val = make_uint4(packed[ch][4 * v], packed[ch][4 * v + 1], packed[ch][4 * v + 2], packed[ch][4 * v + 3]);
         if (MODE == kStage2Pad || push)
           *reinterpret_cast<uint4*>(dst + v * 8) = val;
+        else if (args.out_evict_last)
+          red_add_v4(dst + v * 8, val, l2_policy_evict_last());
         else
           red_add_v4(dst + v * 8, val);
       }
