@@ -67,7 +67,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   std::atomic<int> sms{0};
   std::atomic<uint32_t*> status{nullptr};
-  std::atomic<uint64_t> attr_done[32] = {};  // bit per kernel whose smem attribute has been raised
+  std::atomic<uint64_t> attr_done[48] = {};  // bit per kernel whose smem attribute has been raised
 };
 DeviceInfo g_dev[kMaxDevices];
 
@@ -128,6 +128,7 @@ struct TileInfo {
   int pair;  // 1: CTA-pair kernel (cta_group::2), 256-row units, each CTA loads half the weights
   int epi;   // epilogue warps (4, or 8: two per TMEM lane quadrant, each half of the columns)
   int tn;    // 1: operand-swapped kernel (weights as M, an expert's tokens as N; fused path only)
+  int kpa = 1;  // k-blocks per A box (one-block units on the TMA A path)
 };
 
 // Tiled map over a tensor of `rank` dimensions (dims[0] innermost, in elements; strides of dims
@@ -183,8 +184,21 @@ struct StageMaps {
   int b1_row_offset = 0;  // Stage1 split: row offset of the up rows inside map b1
 };
 
-// A operand: one box per block group (gmax x 128 rows) and one per block.
-int make_a_maps(StageMaps* m, const void* base, int elt, int64_t rows, int64_t K, int gmax, const char* what) {
+// A operand: one box per block group (gmax x 128 rows) and one per block; with kpa > 1 (one-block
+// units) one 3-D box holds kpa consecutive 128-byte k-blocks of a block's rows (a k-block
+// dimension of stride 128 bytes), which lands as kpa consecutive 128B-swizzled k-block tiles.
+int make_a_maps(StageMaps* m, const void* base, int elt, int64_t rows, int64_t K, int gmax, const char* what,
+                int kpa = 1) {
+  if (kpa > 1) {
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kKBytes / elt), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(K * elt / kKBytes)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(K * elt), static_cast<cuuint64_t>(kKBytes)};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(kKBytes / elt), static_cast<cuuint32_t>(kBM),
+                               static_cast<cuuint32_t>(kpa)};
+    MOE_TRY(encode_map(&m->a, base, elt, 3, dims, strides, box, what));
+    m->a1 = m->a;
+    return MOE_OK;
+  }
   const int box = (gmax > 1 && rows >= gmax * kBM) ? gmax * kBM : kBM;  // fewer rows: no multi-block group
   MOE_TRY(make_tmap(&m->a, base, elt, rows, K, box, what));
   if (box != kBM) {
@@ -277,6 +291,15 @@ enum TileCfg {
   kT256x2A3B4E8,
   kTTN,
   kT128x2A4B6E8,
+  kT256A3B4E8KA2,
+  kT256A2B3E8KA4,
+  kT256A3B2E8K2KA2,
+  kT256A2B6E8,
+  kT256A3B5E8,
+  kT256X2A2B5E8,
+  kT256A5B4E8,
+  kT256A6B4E8,
+  kT256X2A4B3E8,
   kNumTileCfg
 };
 constexpr TileInfo kTiles[kNumTileCfg] = {
@@ -289,6 +312,11 @@ constexpr TileInfo kTiles[kNumTileCfg] = {
     {"p256a4b10", 256, 2, 4, 10, 1, 1, 1, 4},  {"256a4b5e8", 256, 1, 4, 5, 1, 1, 0, 8},
     {"256x2a3b4e8", 256, 2, 3, 4, 1, 1, 0, 8}, {"tn", 256, 1, 6, 4, 1, 1, 0, 4, 1},
     {"128x2a4b6e8", 128, 2, 4, 6, 1, 1, 0, 8},
+    {"256a3b4e8ka2", 256, 1, 3, 4, 1, 1, 0, 8, 0, 2}, {"256a2b3e8ka4", 256, 1, 2, 3, 1, 1, 0, 8, 0, 4},
+    {"256a3b2e8k2ka2", 256, 1, 3, 2, 1, 2, 0, 8, 0, 2},
+    {"256a2b6e8", 256, 1, 2, 6, 1, 1, 0, 8},   {"256a3b5e8", 256, 1, 3, 5, 1, 1, 0, 8},
+    {"256x2a2b5e8", 256, 2, 2, 5, 1, 1, 0, 8}, {"256a5b4e8", 256, 1, 5, 4, 1, 1, 0, 8},
+    {"256a6b4e8", 256, 1, 6, 4, 1, 1, 0, 8},   {"256x2a4b3e8", 256, 2, 4, 3, 1, 1, 0, 8},
 };
 
 // Defaults, measured on B200. Stage1: 256a4b5e8 (single CTA, 8 epilogue warps: the SiLU*up
@@ -374,8 +402,9 @@ TileCfg usable_cfg(int stage, int64_t K, int elt, bool lsu, double blocks_per_ex
   }
   const TileInfo& t = kTiles[c];
   if (t.kpb > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpb != 0)) return safe;
+  if (t.kpa > 1 && ((K * elt) % kKBytes != 0 || ((K * elt) / kKBytes) % t.kpa != 0)) return safe;
   if (t.bn == 128 && stage != 1 && c != kT128x2A4B6E8) return safe;  // 128-wide Stage2: this tile only
-  if (lsu && (t.kpb > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
+  if (lsu && (t.kpb > 1 || t.kpa > 1 || t.bn == 128 || t.pair || t.epi != 4)) return safe;
   if (t.tn && (lsu || (K * elt) % kKBytes != 0)) return safe;
   return c;
 }
@@ -416,7 +445,7 @@ int unit_order() {
 constexpr int kSmemKinds = 3 * 2 * 3;  // stage mode x 16-bit element type x operand kind
 constexpr int kSmemBitsGemm = kSmemKinds * kNumTileCfg * 4;
 constexpr int kSmemBitsOther = kSmemKinds * kNumTileCfg * 2;
-static_assert(kSmemBitsGemm + kSmemBitsOther <= 64 * 32, "attr_done holds 32 words of bits");
+static_assert(kSmemBitsGemm + kSmemBitsOther <= 64 * 48, "attr_done holds 48 words of bits");
 constexpr int smem_bit_gemm(int mode, bool bf16, int q8, int tcfg, int amode) {
   return (((mode * 2 + (bf16 ? 1 : 0)) * 3 + q8) * kNumTileCfg + tcfg) * 4 + amode;
 }
@@ -540,9 +569,9 @@ int launch_single_rt(int dtype, int dev, const StageMaps& m1, const GemmArgs& a1
 }
 
 template <int MODE, typename OutT, int I8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
-          int EPI = 4>
+          int EPI = 4, int KPA = 1>
 int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
-  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>;
+  auto kern = moe_gemm_kernel<MODE, OutT, I8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI, KPA>;
   GemmArgs args_l = args;
   args_l.b_evict_first = weights_evict_first(MODE);
   args_l.out_evict_last = out_evict_last();
@@ -553,7 +582,7 @@ int launch_gemm(int dev, int tcfg, const StageMaps& m, const GemmArgs& args, int
   args_l.gu_swap = m.gu_swap;
   if (m.b_split) args_l.b1_row_offset = m.b1_row_offset;
   const int bit = smem_bit_gemm(MODE, Elt<OutT>::kBF16, I8, tcfg, AMODE);
-  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>::kSmemBytes;
+  constexpr int smem = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB, KPA>::kSmemBytes;
   MOE_TRY(raise_smem(dev, bit, kern, smem));
   int sms = 0;
   MOE_TRY(device_sms(dev, &sms));
@@ -727,6 +756,33 @@ int launch_stage(TileCfg c, int dev, const StageMaps& m, const GemmArgs& args, i
         break;
       case kT128x2A4B6E8:  // two-block groups, 128 columns per block: two units' accumulators in TMEM
         if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 128, 2, 4, 6, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A2B6E8:  // deeper weight rings, shallower token-row rings
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 2, 6, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A3B5E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 3, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256X2A2B5E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 2, 5, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A5B4E8:  // deeper token-row rings
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 5, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A6B4E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 6, 4, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256X2A4B3E8:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 2, 4, 3, AMODE, 1, 1, 8>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A3B4E8KA2:  // A boxes of 2 k-blocks: fewer, larger TMA loads per unit
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 3, 4, AMODE, 1, 1, 8, 2>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A2B3E8KA4:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 2, 3, AMODE, 1, 1, 8, 4>(dev, c, m, args, max_tiles, stream);
+        break;
+      case kT256A3B2E8K2KA2:
+        if constexpr (kTma) return launch_gemm<MODE, OutT, I8, 256, 1, 3, 2, AMODE, 1, 2, 8, 2>(dev, c, m, args, max_tiles, stream);
         break;
 
       default:
@@ -1087,10 +1143,10 @@ int moe_run_kernel(const void* x, const void* gate_w, const void* up_w, const vo
     MOE_TRY(make_tmap(&m1.b1, up_w, 2, E * I, H, kBM, "up_w"));
     m1.b1_row_offset = 0;
   } else {
-    MOE_TRY(make_a_maps(&m1, x, 2, P, H, gmax1, "stacked_expert_tokens"));
+    MOE_TRY(make_a_maps(&m1, x, 2, P, H, gmax1, "stacked_expert_tokens", t1.kpa));
     MOE_TRY(make_stage1_weights(&m1, gate_w, up_w, 2, E * I, H, t1, gate_w, up_w, E * I, 0, "gate_w/up_w"));
   }
-  MOE_TRY(make_a_maps(&m2, U, 2, P, I, t2.pair ? 1 : gmax2, "workspace"));
+  MOE_TRY(make_a_maps(&m2, U, 2, P, I, t2.pair ? 1 : gmax2, "workspace", t2.kpa));
   MOE_TRY(make_w_map(&m2.b0, down_w, 2, E * H, I, t2.pair ? kBM : (bn2 < kMmaN ? bn2 : kMmaN), t2.kpb, "down_w"));
   m2.b1 = m2.b0;
 
@@ -1480,14 +1536,14 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
   if (lsu) {  // the LSU path does not use the A tensor maps
     m1.a = m1.a1 = m1.b0;
     m2.a = m2.a1 = m2.b0;
-    if (ordered) MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
+    if (ordered) MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate", t2.kpa));
   } else if (gather) {  // Stage1: the token rows themselves, boxes one row high (tile::gather4)
     MOE_TRY(make_tmap(&m1.a, a1_src, elt, T, H, 1, "hidden_states (gather4)"));
     m1.a1 = m1.a;
-    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
+    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate", t2.kpa));
   } else {
-    MOE_TRY(make_a_maps(&m1, xs, elt, L.P_max, H, t1.pair ? 1 : gmax1, "gathered hidden_states"));
-    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate"));
+    MOE_TRY(make_a_maps(&m1, xs, elt, L.P_max, H, t1.pair ? 1 : gmax1, "gathered hidden_states", t1.kpa));
+    MOE_TRY(make_a_maps(&m2, a2_src, elt, L.P_max, I, t2.pair ? 1 : gmax2, "intermediate", t2.kpa));
   }
 
   GemmArgs a1{};

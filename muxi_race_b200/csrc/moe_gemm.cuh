@@ -64,16 +64,21 @@ constexpr int kRingMax = 224 * 1024;
 
 // Shared-memory rings: A (token rows, mostly L2 hits) and B (expert weights, streamed from HBM)
 // have separate depths, so the weight stream can run further ahead than the A stream. An A stage
-// holds one k-block of every block of a group; a B stage holds KPB k-blocks of the weight tile,
-// laid out [k-block][BN rows] (Stage1 rows: [gate BN/2 | up BN/2]).
-template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false, int KPB = 1> struct Ring {
+// holds one k-block of every block of a group (or, with KPA > 1, KPA k-blocks of one block,
+// [k-block][128 rows]); a B stage holds KPB k-blocks of the weight tile, laid out
+// [k-block][BN rows] (Stage1 rows: [gate BN/2 | up BN/2]).
+template <int BN, int GMAX, int AST, int BST, int CPS = 1, bool ROWTAB = false, int KPB = 1, int KPA = 1>
+struct Ring {
   static_assert(BN == 128 || BN == 256 || BN == 512, "accumulator width");
   static_assert(CPS == 1 || CPS == 2, "CTAs per SM");
   static_assert(KPB == 1 || (KPB >= 1 && KPB <= 4 && BN <= kMmaN), "k-blocks per weight box");
+  // k-blocks per A box (one 3-D box of KPA consecutive k-blocks of one block's rows): one-block
+  // units on the TMA A path only
+  static_assert(KPA == 1 || (KPA >= 1 && KPA <= 4 && GMAX == 1 && !ROWTAB), "k-blocks per A box");
   static constexpr int kMN = BN < kMmaN ? BN : kMmaN;  // N of one MMA
   static constexpr int kTmemColsCta = kTmemCols / CPS;  // TMEM columns this CTA allocates
   static_assert(GMAX >= 1 && GMAX * BN <= kTmemColsCta, "a block group must fit in TMEM");
-  static constexpr int kAStageBytes = GMAX * kABytes;
+  static constexpr int kAStageBytes = KPA * GMAX * kABytes;
   static constexpr int kBKBytes = BN * kKBytes;  // one k-block of the weight tile
   static constexpr int kBBytes = KPB * kBKBytes;
   static constexpr int kAStages = AST;
@@ -473,12 +478,14 @@ __host__ __device__ constexpr int pipeline_bars(int ast, int bst, int slots) { r
 // address is at *tmem_slot once the CTA has synchronised) and whose abort flag is cleared: the
 // phase initialises its mbarriers at `bars`, runs the producers, the MMA issuer and the
 // epilogue, and returns once every role has drained (its loads landed, its MMAs retired).
-template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB, int EPI>
+template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB, int EPI,
+          int KPA = 1>
 __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUtensorMap* tmA1_p,
                                            const CUtensorMap* tmB0_p, const CUtensorMap* tmB1_p,
                                            const GemmArgs& args, uint8_t* smem, uint64_t* bars,
                                            const uint32_t* tmem_slot, volatile int* abort_flag, long long* row_tab) {
-  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>;
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB, KPA>;
+  static_assert(KPA == 1 || AMODE == kATma, "multi-k-block A boxes are TMA boxes");
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kBKBytes = RingT::kBKBytes;
@@ -686,7 +693,7 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
             }
           __syncwarp();
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < num_kb; kb += KPA) {
           const int kx = kb * kKElems;
           bool got = mbar_wait(&emptyA[st], ph ^ 1u, abort_flag, args.status);
           if (AMODE != kATma) got = __all_sync(0xffffffffu, got);  // the warp stays converged
@@ -694,7 +701,10 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
             ok = false;
             break;
           }
-          if (AMODE == kATma) {
+          if (AMODE == kATma && KPA > 1) {  // KPA k-blocks of the block's rows in one 3-D box
+            mbar_arrive_expect_tx(&fullA[st], static_cast<uint32_t>(KPA * kABytes));
+            tma_load_3d(stage_a(st, 0), &tmA, &fullA[st], 0, fb * kBM, kb, pol);
+          } else if (AMODE == kATma) {
             mbar_arrive_expect_tx(&fullA[st], static_cast<uint32_t>(nb * kABytes));
             if (GMAX > 1 && nb == GMAX)
               tma_load_2d(stage_a(st, 0), &tmA, &fullA[st], kx, fb * kBM, pol);
@@ -767,11 +777,12 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
           const int kk = kb % KPB;  // k-block inside the current B stage
+          const int ka = kb % KPA;  // k-block inside the current A stage
           if (kk == 0 && !mbar_wait(&fullB[sb], pb, abort_flag, args.status)) {
             ok = false;
             break;
           }
-          if (!mbar_wait(&fullA[sa], pa, abort_flag, args.status)) {
+          if (ka == 0 && !mbar_wait(&fullA[sa], pa, abort_flag, args.status)) {
             ok = false;
             break;
           }
@@ -781,7 +792,7 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
 #pragma unroll
           for (int j = 0; j < GMAX; ++j) {
             if (j >= nb) break;
-            const uint32_t a_addr = smem_u32(stage_a(sa, j));
+            const uint32_t a_addr = smem_u32(stage_a(sa, j)) + static_cast<uint32_t>(ka * kABytes);
 #pragma unroll
             for (int k = 0; k < kKBytes / 32; ++k) {
               const uint64_t ad = smem_desc_sw128(a_addr + k * 32);
@@ -798,10 +809,12 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
               }
             }
           }
-          tc_commit(&emptyA[sa]);  // frees the A slot once the MMAs have read it
-          if (++sa == AST) {
-            sa = 0;
-            pa ^= 1u;
+          if (ka == KPA - 1 || kb == num_kb - 1) {  // last k-block of the A stage
+            tc_commit(&emptyA[sa]);  // frees the A slot once the MMAs have read it
+            if (++sa == AST) {
+              sa = 0;
+              pa ^= 1u;
+            }
           }
           if (kk == KPB - 1 || kb == num_kb - 1) {  // last k-block of the B stage
             tc_commit(&emptyB[sb]);
@@ -892,12 +905,12 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
 
 // One grouped GEMM (one stage) per launch.
 template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
-          int EPI = 4>
+          int EPI = 4, int KPA = 1>
 __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
                     const GemmArgs args) {
-  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB>;
+  using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB, KPA>;
   static_assert(8 + 8 * pipeline_bars(AST, BST, RingT::kSlots) <= kCtlBytes, "control block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -912,8 +925,8 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     tmem_alloc(tmem_slot, RingT::kTmemColsCta);
     tmem_relinquish();
   }
-  gemm_phase<MODE, OutT, Q8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI>(&tmA, &tmA1, &tmB0, &tmB1, args, smem, bars,
-                                                                        tmem_slot, abort_flag, row_tab);
+  gemm_phase<MODE, OutT, Q8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI, KPA>(&tmA, &tmA1, &tmB0, &tmB1, args, smem,
+                                                                             bars, tmem_slot, abort_flag, row_tab);
   // push combine: this thread's reductions into peer memory are performed system-wide before
   // the kernel ends (the flag barrier that follows publishes them to the home ranks)
   if (MODE == kStage2Comb && args.out_regions != nullptr) __threadfence_system();

@@ -1,8 +1,8 @@
 """GPU: every grouped-GEMM tile configuration, forced with ``set_tile``, against the oracle.
 
 The per-call choice picks a configuration from the expected blocks per expert; this file runs
-each configuration (single-CTA, two-block groups, k-block-spanning weight boxes, BN = 128 (in
-Stage2 too: 128x2a4b6e8), CTA pairs) on shapes that exercise empty experts, one-, two- and three-block experts, partial column
+each configuration (single-CTA, two-block groups, k-block-spanning weight boxes and token-row
+boxes (``ka``), BN = 128 (in Stage2 too: 128x2a4b6e8), CTA pairs) on shapes that exercise empty experts, one-, two- and three-block experts, partial column
 tiles and both element types, for the fused, int8 and reference drop-in paths.
 Tolerance: |out - ref_fp32| <= 1e-2 + 1e-2 * |ref| (int8: relative L2 <= 5e-2 vs the fp reference).
 """
@@ -17,7 +17,9 @@ from oracle.moe_ref import fused_moe_ref, run_kernel_ref_f32
 pytestmark = pytest.mark.gpu
 
 TILES = ["256a4b5", "256x2a3b4", "256a4b5e8", "256x2a3b4e8", "512a2b3", "256a2b2c2", "256a6b4", "256a6b2k2",
-         "128x2a3b4k2", "128x2a3b8", "256x2a3b2k2", "p256a6b8", "p256a7b7", "p256a4b10", "128x2a4b6e8"]
+         "128x2a3b4k2", "128x2a3b8", "256x2a3b2k2", "p256a6b8", "p256a7b7", "p256a4b10", "128x2a4b6e8",
+         "256a3b4e8ka2", "256a2b3e8ka4", "256a3b2e8k2ka2", "256a2b6e8", "256a3b5e8", "256x2a2b5e8",
+         "256a5b4e8", "256a6b4e8", "256x2a4b3e8"]
 
 
 @pytest.fixture
