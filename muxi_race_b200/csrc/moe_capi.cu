@@ -413,15 +413,18 @@ bool gather_cfg(TileCfg c) { return c == kT256A4B5 || c == kT256A4B5E8 || c == k
 // Peer-memory EP gather: MOE_B200_EP_GATHER = dedup (default) selects
 // gather_rows_peer_dedup_kernel (each token row read over NVLink once per rank, stored into all
 // its local slots), route the per-route 16-byte load loop (one read per local route), bulk
-// gather_rows_peer_bulk_kernel (bulk copies through shared memory). Measured at 4096 tokens per
-// rank: gather 0.17 vs 0.41 ms on 2 GPUs; on 8 GPUs the step 4.13 ms with dedup.
+// gather_rows_peer_bulk_kernel (bulk copies through shared memory), fused Stage1's gather warps
+// (launch_stage1_gather_warps: no gather launch, the copies overlap the weight stream). Measured
+// at 4096 tokens per rank: gather 0.17 vs 0.41 ms on 2 GPUs; on 8 GPUs the step 4.13 ms with
+// dedup; fused on 2 GPUs: Stage1 grows by more than the gather it absorbs.
 constexpr size_t kEpBulkMaxSmem = 220 * 1024;
-enum EpGather : int { kEpGatherRoute = 0, kEpGatherBulk = 1, kEpGatherDedup = 2 };
+enum EpGather : int { kEpGatherRoute = 0, kEpGatherBulk = 1, kEpGatherDedup = 2, kEpGatherFused = 3 };
 static int ep_gather_mode() {
   static const int v = [] {
     const char* e = getenv("MOE_B200_EP_GATHER");
     if (e && strcmp(e, "bulk") == 0) return (int)kEpGatherBulk;
     if (e && strcmp(e, "route") == 0) return (int)kEpGatherRoute;
+    if (e && strcmp(e, "fused") == 0) return (int)kEpGatherFused;
     return (int)kEpGatherDedup;
   }();
   return v;
@@ -521,8 +524,45 @@ bool single_kernel(double blocks_per_expert) {
   return mode == 1 || (mode == 2 && blocks_per_expert < kPairBlocksPerExpert);
 }
 // The single kernel's shared-memory attribute bit: the operand-swapped kernel's range at a
-// configuration that kernel never runs with.
+// configuration that kernel never runs with (Stage2 modes); the Stage1 kernel with gather warps
+// takes the Stage1 mode's bit there.
 constexpr int smem_bit_single(int mode2, bool bf16) { return smem_bit_other(mode2, bf16, kQ16, kT256A4B5E8, 1); }
+constexpr int smem_bit_gather_warps(bool bf16) { return smem_bit_other(kStage1, bf16, kQ16, kT256A4B5E8, 1); }
+
+// Stage1 (tile 256a4b5e8) with 4 gather warps that copy the routed token rows from the peers'
+// regions while the weights stream (expert parallelism over peer memory, MOE_B200_EP_GATHER =
+// fused). Cooperative: every CTA's gather warps run, so every block the A producers wait for fills.
+constexpr int kGatherWarps = 4;
+template <typename OutT>
+int launch_stage1_gather_warps(int dev, const StageMaps& m, const GemmArgs& args, int max_tiles, cudaStream_t stream) {
+  auto kern = moe_gemm_kernel<kStage1, OutT, kQ16, 256, 1, 4, 5, kATma, 1, 1, 8, 1, kGatherWarps>;
+  GemmArgs a = args;
+  a.b_evict_first = weights_evict_first(kStage1);
+  a.late_release = epilogue_late_release();
+  a.m64_tail = m64_tail();
+  a.unit_order = a.group_padded_offsets ? unit_order() : 0;
+  a.b_split = m.b_split;
+  a.gu_swap = m.gu_swap;
+  if (m.b_split) a.b1_row_offset = m.b1_row_offset;
+  constexpr int smem = Ring<256, 1, 4, 5>::kSmemBytes;
+  MOE_TRY(raise_smem(dev, smem_bit_gather_warps(Elt<OutT>::kBF16), kern, smem));
+  int sms = 0;
+  MOE_TRY(device_sms(dev, &sms));
+  const int grid = max_tiles < sms ? max_tiles : sms;
+  if (grid <= 0) return MOE_OK;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(96 + 32 * 8 + 32 * kGatherWarps, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MOE_CUDA(cudaLaunchKernelEx(&cfg, kern, m.a, m.a1, m.b0, m.b1, a));
+  return MOE_OK;
+}
 
 template <typename OutT, int MODE2>
 int launch_single(int dev, const StageMaps& m1, const GemmArgs& a1, const StageMaps& m2, const GemmArgs& a2,
@@ -895,7 +935,8 @@ FusedLayout fused_layout(int64_t T, int64_t topk, int64_t E, int64_t H, int64_t 
   L.meta = take(sizeof(int) * 4);
   L.gidx = take(sizeof(int) * (size_t)L.nblk_max);
   L.groups = take(sizeof(int) * (size_t)(L.nblk_max + 1));  // block groups + their count
-  L.done = take(sizeof(uint32_t) * (size_t)L.nblk_max);      // single kernel: Stage1 counts per block
+  // single kernel: Stage1 counts per block; fused peer gather: rows per block, then token claims
+  L.done = take(sizeof(uint32_t) * (size_t)(L.nblk_max + T));
   L.tn = take(sizeof(int) * (size_t)(2 * L.nblk_max + 1));   // operand-swapped kernel: entries + count
   L.sorted = take(sizeof(int) * (size_t)L.P_max);
   L.slot = take(sizeof(int) * (size_t)R);
@@ -1397,6 +1438,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
     tc1 = kDefaultTile1;
     tc2 = kDefaultTile2;
   }
+  // peer memory with the fused token gather: Stage1's gather warps copy the routed rows from the
+  // peers' regions while its weights stream (Stage1 on its default tile)
+  const bool fused_gather = peer && ep_gather_mode() == kEpGatherFused && !int8 && tc1 == kDefaultTile1;
   const TileInfo &t1 = kTiles[tc1], &t2 = kTiles[tc2];
   if (peer && peer->push && t2.tn) return fail(MOE_ERR_UNSUPPORTED, "the operand-swapped Stage2 has no push combine");
   const int bn1 = t1.bn, gmax1 = t1.gmax, bn2 = t2.bn, gmax2 = t2.gmax;
@@ -1408,9 +1452,9 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
                           static_cast<int32_t*>(const_cast<void*>(ids)), static_cast<float*>(const_cast<void*>(tw)),
                           counts, s));
   MOE_TRY(launch_align(ids, ids_dtype, R, E, kBM, gs, go, gpo, gidx, sorted, slot, meta, counts, s, router != nullptr));
-  if (gmax1 > 1 || gmax2 > 1) {
+  if (gmax1 > 1 || gmax2 > 1 || single || fused_gather) {  // also clears the per-block counts
     build_groups_kernel<<<1, 1024, 0, s>>>(gpo, (int)E, 2, (int)L.nblk_max, groups, ngroups, done,
-                                           single ? (int)L.nblk_max : 0);
+                                           fused_gather ? (int)(L.nblk_max + T) : single ? (int)L.nblk_max : 0);
     MOE_CUDA(cudaGetLastError());
   }
   int32_t* tn_entries = reinterpret_cast<int32_t*>(ws + L.tn);
@@ -1445,6 +1489,8 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_CUDA(cudaGetLastError());
       MOE_CUDA(cudaMemsetAsync(amax, 0, sizeof(float) * (size_t)L.P_max, s));
     }
+  } else if (fused_gather) {
+    // the token rows are copied by Stage1's gather warps, which also zero the served partial rows
   } else if (peer && ep_gather_mode() == kEpGatherDedup && topk <= 32) {
     // one warp per virtual token: its row crosses NVLink once, then lands in all its local slots
     const int zero_served = peer->push ? 0 : 1;
@@ -1635,6 +1681,20 @@ static int fused_common(bool int8, const void* x, const void* w13, const float* 
       MOE_TRY(launch_tn_rt<kStage1>(dtype, dev, tc1, tm, t, (int)L.nblk_max * t.n_tiles, s));
     } else if (gather) {
       MOE_TRY(launch_stage1_gather_rt<kQ16>(dtype, tc1, dev, m1, a1, max_tiles1, s));
+    } else if (fused_gather) {
+      a1.g_regions = peer->regions;
+      a1.g_x_off = peer->L.x;
+      a1.g_T_max = peer->T_max;
+      a1.g_rows = xs;
+      a1.a_done = done;
+      a1.g_zero_y = peer->push ? nullptr : out;
+      a1.g_route_slot = slot;
+      a1.g_tokens = (int)T;
+      a1.g_claim = done + L.nblk_max;
+      if (dtype == MOE_F16)
+        MOE_TRY(launch_stage1_gather_warps<__half>(dev, m1, a1, max_tiles1, s));
+      else
+        MOE_TRY(launch_stage1_gather_warps<__nv_bfloat16>(dev, m1, a1, max_tiles1, s));
     } else if (single) {  // Stage1 and Stage2 in one launch: the Stage1 event marks the end of both
       a1.block_done = a2.block_done = done;
       a1.block_done_target = a2.block_done_target = static_cast<uint32_t>(a1.n_tiles * 8);  // x 8 epilogue warps

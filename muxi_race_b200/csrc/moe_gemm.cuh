@@ -162,6 +162,25 @@ struct GemmArgs {
   uint32_t* block_done;
   uint32_t block_done_target;
 
+  // Stage1 with gather warps (expert parallelism over peer memory, the fused token gather): the
+  // kernel's GW extra warps copy the token row of every routed padded row p, in row order, into
+  // row p of g_rows (the A rows): virtual route sorted_route_ids[p] = (s * g_T_max + t) * topk + j
+  // names row t of rank s's hidden states, at g_regions[s] + g_x_off. After each row (padding rows
+  // too) a warp adds one to a_done[p / 128]; the A producer loads a block once its count reaches
+  // 128. A token's row is read once per rank: the warp that claims the token (g_claim[tok], zero
+  // at the start of a call) stores it into all its local rows (g_route_slot[tok * topk + j]). With
+  // g_zero_y they then zero row tok of g_zero_y (the pull combine's partial rows) for every token
+  // tok < g_tokens with a local route.
+  const uint64_t* g_regions;
+  long long g_x_off;
+  int g_T_max;
+  void* g_rows;
+  uint32_t* a_done;
+  void* g_zero_y;
+  const int32_t* g_route_slot;
+  int g_tokens;
+  uint32_t* g_claim;
+
   uint32_t* status;           // device status word (OR of kStatus* bits)
 };
 
@@ -479,13 +498,14 @@ __host__ __device__ constexpr int pipeline_bars(int ast, int bst, int slots) { r
 // phase initialises its mbarriers at `bars`, runs the producers, the MMA issuer and the
 // epilogue, and returns once every role has drained (its loads landed, its MMAs retired).
 template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB, int EPI,
-          int KPA = 1>
+          int KPA = 1, int GW = 0>
 __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUtensorMap* tmA1_p,
                                            const CUtensorMap* tmB0_p, const CUtensorMap* tmB1_p,
                                            const GemmArgs& args, uint8_t* smem, uint64_t* bars,
                                            const uint32_t* tmem_slot, volatile int* abort_flag, long long* row_tab) {
   using RingT = Ring<BN, GMAX, AST, BST, CPS, a_mode_lsu(AMODE), KPB, KPA>;
   static_assert(KPA == 1 || AMODE == kATma, "multi-k-block A boxes are TMA boxes");
+  static_assert(GW == 0 || (MODE == kStage1 && AMODE == kATma && GMAX == 1), "gather warps feed one-block Stage1 units");
   constexpr int kAStageBytes = RingT::kAStageBytes;
   constexpr int kBBytes = RingT::kBBytes;
   constexpr int kBKBytes = RingT::kBKBytes;
@@ -670,6 +690,18 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int fb, nb, nt, e;
         if (!tile_unit<GMAX>(args, tile, fb, nb, nt, e)) continue;
+        if (GW > 0 && args.a_done != nullptr) {
+          // the gather warps of all CTAs have copied every row of this block (generic-proxy stores
+          // read here by TMA: acquire, then the proxy fence)
+          bool dep = true;
+          for (int j = 0; j < nb && dep; ++j)
+            dep = counter_wait(args.a_done + fb + j, static_cast<uint32_t>(kBM), abort_flag, args.status);
+          if (!dep) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         if (MODE != kStage1 && AMODE == kATma && args.block_done != nullptr) {
           // single-kernel MoE: the group's U rows are complete once every Stage1 column tile of
           // each of its blocks has published its stores (other CTAs' generic-proxy stores, read
@@ -833,6 +865,63 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
       tc_commit(drain_bar);
       mbar_wait_drain(drain_bar, 0);
     }
+  } else if (GW > 0 && warp >= 3 + EPI) {
+    // ---------------------------------------------------------------- gather warps
+    // Rows in order, so the blocks the first units need are complete first. Eight 16-byte peer
+    // loads in flight per lane (NVLink reads have microseconds of latency). Every row, padding
+    // included, adds exactly one to its block's count.
+    const int gw = static_cast<int>(blockIdx.x) * GW + (warp - 3 - EPI);
+    const int n_gw = static_cast<int>(gridDim.x) * GW;
+    const int rows = ngroups * kBM;
+    const int vecs = static_cast<int>(args.a_row_bytes / 16);
+    char* a_rows = static_cast<char*>(args.g_rows);
+    for (int p = gw; p < rows; p += n_gw) {
+      const int route = args.sorted_route_ids[p];
+      if (route < 0 || route >= args.R) {  // padding row: nothing to copy
+        if (lane == 0) atomicAdd(args.a_done + (p >> 7), 1u);
+        continue;
+      }
+      // The first warp to reach one of a token's rows claims the token, reads its row over NVLink
+      // once and stores it into all the token's local rows (a token's lowest row comes first in
+      // row order, so every row of a block is claimed by the time the block's rows are passed).
+      const long long tok = route / args.topk;
+      int claimed = 0;
+      if (lane == 0) claimed = atomicCAS(reinterpret_cast<int*>(args.g_claim) + tok, 0, 1) == 0;
+      if (!__shfl_sync(0xffffffffu, claimed, 0)) continue;
+      const int my_slot = lane < args.topk ? args.g_route_slot[tok * args.topk + lane] : -1;
+      const unsigned local = __ballot_sync(0xffffffffu, my_slot >= 0);
+      const int s = static_cast<int>(tok / args.g_T_max);
+      const long long t = tok - static_cast<long long>(s) * args.g_T_max;
+      const uint4* src =
+          reinterpret_cast<const uint4*>(args.g_regions[s] + static_cast<uint64_t>(args.g_x_off)) + t * vecs;
+      constexpr int U = 8;
+      for (int v0 = lane; v0 < vecs; v0 += 32 * U) {
+        uint4 tmp[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + u * 32 < vecs) tmp[u] = __ldcg(src + v0 + u * 32);
+        for (unsigned m = local; m != 0u; m &= m - 1u) {
+          const int q = __shfl_sync(0xffffffffu, my_slot, __ffs(static_cast<int>(m)) - 1);
+          uint4* dst = reinterpret_cast<uint4*>(a_rows + static_cast<size_t>(q) * args.a_row_bytes);
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+            if (v0 + u * 32 < vecs) dst[v0 + u * 32] = tmp[u];
+        }
+      }
+      fence_proxy_async_global();
+      __threadfence();
+      __syncwarp();
+      if (my_slot >= 0) atomicAdd(args.a_done + (my_slot >> 7), 1u);  // one per row stored
+    }
+    if (args.g_zero_y != nullptr) {
+      uint4* y = static_cast<uint4*>(args.g_zero_y);
+      for (int tok = gw; tok < args.g_tokens; tok += n_gw) {
+        const int slot = lane < args.topk ? args.g_route_slot[static_cast<long long>(tok) * args.topk + lane] : -1;
+        if (__ballot_sync(0xffffffffu, slot >= 0) == 0u) continue;
+        uint4* dst = y + static_cast<long long>(tok) * vecs;
+        for (int v = lane; v < vecs; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
+      }
+    }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5, 7..10)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
@@ -905,8 +994,8 @@ __device__ __forceinline__ void gemm_phase(const CUtensorMap* tmA_p, const CUten
 
 // One grouped GEMM (one stage) per launch.
 template <int MODE, typename OutT, int Q8, int BN, int GMAX, int AST, int BST, int AMODE, int CPS, int KPB,
-          int EPI = 4, int KPA = 1>
-__global__ void __launch_bounds__(96 + EPI * 32, CPS)
+          int EPI = 4, int KPA = 1, int GW = 0>
+__global__ void __launch_bounds__(96 + EPI * 32 + GW * 32, CPS)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA1,
                     const __grid_constant__ CUtensorMap tmB0, const __grid_constant__ CUtensorMap tmB1,
                     const GemmArgs args) {
@@ -925,8 +1014,9 @@ __global__ void __launch_bounds__(96 + EPI * 32, CPS)
     tmem_alloc(tmem_slot, RingT::kTmemColsCta);
     tmem_relinquish();
   }
-  gemm_phase<MODE, OutT, Q8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI, KPA>(&tmA, &tmA1, &tmB0, &tmB1, args, smem,
-                                                                             bars, tmem_slot, abort_flag, row_tab);
+  gemm_phase<MODE, OutT, Q8, BN, GMAX, AST, BST, AMODE, CPS, KPB, EPI, KPA, GW>(&tmA, &tmA1, &tmB0, &tmB1, args,
+                                                                                 smem, bars, tmem_slot, abort_flag,
+                                                                                 row_tab);
   // push combine: this thread's reductions into peer memory are performed system-wide before
   // the kernel ends (the flag barrier that follows publishes them to the home ranks)
   if (MODE == kStage2Comb && args.out_regions != nullptr) __threadfence_system();
